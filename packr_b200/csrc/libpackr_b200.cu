@@ -1,0 +1,5 @@
+// Single translation unit of libpackr_b200.so: every kernel and every C-ABI
+// entry point is compiled together so that device globals are shared without
+// relocatable device code.
+#include "common.cu"
+#include "adam8.cu"

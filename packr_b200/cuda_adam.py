@@ -1,0 +1,129 @@
+"""CUDA8BitAdam — 8-bit AdamW with per-block int8 moments on sm_100a.
+
+Drop-in for reference packr/cuda_adam.py:142-194: same constructor, same
+`step(closure=None)`, same lazily created per-parameter state
+  state[p]["m"], ["v"]              int8  [numel]
+  state[p]["m_scale"], ["v_scale"]  f32   [ceil(numel/256)]  (init ones)
+(reference packr/cuda_adam.py:132-139), which VelvetController reads.
+Instead of one kernel launch per parameter, each parameter group is updated
+by one packr_adam8_multi call (libpackr_b200.so), which walks every tensor of
+the group with 128-bit vector accesses.
+
+Additions over the reference: `_step_count` is saved in state_dict() (the
+reference keeps it only as an attribute, so bias correction restarted on
+resume), and step() raises if a parameter is not on a CUDA device.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+BLOCK_SIZE = 256
+
+
+def _init_state(state, p):
+    """Initialise int8 m/v + per-block float32 scales for one param
+    (reference packr/cuda_adam.py:132-139)."""
+    n = p.numel()
+    nb = (n + BLOCK_SIZE - 1) // BLOCK_SIZE
+    state["m"] = torch.zeros(n, dtype=torch.int8, device=p.device)
+    state["v"] = torch.zeros(n, dtype=torch.int8, device=p.device)
+    state["m_scale"] = torch.ones(nb, dtype=torch.float32, device=p.device)
+    state["v_scale"] = torch.ones(nb, dtype=torch.float32, device=p.device)
+
+
+def adam8_launch(entries, lr, b1, b2, eps, bc1, bc2, wd, stream=None) -> None:
+    """Runs packr_adam8_multi over `entries` = [(p, g, m, v, ms, vs), ...] of
+    CUDA tensors on one device.  p/g are bf16 or f32 (same dtype), contiguous."""
+    if not entries:
+        return
+    lib = _lib.load()
+    arr = (_lib.AdamTensor * len(entries))()
+    dev = None
+    for i, (p, g, m, v, ms, vs) in enumerate(entries):
+        if not p.is_cuda:
+            raise RuntimeError("CUDA8BitAdam: parameters must be CUDA tensors (no CPU path)")
+        if dev is None:
+            dev = p.device
+        elif p.device != dev:
+            raise RuntimeError("adam8_launch: all tensors of one launch must be on one device")
+        if g.dtype != p.dtype or p.dtype not in (torch.bfloat16, torch.float32):
+            raise TypeError(f"CUDA8BitAdam: unsupported dtype {p.dtype}/{g.dtype}")
+        for t in (p, g, m, v, ms, vs):
+            if not t.is_contiguous():
+                raise ValueError("adam8_launch: tensors must be contiguous")
+        e = arr[i]
+        e.p, e.g, e.m, e.v = p.data_ptr(), g.data_ptr(), m.data_ptr(), v.data_ptr()
+        e.m_scale, e.v_scale = ms.data_ptr(), vs.data_ptr()
+        e.numel = p.numel()
+        e.dtype = _lib.PACKR_DTYPE_BF16 if p.dtype == torch.bfloat16 else _lib.PACKR_DTYPE_F32
+        e.reserved = 0
+    with torch.cuda.device(dev):
+        s = stream if stream is not None else torch.cuda.current_stream(dev)
+        code = lib.packr_adam8_multi(arr, len(entries), lr, b1, b2, eps, bc1, bc2, wd,
+                                     ctypes.c_void_p(s.cuda_stream))
+    _lib.check("packr_adam8_multi", code)
+
+
+class CUDA8BitAdam(torch.optim.Optimizer):
+    """8-bit AdamW with per-block int8 quantization (block 256).
+
+    Args:
+        params:       iterable of parameters (bf16 or fp32, CUDA)
+        lr:           learning rate
+        betas:        (beta1, beta2)
+        eps:          epsilon
+        weight_decay: AdamW-style weight decay
+    """
+
+    def __init__(self, params, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0):
+        defaults = dict(lr=lr, betas=betas, eps=eps, weight_decay=weight_decay)
+        super().__init__(params, defaults)
+        self._step_count = 0
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        if closure is not None:
+            with torch.enable_grad():
+                closure()
+        self._step_count += 1
+        step = self._step_count
+        for group in self.param_groups:
+            lr = group["lr"]
+            b1, b2 = group["betas"]
+            eps = group["eps"]
+            wd = group["weight_decay"]
+            bc1 = 1.0 - b1 ** step
+            bc2 = 1.0 - b2 ** step
+            by_dev = {}
+            for p in group["params"]:
+                if p.grad is None:
+                    continue
+                if p.grad.is_sparse:
+                    raise RuntimeError("CUDA8BitAdam does not support sparse gradients")
+                state = self.state[p]
+                if "m" not in state:
+                    _init_state(state, p)
+                g = p.grad if p.grad.is_contiguous() else p.grad.contiguous()
+                if g.dtype != p.dtype:
+                    g = g.to(p.dtype)
+                if not p.is_contiguous():
+                    raise ValueError("CUDA8BitAdam: parameters must be contiguous")
+                by_dev.setdefault(p.device, []).append(
+                    (p, g, state["m"], state["v"], state["m_scale"], state["v_scale"]))
+            for entries in by_dev.values():
+                adam8_launch(entries, lr, b1, b2, eps, bc1, bc2, wd)
+        return None
+
+    def state_dict(self):
+        sd = super().state_dict()
+        sd["packr_step_count"] = self._step_count
+        return sd
+
+    def load_state_dict(self, state_dict):
+        state_dict = dict(state_dict)
+        self._step_count = int(state_dict.pop("packr_step_count", self._step_count))
+        super().load_state_dict(state_dict)
