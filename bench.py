@@ -135,11 +135,18 @@ def max_over_ranks(x: float, world: int) -> float:
     return float(t.item())
 
 
-def timed(fn, steps: int, warmup: int, world: int, flush=None) -> tuple[float, list[float]]:
-    """Runs fn() warmup times, then times `steps` calls with CUDA events on the
-    current stream; returns (max-over-ranks total ms, per-step ms)."""
-    for _ in range(warmup):
+def timed(fn, steps: int, warmup: int, world: int, flush=None, warm_seconds: float = 0.0) -> tuple[float, list[float]]:
+    """Runs fn() `warmup` times (and keeps warming until `warm_seconds` have
+    passed, so clock samples cover steady state), then times `steps` calls
+    with CUDA events on the current stream; returns (max-over-ranks total ms,
+    per-step ms)."""
+    t0 = time.perf_counter()
+    done = 0
+    while done < warmup or time.perf_counter() - t0 < warm_seconds:
         fn()
+        done += 1
+        if done % 16 == 0:
+            torch.cuda.synchronize()
     torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
@@ -225,7 +232,7 @@ def bench_adam8(args, world, rank, peaks, peak_kind):
     opt = CUDA8BitAdam([p], lr=2e-5, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01)
     step = opt.step
     with ClockSampler(torch.cuda.current_device()) as clk:
-        total_ms, per = timed(step, args.steps, args.warmup, world)
+        total_ms, per = timed(step, args.steps, args.warmup, world, warm_seconds=1.5)
     ms_step = total_ms / args.steps
     value = world * n / (ms_step * 1e-3) / 1e9
     kernel_ms = statistics.mean(per)

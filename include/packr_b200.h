@@ -76,6 +76,54 @@ int packr_adam8_multi(const packr_adam_tensor* tensors, int n_tensors, float lr,
                       float beta1, float beta2, float eps, float bc1, float bc2,
                       float weight_decay, void* stream);
 
+/* ---- PackRLinear ---------------------------------------------------------
+ * out[M,N] (f32) = x[M,K] @ W + bias,  W = bf16(W_f + bf16(lut[W_p])),
+ * computed on the tensor cores with x and W as bf16 operands and an f32
+ * accumulator; W is decoded in shared memory and never written to HBM.
+ * x is bf16 or f32 (f32 x is rounded to bf16 in the workspace first).
+ * bias: [N] of bias_dtype (bf16 or f32, added in f32 in the epilogue) or
+ * NULL.  M = 0 is a no-op; K, N >= 1.
+ * Replaces packr_matmul(x, W_p, W_f, lut, bias) of reference
+ * packr/kernel.py:98-141 plus the bias add of packr/layer.py:96-97.
+ */
+size_t packr_forward_workspace_bytes(int64_t M, int64_t K, int64_t N, int x_dtype);
+int packr_forward(const void* x, int x_dtype, const uint8_t* W_p, const uint16_t* W_f, const float* lut,
+                  const void* bias, int bias_dtype, float* out, int64_t M, int64_t K, int64_t N, void* workspace,
+                  size_t workspace_bytes, void* stream);
+
+/* Backward of the forward above; replaces PackRMatmulFunction.backward of
+ * reference packr/autograd.py:56-88 and the bias gradient of layer.py:97:
+ *   dX[M,K]   = bf16(bf16(dY) @ W^T)      stored as x's dtype (NULL: skipped)
+ *   dW_f[K,N] = bf16(x^T @ dY)             fp32 accumulate     (NULL: skipped)
+ *   dlut[256] = sum_{W_p==b} (x^T @ dY) / (count[b] + 1e-8)     (NULL: skipped)
+ *   dbias[N]  = bf16(sum_m dY)                                  (NULL: skipped)
+ * dY is the f32 upstream gradient [M,N].  lut_counts = bincount(W_p, 256)
+ * (packr_bincount256; W_p is frozen, so callers cache it) or NULL to count
+ * here.  flags: PACKR_BWD_DW_SPLIT makes the dW product fp32-faithful by
+ * splitting dY (and an f32 x) into bf16 hi + lo parts (x.dY_hi + x.dY_lo
+ * [+ x_lo.dY_hi]); without it dY is rounded to bf16 as the reference does for
+ * dX.  A workspace of packr_backward_workspace_bytes(M, K, N, x_dtype, flags)
+ * bytes (256-byte aligned) holds bf16(dY), its split parts, a bf16 copy of an
+ * f32 x and the partial sums. */
+#define PACKR_BWD_DW_SPLIT 1
+size_t packr_backward_workspace_bytes(int64_t M, int64_t K, int64_t N, int x_dtype, int flags);
+int packr_backward(const float* dY, const void* x, int x_dtype, const uint8_t* W_p, const uint16_t* W_f,
+                   const float* lut, const int32_t* lut_counts, void* dX, uint16_t* dW_f, float* dlut,
+                   uint16_t* dbias, int64_t M, int64_t K, int64_t N, int flags, void* workspace,
+                   size_t workspace_bytes, void* stream);
+
+/* counts[b] = number of bytes equal to b in W_p[0..n) (the
+ * torch.bincount(W_p, minlength=256) of reference packr/autograd.py:80). */
+int packr_bincount256(const uint8_t* W_p, int64_t n, int32_t* counts, void* stream);
+
+/* dlut[b] = dlut_sum[b] / (counts[b] + 1e-8)  (reference autograd.py:83). */
+int packr_lut_finalize(float* dlut, const float* dlut_sum, const int32_t* counts, void* stream);
+
+/* out[K,N] = bf16(W_f + bf16(lut[W_p])) through the GEMM's own decode path
+ * (reference packr/autograd.py:66-67); for bit-exactness checks. */
+int packr_decode_bf16(const uint8_t* W_p, const uint16_t* W_f, const float* lut, uint16_t* out, int64_t K,
+                      int64_t N, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

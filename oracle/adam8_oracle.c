@@ -7,9 +7,11 @@
  * of 256 elements at a time) in plain C with the same operation order:
  *   :21-31  load p, g (bf16 widened by <<16), mf = m*ms, vf = v*vs
  *   :34     if wd > 0: p -= (lr*wd)*p            (one fused multiply-add)
- *   :36-37  m_new = b1*mf + (1-b1)*g,  v_new = b2*vf + (1-b2)*g*g
- *           (first product fused into the add, as nvcc's default -fmad
- *            contracts these source expressions)
+ *   :36-37  m_new = fma(1-b1, g, b1*mf),  v_new = fma((1-b2)*g, g, b2*vf)
+ *           (the second product of each source expression fused into the
+ *            add: the contraction nvcc's default -fmad applies to the
+ *            reference, confirmed bit-for-bit against the reference kernel's
+ *            outputs in tests/golden/adam8_golden.npz)
  *   :39-48  block absmax; ms' = max(amax/127, 1e-14), same for v
  *   :53-54  codes: truncate(clamp(m_new/ms' +- 0.5, -127, 127)),
  *                  truncate(clamp(v_new/vs' + 0.5, 1, 127))
@@ -63,8 +65,8 @@ void oracle_adam8_step(void* p_raw, const void* g_raw, int8_t* m, int8_t* v, flo
       const float mf = (float)m[k] * s_m;
       const float vf = (float)v[k] * s_v;
       if (wd > 0.0f) p = fmaf(-lr_wd, p, p);
-      mn[i] = fmaf(b1, mf, one_m_b1 * g);
-      vn[i] = fmaf(b2, vf, (one_m_b2 * g) * g);
+      mn[i] = fmaf(one_m_b1, g, b1 * mf);
+      vn[i] = fmaf(one_m_b2 * g, g, b2 * vf);
       pv[i] = p;
       amax_m = fmaxf(amax_m, fabsf(mn[i]));
       amax_v = fmaxf(amax_v, fabsf(vn[i]));

@@ -10,6 +10,22 @@ Drop-in for the reference package's public surface on this path
 Every op runs hand-written sm_100a kernels from libpackr_b200.so through its
 C ABI (include/packr_b200.h); there is no CPU fallback.
 """
+from .kernel import packr_matmul
+from .autograd import PackRMatmulFunction, PackRLinearFunction
+from .layer import PackRLinear
+from .layer_patcher import compress_model
+from .config import PackRConfig, SchemeType
+from .optim import FusedQuantizedAdam
 from .cuda_adam import CUDA8BitAdam
 
-__all__ = ["CUDA8BitAdam"]
+# Legacy aliases (reference packr/__init__.py:29-34)
+PHRConfig = PackRConfig
+PHRLinear = PackRLinear
+PHRMatmulFunction = PackRMatmulFunction
+phr_matmul = packr_matmul
+
+__all__ = [
+    "PackRConfig", "PackRLinear", "PackRMatmulFunction", "PackRLinearFunction", "packr_matmul", "compress_model",
+    "SchemeType", "FusedQuantizedAdam", "CUDA8BitAdam",
+    "PHRConfig", "PHRLinear", "PHRMatmulFunction", "phr_matmul",
+]

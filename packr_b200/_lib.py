@@ -45,7 +45,16 @@ SIGNATURES = {
     "packr_abi_version": (_I32, []),
     "packr_device_status": (_I32, [_VP]),
     "packr_adam8_multi": (_I32, [ctypes.POINTER(AdamTensor), _I32, _F32, _F32, _F32, _F32, _F32, _F32, _F32, _VP]),
+    "packr_forward_workspace_bytes": (_SZ, [_I64, _I64, _I64, _I32]),
+    "packr_forward": (_I32, [_VP, _I32, _VP, _VP, _VP, _VP, _I32, _VP, _I64, _I64, _I64, _VP, _SZ, _VP]),
+    "packr_backward_workspace_bytes": (_SZ, [_I64, _I64, _I64, _I32, _I32]),
+    "packr_backward": (_I32, [_VP, _VP, _I32, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _I64, _I64, _I64, _I32, _VP,
+                              _SZ, _VP]),
+    "packr_bincount256": (_I32, [_VP, _I64, _VP, _VP]),
+    "packr_lut_finalize": (_I32, [_VP, _VP, _VP, _VP]),
+    "packr_decode_bf16": (_I32, [_VP, _VP, _VP, _VP, _I64, _I64, _VP]),
 }
+PACKR_BWD_DW_SPLIT = 1
 
 
 def lib_path() -> Path:

@@ -11,15 +11,16 @@
 // Arithmetic is written with explicit round-to-nearest intrinsics so that the
 // compiler cannot re-associate or contract it differently from the oracle:
 //   wd decay  p  = fma(-(lr*wd), p, p)                     (cuda_adam_kernel.cu:34)
-//   m_new     = fma(b1, m*ms, (1-b1)*g)                    (:36)
-//   v_new     = fma(b2, v*vs, ((1-b2)*g)*g)                (:37)
+//   m_new     = fma(1-b1, g, b1*(m*ms))                    (:36)
+//   v_new     = fma((1-b2)*g, g, b2*(v*vs))                (:37)
 //   scales    = max(absmax/127, 1e-14)                     (:48)
 //   m code    = trunc(clamp(m_new/ms' +- 0.5, -127, 127))  (:53)
 //   v code    = trunc(clamp(v_new/vs' + 0.5, 1, 127))      (:54)
 //   p_new     = p - (lr*(m_new/bc1)) / (sqrt(v_new/bc2) + eps)   (:55)
 //   bf16 store: integer round-to-nearest-even              (:62-64)
 // The fused multiply-adds are where nvcc's default -fmad=true contracts the
-// reference's source expressions.
+// reference's source expressions (checked bit for bit against the reference
+// kernel's outputs).
 #include "common.cuh"
 
 namespace packr {
@@ -60,13 +61,43 @@ __device__ __forceinline__ void unpack_bf16x8(const uint4& q, float* f) {
   }
 }
 
+// int8 -> float without the conversion unit: (x ^ 0x80) is x + 128 in
+// [0, 255]; placed in the low byte of 2^23 (0x4B000000) it forms the float
+// 2^23 + 128 + x exactly, and subtracting 2^23 + 128 leaves x exactly.
 __device__ __forceinline__ void unpack_i8x8(const uint2& q, float* f) {
-  const uint32_t w[2] = {q.x, q.y};
+  const uint32_t w[2] = {q.x ^ 0x80808080u, q.y ^ 0x80808080u};
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) f[4 * i + j] = (float)(int8_t)((w[i] >> (8 * j)) & 0xFFu);
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t bits = __byte_perm(w[i], 0x4B000000u, 0x7440u + j);
+      f[4 * i + j] = __fsub_rn(__uint_as_float(bits), 8388736.0f);
+    }
   }
+}
+
+// floor(y) for 0 <= y < 2^22 without the conversion unit: 2^23 + y rounded
+// toward zero is 2^23 + floor(y), whose low mantissa bits hold floor(y).
+__device__ __forceinline__ int floor_small(float y) {
+  return (int)(__float_as_uint(__fadd_rz(y, 8388608.0f)) - 0x4B000000u);
+}
+
+// a / b rounded to nearest, given y = RN(1/b), by Markstein's correction
+// (P. Markstein, "Computation of elementary functions on the IBM RISC
+// System/6000 processor", IBM J. Res. Dev. 34(1), 1990; Muller et al.,
+// Handbook of Floating-Point Arithmetic, ch. 4): q = RN(a*y); r = a - b*q is
+// exact by FMA; RN(q + r*y) equals RN(a/b) when y = RN(1/b) and every
+// intermediate stays in the normal range.  A zero dividend returns q (its
+// sign is right); dividends outside [2^-96, 2^100) take the IEEE division.
+__device__ __forceinline__ float div_recip(float a, float b, float y) {
+  const float q = __fmul_rn(a, y);
+  const float r = __fmaf_rn(-q, b, a);
+  const float q2 = __fmaf_rn(r, y, q);
+  return a == 0.0f ? q : q2;
+}
+__device__ __forceinline__ bool div_recip_ok(float a) {
+  const float m = fabsf(a);
+  return a == 0.0f || (m >= 0x1p-96f && m < 0x1p+100f);
 }
 
 __device__ __forceinline__ uint32_t pack_i8x4(const int* c) {
@@ -74,7 +105,7 @@ __device__ __forceinline__ uint32_t pack_i8x4(const int* c) {
          ((uint32_t)(c[3] & 0xFF) << 24);
 }
 
-__global__ void __launch_bounds__(kThreads) adam8_multi_kernel(const __grid_constant__ AdamLaunch L,
+__global__ void __launch_bounds__(kThreads, 3) adam8_multi_kernel(const __grid_constant__ AdamLaunch L,
                                                                const AdamHyper h) {
   const int lane = threadIdx.x & 31;
   const long long warp0 = ((long long)blockIdx.x * kThreads + threadIdx.x) >> 5;
@@ -84,6 +115,9 @@ __global__ void __launch_bounds__(kThreads) adam8_multi_kernel(const __grid_cons
   const float one_m_b1 = __fsub_rn(1.0f, h.b1);
   const float one_m_b2 = __fsub_rn(1.0f, h.b2);
   const float lr_wd = __fmul_rn(h.lr, h.wd);
+  // bc1, bc2 lie in (0, 1]: their reciprocals are normal numbers.
+  const float y_bc1 = __frcp_rn(h.bc1);
+  const float y_bc2 = __frcp_rn(h.bc2);
 
   for (long long b = warp0; b < total; b += nwarps) {
     // Largest tensor index t with block_begin[t] <= b (warp-uniform).
@@ -141,8 +175,8 @@ __global__ void __launch_bounds__(kThreads) adam8_multi_kernel(const __grid_cons
         const float mf = __fmul_rn(mq[i], ms);
         const float vf = __fmul_rn(vq[i], vs);
         if (h.wd > 0.0f) pv[i] = __fmaf_rn(-lr_wd, pv[i], pv[i]);
-        mn[i] = __fmaf_rn(h.b1, mf, __fmul_rn(one_m_b1, gv[i]));
-        vn[i] = __fmaf_rn(h.b2, vf, __fmul_rn(__fmul_rn(one_m_b2, gv[i]), gv[i]));
+        mn[i] = __fmaf_rn(one_m_b1, gv[i], __fmul_rn(h.b1, mf));
+        vn[i] = __fmaf_rn(__fmul_rn(one_m_b2, gv[i]), gv[i], __fmul_rn(h.b2, vf));
       } else {
         mn[i] = 0.0f;
         vn[i] = 0.0f;
@@ -161,28 +195,51 @@ __global__ void __launch_bounds__(kThreads) adam8_multi_kernel(const __grid_cons
       s.ms[blk] = nms;
       s.vs[blk] = nvs;
     }
+    // Warp-uniform reciprocals of this block's divisors (the divisors are
+    // >= 1e-14 and finite, so RN(1/b) is a normal number).
+    const float y_ms = __frcp_rn(nms);
+    const float y_vs = __frcp_rn(nvs);
 
     int mc[8], vc[8];
+    float qm[8], qv[8], t1[8], t2[8];
+    bool fast = true;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      qm[i] = div_recip(mn[i], nms, y_ms);
+      qv[i] = div_recip(vn[i], nvs, y_vs);
+      t1[i] = div_recip(mn[i], h.bc1, y_bc1);
+      t2[i] = div_recip(vn[i], h.bc2, y_bc2);
+      fast = fast && div_recip_ok(mn[i]) && div_recip_ok(vn[i]);
+    }
+    if (__any_sync(0xFFFFFFFFu, !fast)) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        qm[i] = __fdiv_rn(mn[i], nms);
+        qv[i] = __fdiv_rn(vn[i], nvs);
+        t1[i] = __fdiv_rn(mn[i], h.bc1);
+        t2[i] = __fdiv_rn(vn[i], h.bc2);
+      }
+    }
     float pn[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const float qm = __fdiv_rn(mn[i], nms);
-      const float rm = mn[i] >= 0.0f ? __fadd_rn(qm, 0.5f) : __fsub_rn(qm, 0.5f);
-      mc[i] = __float2int_rz(fminf(fmaxf(rm, -127.0f), 127.0f));
-      const float rv = __fadd_rn(__fdiv_rn(vn[i], nvs), 0.5f);
-      vc[i] = __float2int_rz(fminf(fmaxf(rv, 1.0f), 127.0f));
-      const float step = __fmul_rn(h.lr, __fdiv_rn(mn[i], h.bc1));
-      const float denom = __fadd_rn(__fsqrt_rn(__fdiv_rn(vn[i], h.bc2)), h.eps);
+      // m code: trunc(clamp(q +- 0.5, -127, 127)) = sign(m_new) * floor(min(|q| + 0.5, 127))
+      const int cm = floor_small(fminf(__fadd_rn(fabsf(qm[i]), 0.5f), 127.0f));
+      mc[i] = mn[i] >= 0.0f ? cm : -cm;
+      // v code: trunc(clamp(q + 0.5, 1, 127))
+      vc[i] = floor_small(fminf(fmaxf(__fadd_rn(qv[i], 0.5f), 1.0f), 127.0f));
+      const float step = __fmul_rn(h.lr, t1[i]);
+      const float denom = __fadd_rn(__fsqrt_rn(t2[i]), h.eps);
       pn[i] = __fsub_rn(pv[i], __fdiv_rn(step, denom));
     }
 
     if (vec) {
       if (s.bf16) {
         uint4 q;
-        q.x = f32_to_bf16_rne(pn[0]) | (f32_to_bf16_rne(pn[1]) << 16);
-        q.y = f32_to_bf16_rne(pn[2]) | (f32_to_bf16_rne(pn[3]) << 16);
-        q.z = f32_to_bf16_rne(pn[4]) | (f32_to_bf16_rne(pn[5]) << 16);
-        q.w = f32_to_bf16_rne(pn[6]) | (f32_to_bf16_rne(pn[7]) << 16);
+        q.x = pack_bf16x2_rne(pn[0], pn[1]);
+        q.y = pack_bf16x2_rne(pn[2], pn[3]);
+        q.z = pack_bf16x2_rne(pn[4], pn[5]);
+        q.w = pack_bf16x2_rne(pn[6], pn[7]);
         __stcs(reinterpret_cast<uint4*>(static_cast<uint16_t*>(s.p) + e0), q);
       } else {
         float4* pp = reinterpret_cast<float4*>(static_cast<float*>(s.p) + e0);

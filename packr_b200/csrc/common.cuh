@@ -24,7 +24,7 @@ int launch_status();
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
-inline bool aligned(const void* p, uintptr_t a) {
+__host__ __device__ inline bool aligned(const void* p, uintptr_t a) {
   return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0;
 }
 
@@ -38,5 +38,13 @@ __device__ __forceinline__ uint32_t f32_to_bf16_rne(float f) {
 }
 
 __device__ __forceinline__ float bf16_to_f32(uint32_t h) { return __uint_as_float(h << 16); }
+
+// Two floats -> packed bf16x2 (lo in bits 0-15), round to nearest even: the
+// hardware conversion, identical to f32_to_bf16_rne for every non-NaN input.
+__device__ __forceinline__ uint32_t pack_bf16x2_rne(float lo, float hi) {
+  uint32_t d;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
 
 }  // namespace packr

@@ -1,0 +1,647 @@
+// tcgen05 GEMMs of the PackRLinear forward and backward, with the weight
+// decode fused into the operand pipeline and the lut gradient folded into the
+// dW epilogue.
+//
+// One persistent, warp-specialised kernel template serves three GEMMs
+// (K = in_features, N = out_features, T = tokens):
+//   FWD  out[T,N]  (f32)  = x[T,K] . W[K,N]           + bias      (kernel.py:133-139, layer.py:96-97)
+//   DX   dX[T,K]   (bf16) = bf16(dY)[T,N] . W[K,N]^T             (autograd.py:70)
+//   DW   dW_f[K,N] (bf16) = x^T[K,T] . dY[T,N], fp32 accumulate   (autograd.py:73-75)
+//        + dlut_sum[W_p[k,n]] += dW[k,n]                          (autograd.py:77-82)
+// with W = bf16(W_f + bf16(lut[W_p])) (autograd.py:66-67) never written to
+// HBM: decode warps read W_p (u8) and W_f (bf16) tiles straight from global
+// memory, look the 256-entry lut up in a lane-replicated shared-memory copy
+// (bank-conflict free), add in bf16 (add.rn.bf16x2; the reference's fp32 add
+// then bf16 rounding gives the same bits because 24 >= 2*8+2), and store the
+// bf16 operand into the 128-byte-swizzled shared-memory tile the tensor core
+// reads.  Activations (x, dY) arrive by TMA.
+//
+// Roles (one CTA per SM, persistent over output tiles of 128 x 256):
+//   warp 0      TMA producer (activation tiles; both operands for DW)
+//   warp 1      TMEM owner + single-thread tcgen05.mma issuer
+//   warps 2-5   epilogue: tcgen05.ld of the f32 accumulator, bias / rounding /
+//               lut-gradient histogram, global stores
+//   warps 6-13  weight decode (FWD, DX only)
+// Shared memory: 4 stages x (A 16 KB + B 32 KB) + 32 KB lut copy (decode
+// modes) or 4 KB of per-warp lut-gradient histograms (DW).  TMEM: two
+// 128 x 256 f32 accumulators (512 columns) so the epilogue of tile i overlaps
+// the mainloop of tile i+1.  Every mbarrier wait is bounded (2 s); a wait that
+// gives up sets the CTA abort word and the device timeout word, every role
+// drains and the kernel returns.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "sm100.cuh"
+
+namespace packr {
+namespace gemm {
+
+using namespace sm100;
+
+constexpr int BM = 128, BN = 256, BK = 64, UK = 16;
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;  // 16 KB
+constexpr int B_BYTES = BN * BK * 2;  // 32 KB
+constexpr int EPI_WARPS = 4;
+constexpr int DEC_WARPS = 8;
+constexpr int DEC_THREADS = DEC_WARPS * 32;
+constexpr int LUT_BYTES = 256 * 32 * 4;  // one u32 per (entry, lane)
+constexpr int HIST_BYTES = EPI_WARPS * 256 * 4;
+constexpr int ACC_COLS = BN;
+constexpr int TMEM_COLS = 2 * ACC_COLS;
+
+enum Mode { FWD = 0, DX = 1, DW = 2 };
+
+template <int MODE>
+struct Cfg {
+  static constexpr bool kDecode = MODE != DW;
+  static constexpr int kWarps = 2 + EPI_WARPS + (kDecode ? DEC_WARPS : 0);
+  static constexpr int kThreads = kWarps * 32;
+  static constexpr bool kAmn = MODE == DW;   // A stored MN-major in smem
+  static constexpr bool kBmn = MODE != DX;   // B stored MN-major in smem
+  static constexpr int kAuxBytes = kDecode ? LUT_BYTES : HIST_BYTES;
+  static constexpr int kBarOff = STAGES * (A_BYTES + B_BYTES) + kAuxBytes;
+  static constexpr int kSmemBytes = kBarOff + 256 + 1024;  // barriers + alignment slack
+  static constexpr uint32_t kIdesc = idesc_bf16_f32(BM, BN, kAmn, kBmn);
+};
+
+struct Params {
+  int Mg, Ng;          // output tile space: D[Mg, Ng]
+  int Kg;              // reduction length of one segment
+  int nseg;            // reduction segments (1..3), each with its own A/B maps
+  int m_tiles, n_tiles, k_blocks;
+  // decoded operand W[w_rows, w_cols] row-major with leading dimension ldw
+  const uint8_t* W_p;
+  const uint16_t* W_f;
+  const float* lut;
+  long long ldw;
+  int w_rows, w_cols;
+  int w_vec;                 // W_f 16-B / W_p 8-B aligned rows: vector loads allowed
+  // epilogue
+  void* out;
+  long long ld_out;
+  int out_f32;               // DX: 1 -> f32(bf16(acc)), 0 -> bf16
+  const void* bias;          // FWD, nullable
+  int bias_f32;              // bias dtype: 1 f32, 0 bf16
+  const uint8_t* hist_idx;   // DW: W_p (same indexing as dW_f), nullable
+  float* dlut_sum;           // DW: [256], nullable
+  int out_vec;               // out base 16-B aligned
+  int idx_vec;               // hist_idx base 16-B aligned
+};
+
+struct Maps {
+  CUtensorMap a[3];
+  CUtensorMap b[3];
+};
+
+struct Bars {
+  uint64_t full[STAGES];    // TMA bytes landed
+  uint64_t bfull[STAGES];   // decoded B written (decode modes)
+  uint64_t empty[STAGES];   // MMA done reading the stage
+  uint64_t tfull[2];        // accumulator complete
+  uint64_t tempty[2];       // accumulator drained by the epilogue
+  uint64_t drain;           // final commit before TMEM release
+  uint32_t tmem_base;
+  int abort;
+};
+
+__device__ __forceinline__ uint32_t bf16x2_add(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+
+// ------------------------------------------------------------------ decode
+// One decode thread moves 8 chunks of 8 consecutive weights per stage.
+struct Chunks {
+  uint4 wf[8];
+  uint2 wp[8];
+  uint32_t nvalid;  // 4 bits per chunk: number of valid weights (0..8)
+};
+
+// FWD: chunk i of thread t covers B rows k = t/32 + 8i (reduction), columns
+//      n = 8*(t%32) .. +7 of the 256-wide tile (W row = k, W cols = n).
+// DX : chunk i covers B row r = t/8 + 32i (output column = W row) and
+//      reduction columns 8*(t%8) .. +7 (W cols).
+template <int MODE>
+__device__ __forceinline__ void chunk_coords(int t, int i, int& brow, int& bcol8) {
+  if (MODE == FWD) {
+    brow = (t >> 5) + 8 * i;
+    bcol8 = t & 31;
+  } else {
+    brow = (t >> 3) + 32 * i;
+    bcol8 = t & 7;
+  }
+}
+
+template <int MODE>
+__device__ __forceinline__ void decode_load(Chunks& c, const Params& P, int t, int m_or_n0, int k0) {
+  c.nvalid = 0;
+  const bool vec_ok = P.w_vec != 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    int brow, bcol8;
+    chunk_coords<MODE>(t, i, brow, bcol8);
+    long long wr, wc;
+    if (MODE == FWD) {
+      wr = (long long)k0 + brow;
+      wc = (long long)m_or_n0 + 8 * bcol8;
+    } else {
+      wr = (long long)m_or_n0 + brow;
+      wc = (long long)k0 + 8 * bcol8;
+    }
+    int nv = 0;
+    if (wr < P.w_rows && wc < P.w_cols) nv = (int)min(8ll, (long long)P.w_cols - wc);
+    c.nvalid |= (uint32_t)nv << (4 * i);
+    const long long off = wr * P.ldw + wc;
+    if (nv == 8 && vec_ok) {
+      c.wf[i] = __ldg(reinterpret_cast<const uint4*>(P.W_f + off));
+      c.wp[i] = __ldg(reinterpret_cast<const uint2*>(P.W_p + off));
+    } else {
+      uint32_t f[4] = {0, 0, 0, 0}, p[2] = {0, 0};
+      for (int j = 0; j < nv; ++j) {
+        f[j >> 1] |= (uint32_t)__ldg(P.W_f + off + j) << (16 * (j & 1));
+        p[j >> 2] |= (uint32_t)__ldg(P.W_p + off + j) << (8 * (j & 3));
+      }
+      c.wf[i] = make_uint4(f[0], f[1], f[2], f[3]);
+      c.wp[i] = make_uint2(p[0], p[1]);
+    }
+  }
+}
+
+// lut_lane = shared address of this lane's column of the replicated lut:
+// entry e lives at lut_lane + 128*e.
+__device__ __forceinline__ uint32_t lut_fetch(uint32_t lut_lane, uint32_t idx_byte_shifted7) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(lut_lane + idx_byte_shifted7));
+  return v;
+}
+
+template <int MODE>
+__device__ __forceinline__ void decode_store(const Chunks& c, uint32_t b_stage, uint32_t lut_lane, int t) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    int brow, bcol8;
+    chunk_coords<MODE>(t, i, brow, bcol8);
+    uint32_t off;
+    if (MODE == FWD)  // MN-major: 64-wide column blocks of 8 KB, one 128 B row per k
+      off = (uint32_t)((bcol8 >> 3) * 8192 + brow * 128 + (((bcol8 & 7) ^ (brow & 7)) << 4));
+    else  // K-major: one 128 B row per output column
+      off = (uint32_t)(brow * 128 + ((bcol8 ^ (brow & 7)) << 4));
+    const uint32_t w[2] = {c.wp[i].x, c.wp[i].y};
+    const uint32_t f[4] = {c.wf[i].x, c.wf[i].y, c.wf[i].z, c.wf[i].w};
+    uint32_t r[4];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const uint32_t word = w[p >> 1];
+      const int sh = 16 * (p & 1);
+      const uint32_t e0 = ((word >> sh) & 0xFFu) << 7;
+      const uint32_t e1 = ((word >> (sh + 8)) & 0xFFu) << 7;
+      const uint32_t l = prmt(lut_fetch(lut_lane, e0), lut_fetch(lut_lane, e1), 0x5410u);
+      r[p] = bf16x2_add(f[p], l);
+    }
+    const int nv = (c.nvalid >> (4 * i)) & 15;
+    if (nv < 8) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (j >= nv) r[j >> 1] &= (j & 1) ? 0x0000FFFFu : 0xFFFF0000u;
+    }
+    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(b_stage + off), "r"(r[0]), "r"(r[1]),
+                 "r"(r[2]), "r"(r[3])
+                 : "memory");
+  }
+}
+
+// ------------------------------------------------------------------ kernel
+template <int MODE>
+__global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
+    packr_gemm_kernel(const Params P, const __grid_constant__ Maps maps) {
+  using C = Cfg<MODE>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint8_t* sAux = smem + STAGES * (A_BYTES + B_BYTES);
+  Bars* bars = reinterpret_cast<Bars*>(smem + C::kBarOff);
+  volatile int* abort_flag = &bars->abort;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_tiles = P.m_tiles * P.n_tiles;
+  const int kb_total = P.nseg * P.k_blocks;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->bfull[s], DEC_WARPS);
+      mbar_init(&bars->empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&bars->tfull[a], 1);
+      mbar_init(&bars->tempty[a], EPI_WARPS);
+    }
+    mbar_init(&bars->drain, 1);
+    bars->abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < P.nseg; ++s) {
+      prefetch_tmap(&maps.a[s]);
+      if (MODE == DW) prefetch_tmap(&maps.b[s]);
+    }
+  }
+  if (MODE == DW && warp >= 2 && warp < 2 + EPI_WARPS) {
+    float* hist = reinterpret_cast<float*>(sAux);
+    for (int i = threadIdx.x - 64; i < EPI_WARPS * 256; i += EPI_WARPS * 32) hist[i] = 0.0f;
+  }
+  if (warp == 1) {
+    tmem_alloc(&bars->tmem_base, TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (C::kDecode && warp >= 2 + EPI_WARPS) {
+    // Lane-replicated bf16 lut: word (e*32 + l) holds bf16_rne(lut[e]) for lane l.
+    uint32_t* lut_s = reinterpret_cast<uint32_t*>(sAux);
+    const int dw = warp - (2 + EPI_WARPS);
+    for (int e = dw; e < 256; e += DEC_WARPS) lut_s[e * 32 + lane] = f32_to_bf16_rne(__ldg(P.lut + e));
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = bars->tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int m0 = (tile % P.m_tiles) * BM;
+        const int n0 = (tile / P.m_tiles) * BN;
+        for (int kk = 0; kk < kb_total; ++kk, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+          if (!mbar_wait(&bars->empty[s], ph ^ 1u, abort_flag)) { ok = false; break; }
+          const int seg = kk / P.k_blocks;
+          const int k0 = (kk % P.k_blocks) * BK;
+          uint8_t* a_dst = sA + s * A_BYTES;
+          if (MODE == DW) {
+            mbar_arrive_expect_tx(&bars->full[s], A_BYTES + B_BYTES);
+            tma_load_2d(a_dst, &maps.a[seg], &bars->full[s], m0, k0);
+            tma_load_2d(a_dst + 8192, &maps.a[seg], &bars->full[s], m0 + 64, k0);
+            uint8_t* b_dst = sB + s * B_BYTES;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) tma_load_2d(b_dst + j * 8192, &maps.b[seg], &bars->full[s], n0 + 64 * j, k0);
+          } else {
+            mbar_arrive_expect_tx(&bars->full[s], A_BYTES);
+            tma_load_2d(a_dst, &maps.a[seg], &bars->full[s], k0, m0);
+          }
+        }
+      }
+      // Drain: every load this thread issued must land before smem is released.
+      if (!ok) {
+        for (int j = (it > STAGES ? it - STAGES : 0); j < it; ++j) {
+          volatile int no_abort = 0;
+          mbar_wait(&bars->full[j % STAGES], (uint32_t)(j / STAGES) & 1u, &no_abort);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int it = 0, t_local = 0;
+      bool ok = true;
+      const uint32_t sA0 = smem_u32(sA), sB0 = smem_u32(sB);
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++t_local) {
+        const int acc = t_local & 1;
+        const uint32_t aph = (uint32_t)(t_local >> 1) & 1u;
+        if (!mbar_wait(&bars->tempty[acc], aph ^ 1u, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * ACC_COLS);
+        for (int kk = 0; kk < kb_total; ++kk, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+          if (!mbar_wait(&bars->full[s], ph, abort_flag)) { ok = false; break; }
+          if (C::kDecode && !mbar_wait(&bars->bfull[s], ph, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_s = sA0 + s * A_BYTES, b_s = sB0 + s * B_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / UK; ++k) {
+            const uint64_t ad = C::kAmn ? sdesc_sw128(a_s + k * 2048, 8192, 1024) : sdesc_sw128(a_s + k * 32, 16, 1024);
+            const uint64_t bd = C::kBmn ? sdesc_sw128(b_s + k * 2048, 8192, 1024) : sdesc_sw128(b_s + k * 32, 16, 1024);
+            umma_bf16_ss(d_tmem, ad, bd, C::kIdesc, (kk | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(&bars->empty[s]);
+        }
+        if (!ok) break;
+        umma_commit(&bars->tfull[acc]);
+      }
+      // Every MMA issued must complete before TMEM is released.
+      umma_commit(&bars->drain);
+      volatile int no_abort = 0;
+      mbar_wait(&bars->drain, 0, &no_abort);
+    }
+  } else if (warp < 2 + EPI_WARPS) {
+    // ------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int row = q * 32 + lane;
+    float* hist = reinterpret_cast<float*>(sAux) + (warp - 2) * 256;
+    int t_local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++t_local) {
+      const int acc = t_local & 1;
+      const uint32_t aph = (uint32_t)(t_local >> 1) & 1u;
+      // every lane waits; the warp proceeds only if all lanes saw the phase
+      if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bars->tfull[acc], aph, abort_flag))) break;
+      tc_fence_after();
+      const int m0 = (tile % P.m_tiles) * BM;
+      const int n0 = (tile / P.m_tiles) * BN;
+      const long long gm = (long long)m0 + row;
+      const bool row_ok = gm < P.Mg;
+#pragma unroll 1
+      for (int cc = 0; cc < BN / 32; ++cc) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tmem_base + (uint32_t)(acc * ACC_COLS + cc * 32) + ((uint32_t)(q * 32) << 16), v);
+        tmem_ld_wait();
+        const int gn0 = n0 + cc * 32;
+        if (!row_ok || gn0 >= P.Ng) continue;
+        const int nval = min(32, P.Ng - gn0);
+        if (MODE == FWD) {
+          float* o = static_cast<float*>(P.out) + gm * P.ld_out + gn0;
+          float f[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
+          if (P.bias != nullptr) {
+            if (P.bias_f32) {
+              const float* bp = static_cast<const float*>(P.bias) + gn0;
+              for (int j = 0; j < nval; ++j) f[j] = __fadd_rn(f[j], __ldg(bp + j));
+            } else {
+              const uint16_t* bp = static_cast<const uint16_t*>(P.bias) + gn0;
+              for (int j = 0; j < nval; ++j) f[j] = __fadd_rn(f[j], bf16_to_f32(__ldg(bp + j)));
+            }
+          }
+          if (nval == 32 && (P.ld_out & 3) == 0 && P.out_vec) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) __stcs(reinterpret_cast<float4*>(o + j), make_float4(f[j], f[j + 1], f[j + 2], f[j + 3]));
+          } else {
+            for (int j = 0; j < nval; ++j) o[j] = f[j];
+          }
+        } else if (MODE == DX) {
+          uint32_t h[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) h[j] = f32_to_bf16_rne(__uint_as_float(v[j]));
+          if (P.out_f32) {
+            float* o = static_cast<float*>(P.out) + gm * P.ld_out + gn0;
+            if (nval == 32 && (P.ld_out & 3) == 0 && P.out_vec) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4)
+                __stcs(reinterpret_cast<float4*>(o + j), make_float4(bf16_to_f32(h[j]), bf16_to_f32(h[j + 1]),
+                                                                      bf16_to_f32(h[j + 2]), bf16_to_f32(h[j + 3])));
+            } else {
+              for (int j = 0; j < nval; ++j) o[j] = bf16_to_f32(h[j]);
+            }
+          } else {
+            uint16_t* o = static_cast<uint16_t*>(P.out) + gm * P.ld_out + gn0;
+            if (nval == 32 && (P.ld_out & 7) == 0 && P.out_vec) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 8)
+                __stcs(reinterpret_cast<uint4*>(o + j), make_uint4(h[j] | (h[j + 1] << 16), h[j + 2] | (h[j + 3] << 16),
+                                                                    h[j + 4] | (h[j + 5] << 16), h[j + 6] | (h[j + 7] << 16)));
+            } else {
+              for (int j = 0; j < nval; ++j) o[j] = (uint16_t)h[j];
+            }
+          }
+        } else {  // DW
+          if (P.out != nullptr) {
+            uint16_t* o = static_cast<uint16_t*>(P.out) + gm * P.ld_out + gn0;
+            uint32_t h[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) h[j] = f32_to_bf16_rne(__uint_as_float(v[j]));
+            if (nval == 32 && (P.ld_out & 7) == 0 && P.out_vec) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 8)
+                __stcs(reinterpret_cast<uint4*>(o + j), make_uint4(h[j] | (h[j + 1] << 16), h[j + 2] | (h[j + 3] << 16),
+                                                                    h[j + 4] | (h[j + 5] << 16), h[j + 6] | (h[j + 7] << 16)));
+            } else {
+              for (int j = 0; j < nval; ++j) o[j] = (uint16_t)h[j];
+            }
+          }
+          if (P.hist_idx != nullptr) {
+            const uint8_t* ip = P.hist_idx + gm * P.ld_out + gn0;
+            uint32_t w[8];
+            if (nval == 32 && (P.ld_out & 15) == 0 && P.idx_vec) {
+              const uint4 a = __ldg(reinterpret_cast<const uint4*>(ip));
+              const uint4 b = __ldg(reinterpret_cast<const uint4*>(ip + 16));
+              w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w; w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
+            } else {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) w[j] = 0;
+              for (int j = 0; j < nval; ++j) w[j >> 2] |= (uint32_t)__ldg(ip + j) << (8 * (j & 3));
+            }
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if (j < nval) atomicAdd(hist + ((w[j >> 2] >> (8 * (j & 3))) & 0xFFu), __uint_as_float(v[j]));
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->tempty[acc]);
+    }
+    if (MODE == DW && P.dlut_sum != nullptr) {
+      asm volatile("bar.sync 1, %0;" ::"n"(EPI_WARPS * 32) : "memory");
+      const float* h0 = reinterpret_cast<const float*>(sAux);
+      const int et = threadIdx.x - 64;
+      for (int b = et; b < 256; b += EPI_WARPS * 32) {
+        float s = 0.0f;
+#pragma unroll
+        for (int w = 0; w < EPI_WARPS; ++w) s += h0[w * 256 + b];
+        if (s != 0.0f) atomicAdd(P.dlut_sum + b, s);
+      }
+    }
+  } else if (C::kDecode) {
+    // ------------------------------------------------ weight decode
+    const int t = threadIdx.x - (2 + EPI_WARPS) * 32;
+    const uint32_t lut_lane = smem_u32(sAux) + (uint32_t)lane * 4u;
+    const uint32_t sB0 = smem_u32(sB);
+    const int my_tiles = blockIdx.x < num_tiles ? (num_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    const int total = my_tiles * kb_total;
+    auto coords = [&](int it, int& mn0, int& k0) {
+      const int tl = it / kb_total;
+      const int kk = it % kb_total;
+      const int tile = blockIdx.x + tl * gridDim.x;
+      // the decoded operand spans the output-column (n) tile of FWD / DX
+      mn0 = (tile / P.m_tiles) * BN;
+      k0 = (kk % P.k_blocks) * BK;
+    };
+    auto process = [&](const Chunks& c, int it) -> bool {
+      const int s = it % STAGES;
+      const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+      if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bars->empty[s], ph ^ 1u, abort_flag))) return false;
+      decode_store<MODE>(c, sB0 + s * B_BYTES, lut_lane, t);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->bfull[s]);
+      return true;
+    };
+    Chunks c0, c1;
+    int mn0, k0;
+    if (total > 0) {
+      coords(0, mn0, k0);
+      decode_load<MODE>(c0, P, t, mn0, k0);
+    }
+    for (int it = 0; it < total; it += 2) {
+      if (it + 1 < total) {
+        coords(it + 1, mn0, k0);
+        decode_load<MODE>(c1, P, t, mn0, k0);
+      }
+      if (!process(c0, it)) break;
+      if (it + 1 >= total) break;
+      if (it + 2 < total) {
+        coords(it + 2, mn0, k0);
+        decode_load<MODE>(c0, P, t, mn0, k0);
+      }
+      if (!process(c1, it + 1)) break;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------ host
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// bf16 2-D map over [rows, inner] with the given row stride, 128-byte swizzle,
+// box {64, box_rows}.  Out-of-range elements read as zero.
+int make_map(CUtensorMap* m, const void* base, long long inner, long long rows, long long row_stride_bytes,
+             int box_rows) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return PACKR_ERR_CUDA;
+  if (!aligned(base, 16) || (row_stride_bytes & 15) != 0) return PACKR_ERR_ALIGNMENT;
+  if (inner <= 0 || rows <= 0) return PACKR_ERR_SHAPE;
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)row_stride_bytes};
+  cuuint32_t box[2] = {64u, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? PACKR_OK : PACKR_ERR_INVALID_ARGUMENT;
+}
+
+template <int MODE>
+int launch(Params P, const Maps& maps, cudaStream_t stream) {
+  using C = Cfg<MODE>;
+  static std::once_flag attr_once[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int attr_rc = 0;
+  std::call_once(attr_once[dev & 63], [&] {
+    attr_rc = cudaFuncSetAttribute(packr_gemm_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   C::kSmemBytes) != cudaSuccess;
+  });
+  if (attr_rc) return PACKR_ERR_CUDA;
+  P.w_vec = (P.ldw & 7) == 0 && aligned(P.W_f, 16) && aligned(P.W_p, 8);
+  P.out_vec = aligned(P.out, 16);
+  P.idx_vec = aligned(P.hist_idx, 16);
+  P.m_tiles = (P.Mg + BM - 1) / BM;
+  P.n_tiles = (P.Ng + BN - 1) / BN;
+  P.k_blocks = (P.Kg + BK - 1) / BK;
+  const int tiles = P.m_tiles * P.n_tiles;
+  if (tiles == 0) return PACKR_OK;
+  const int grid = tiles < sm_count() ? tiles : sm_count();
+  packr_gemm_kernel<MODE><<<grid, C::kThreads, C::kSmemBytes, stream>>>(P, maps);
+  return launch_status();
+}
+
+}  // namespace gemm
+}  // namespace packr
+
+namespace packr {
+namespace gemm {
+
+// Stand-alone decode of W = bf16(W_f + bf16(lut[W_p])) into a row-major
+// [K, N] bf16 array, through exactly the load / lookup / add / swizzled store
+// routines the FWD GEMM's decode warps run, one 64 x 256 tile at a time.
+__global__ void __launch_bounds__(DEC_THREADS) decode_check_kernel(const Params P, uint16_t* __restrict__ out,
+                                                                  int k_tiles, int n_tiles) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint32_t* lut_s = reinterpret_cast<uint32_t*>(smem);
+  uint8_t* tile = smem + LUT_BYTES;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, t = threadIdx.x;
+  for (int e = warp; e < 256; e += DEC_WARPS) lut_s[e * 32 + lane] = f32_to_bf16_rne(__ldg(P.lut + e));
+  __syncthreads();
+  const uint32_t lut_lane = smem_u32(lut_s) + (uint32_t)lane * 4u;
+  for (int idx = blockIdx.x; idx < k_tiles * n_tiles; idx += gridDim.x) {
+    const int k0 = (idx % k_tiles) * BK, n0 = (idx / k_tiles) * BN;
+    Chunks c;
+    decode_load<FWD>(c, P, t, n0, k0);
+    decode_store<FWD>(c, smem_u32(tile), lut_lane, t);
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      int brow, bcol8;
+      chunk_coords<FWD>(t, i, brow, bcol8);
+      const uint32_t off = (uint32_t)((bcol8 >> 3) * 8192 + brow * 128 + (((bcol8 & 7) ^ (brow & 7)) << 4));
+      const uint4 q = *reinterpret_cast<const uint4*>(tile + off);
+      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+      const long long r = (long long)k0 + brow, c0 = (long long)n0 + 8 * bcol8;
+      if (r >= P.w_rows) continue;
+      for (int j = 0; j < 8 && c0 + j < P.w_cols; ++j)
+        out[r * P.ldw + c0 + j] = (uint16_t)(w[j >> 1] >> (16 * (j & 1)));
+    }
+    __syncthreads();
+  }
+}
+
+int decode_check(const uint8_t* W_p, const uint16_t* W_f, const float* lut, uint16_t* out, long long K, long long N,
+                 cudaStream_t st) {
+  static std::once_flag once[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int smem = LUT_BYTES + B_BYTES + 1024;
+  int rc = 0;
+  std::call_once(once[dev & 63], [&] {
+    rc = cudaFuncSetAttribute(decode_check_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess;
+  });
+  if (rc) return PACKR_ERR_CUDA;
+  Params P{};
+  P.W_p = W_p;
+  P.W_f = W_f;
+  P.lut = lut;
+  P.ldw = N;
+  P.w_rows = (int)K;
+  P.w_cols = (int)N;
+  P.w_vec = (N & 7) == 0 && aligned(W_f, 16) && aligned(W_p, 8);
+  const long long kt = (K + BK - 1) / BK, nt = (N + BN - 1) / BN;
+  if (kt * nt == 0) return PACKR_OK;
+  const long long grid = kt * nt < 4 * sm_count() ? kt * nt : 4 * sm_count();
+  decode_check_kernel<<<(int)grid, DEC_THREADS, smem, st>>>(P, out, (int)kt, (int)nt);
+  return launch_status();
+}
+
+}  // namespace gemm
+}  // namespace packr

@@ -3,3 +3,6 @@
 // relocatable device code.
 #include "common.cu"
 #include "adam8.cu"
+#include "prep.cu"
+#include "gemm.cu"
+#include "linear.cu"

@@ -1,0 +1,254 @@
+// C-ABI entry points of the PackRLinear forward and backward: argument
+// checks, workspace carving, tensor-map encoding and the launch sequence.
+#include "common.cuh"
+
+namespace packr {
+namespace linear {
+
+constexpr size_t kAlign = 256;
+
+inline size_t align_up(size_t v) { return (v + kAlign - 1) & ~(kAlign - 1); }
+inline long long round8(long long v) { return (v + 7) & ~7ll; }
+
+// Bump allocator over the caller's workspace.
+struct Carve {
+  uint8_t* base;
+  size_t off = 0;
+  template <class T>
+  T* take(size_t count) {
+    if (count == 0) return nullptr;
+    T* p = base ? reinterpret_cast<T*>(base + off) : nullptr;
+    off = align_up(off + count * sizeof(T));
+    return p;
+  }
+};
+
+bool x_needs_copy(int x_dtype, long long K) { return x_dtype == PACKR_DTYPE_F32 || (K & 7) != 0; }
+
+struct FwdPlan {
+  uint16_t* xh;
+};
+
+size_t plan_forward(Carve& c, FwdPlan& p, long long M, long long K, int x_dtype) {
+  p.xh = x_needs_copy(x_dtype, K) ? c.take<uint16_t>((size_t)M * round8(K)) : nullptr;
+  return c.off;
+}
+
+struct BwdPlan {
+  uint16_t *dh, *dl, *xh, *xl;
+  float *colsum, *dlut_sum;
+  int32_t* counts;
+};
+
+size_t plan_backward(Carve& c, BwdPlan& p, long long M, long long K, long long N, int x_dtype, int flags,
+                     bool want_dx, bool want_dw, bool want_dlut, bool want_dbias, bool have_counts) {
+  const bool split = (flags & PACKR_BWD_DW_SPLIT) != 0 && (want_dw || want_dlut);
+  p.dh = c.take<uint16_t>((size_t)M * round8(N));
+  p.dl = split ? c.take<uint16_t>((size_t)M * round8(N)) : nullptr;
+  const bool need_x = want_dw || want_dlut;
+  p.xh = need_x && x_needs_copy(x_dtype, K) ? c.take<uint16_t>((size_t)M * round8(K)) : nullptr;
+  p.xl = need_x && split && x_dtype == PACKR_DTYPE_F32 ? c.take<uint16_t>((size_t)M * round8(K)) : nullptr;
+  p.colsum = want_dbias ? c.take<float>((size_t)N) : nullptr;
+  p.dlut_sum = want_dlut ? c.take<float>(256) : nullptr;
+  p.counts = want_dlut && !have_counts ? c.take<int32_t>(256) : nullptr;
+  (void)want_dx;
+  return c.off;
+}
+
+int check_common(const void* x, int x_dtype, const uint8_t* W_p, const uint16_t* W_f, const float* lut, long long M,
+                 long long K, long long N) {
+  if (M < 0 || K <= 0 || N <= 0) return PACKR_ERR_SHAPE;
+  if (M > 0x7FFFFFFFll || K > 0x7FFFFFFFll || N > 0x7FFFFFFFll) return PACKR_ERR_SHAPE;
+  if (x_dtype != PACKR_DTYPE_F32 && x_dtype != PACKR_DTYPE_BF16) return PACKR_ERR_INVALID_ARGUMENT;
+  if ((M > 0 && x == nullptr) || W_p == nullptr || W_f == nullptr || lut == nullptr) return PACKR_ERR_INVALID_ARGUMENT;
+  if (!aligned(W_f, 2) || !aligned(lut, 4) || (x && !aligned(x, x_dtype == PACKR_DTYPE_F32 ? 4 : 2)))
+    return PACKR_ERR_ALIGNMENT;
+  return PACKR_OK;
+}
+
+}  // namespace linear
+}  // namespace packr
+
+using namespace packr;
+using namespace packr::linear;
+
+extern "C" size_t packr_forward_workspace_bytes(int64_t M, int64_t K, int64_t N, int x_dtype) {
+  (void)N;
+  Carve c{nullptr};
+  FwdPlan p;
+  return plan_forward(c, p, M > 0 ? M : 0, K > 0 ? K : 0, x_dtype);
+}
+
+extern "C" int packr_forward(const void* x, int x_dtype, const uint8_t* W_p, const uint16_t* W_f, const float* lut,
+                             const void* bias, int bias_dtype, float* out, int64_t M, int64_t K, int64_t N, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+  int st = check_common(x, x_dtype, W_p, W_f, lut, M, K, N);
+  if (st != PACKR_OK) return st;
+  if (out == nullptr && M > 0) return PACKR_ERR_INVALID_ARGUMENT;
+  if (bias != nullptr && bias_dtype != PACKR_DTYPE_BF16 && bias_dtype != PACKR_DTYPE_F32)
+    return PACKR_ERR_INVALID_ARGUMENT;
+  if (bias != nullptr && !aligned(bias, bias_dtype == PACKR_DTYPE_F32 ? 4 : 2)) return PACKR_ERR_ALIGNMENT;
+  if ((st = check_device()) != PACKR_OK) return st;
+  if (M == 0) return PACKR_OK;
+  cudaStream_t s = as_stream(stream);
+  Carve c{static_cast<uint8_t*>(workspace)};
+  FwdPlan p;
+  const size_t need = plan_forward(c, p, M, K, x_dtype);
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need || !aligned(workspace, kAlign)))
+    return PACKR_ERR_WORKSPACE;
+  const void* a_ptr = x;
+  long long lda = K;
+  if (p.xh != nullptr) {
+    st = prep::split_rows(x, x_dtype == PACKR_DTYPE_F32, K, M, K, p.xh, nullptr, round8(K), nullptr, s);
+    if (st != PACKR_OK) return st;
+    a_ptr = p.xh;
+    lda = round8(K);
+  }
+  gemm::Maps maps;
+  st = gemm::make_map(&maps.a[0], a_ptr, K, M, lda * 2, gemm::BM);
+  if (st != PACKR_OK) return st;
+  gemm::Params P{};
+  P.Mg = (int)M;
+  P.Ng = (int)N;
+  P.Kg = (int)K;
+  P.nseg = 1;
+  P.W_p = W_p;
+  P.W_f = W_f;
+  P.lut = lut;
+  P.ldw = N;
+  P.w_rows = (int)K;
+  P.w_cols = (int)N;
+  P.out = out;
+  P.ld_out = N;
+  P.bias = bias;
+  P.bias_f32 = bias_dtype == PACKR_DTYPE_F32;
+  return gemm::launch<gemm::FWD>(P, maps, s);
+}
+
+extern "C" size_t packr_backward_workspace_bytes(int64_t M, int64_t K, int64_t N, int x_dtype, int flags) {
+  Carve c{nullptr};
+  BwdPlan p;
+  return plan_backward(c, p, M > 0 ? M : 0, K > 0 ? K : 0, N > 0 ? N : 0, x_dtype, flags, true, true, true, true,
+                       false);
+}
+
+extern "C" int packr_backward(const float* dY, const void* x, int x_dtype, const uint8_t* W_p, const uint16_t* W_f,
+                              const float* lut, const int32_t* lut_counts, void* dX, uint16_t* dW_f, float* dlut,
+                              uint16_t* dbias, int64_t M, int64_t K, int64_t N, int flags, void* workspace,
+                              size_t workspace_bytes, void* stream) {
+  int st = check_common(x, x_dtype, W_p, W_f, lut, M, K, N);
+  if (st != PACKR_OK) return st;
+  if (M > 0 && dY == nullptr) return PACKR_ERR_INVALID_ARGUMENT;
+  if ((flags & ~PACKR_BWD_DW_SPLIT) != 0) return PACKR_ERR_INVALID_ARGUMENT;
+  if ((dY && !aligned(dY, 4)) || (dX && !aligned(dX, x_dtype == PACKR_DTYPE_F32 ? 4 : 2)) ||
+      (dW_f && !aligned(dW_f, 2)) || (dlut && !aligned(dlut, 4)) || (dbias && !aligned(dbias, 2)) ||
+      (lut_counts && !aligned(lut_counts, 4)))
+    return PACKR_ERR_ALIGNMENT;
+  if ((st = check_device()) != PACKR_OK) return st;
+  cudaStream_t s = as_stream(stream);
+  const bool want_dx = dX != nullptr, want_dw = dW_f != nullptr, want_dlut = dlut != nullptr,
+             want_dbias = dbias != nullptr;
+  if (M == 0) {  // empty batch: every gradient is zero
+    if (want_dw && cudaMemsetAsync(dW_f, 0, (size_t)K * N * 2, s) != cudaSuccess) return PACKR_ERR_CUDA;
+    if (want_dlut && cudaMemsetAsync(dlut, 0, 256 * 4, s) != cudaSuccess) return PACKR_ERR_CUDA;
+    if (want_dbias && cudaMemsetAsync(dbias, 0, (size_t)N * 2, s) != cudaSuccess) return PACKR_ERR_CUDA;
+    return PACKR_OK;
+  }
+  Carve c{static_cast<uint8_t*>(workspace)};
+  BwdPlan p;
+  const size_t need = plan_backward(c, p, M, K, N, x_dtype, flags, want_dx, want_dw, want_dlut, want_dbias,
+                                    lut_counts != nullptr);
+  if (workspace == nullptr || workspace_bytes < need || !aligned(workspace, kAlign)) return PACKR_ERR_WORKSPACE;
+  if (p.colsum && cudaMemsetAsync(p.colsum, 0, (size_t)N * 4, s) != cudaSuccess) return PACKR_ERR_CUDA;
+  if (p.dlut_sum && cudaMemsetAsync(p.dlut_sum, 0, 256 * 4, s) != cudaSuccess) return PACKR_ERR_CUDA;
+  const long long ldN = round8(N), ldK = round8(K);
+  // bf16(dY) (+ its residual for the split dW) and the bias gradient sums
+  st = prep::split_rows(dY, 1, N, M, N, p.dh, p.dl, ldN, p.colsum, s);
+  if (st != PACKR_OK) return st;
+  if (want_dx) {
+    gemm::Maps maps;
+    if ((st = gemm::make_map(&maps.a[0], p.dh, N, M, ldN * 2, gemm::BM)) != PACKR_OK) return st;
+    gemm::Params P{};
+    P.Mg = (int)M;
+    P.Ng = (int)K;
+    P.Kg = (int)N;
+    P.nseg = 1;
+    P.W_p = W_p;
+    P.W_f = W_f;
+    P.lut = lut;
+    P.ldw = N;
+    P.w_rows = (int)K;
+    P.w_cols = (int)N;
+    P.out = dX;
+    P.ld_out = K;
+    P.out_f32 = x_dtype == PACKR_DTYPE_F32;
+    if ((st = gemm::launch<gemm::DX>(P, maps, s)) != PACKR_OK) return st;
+  }
+  if (want_dw || want_dlut) {
+    const void* xa = x;
+    long long ldx = K;
+    if (p.xh != nullptr) {
+      st = prep::split_rows(x, x_dtype == PACKR_DTYPE_F32, K, M, K, p.xh, p.xl, ldK, nullptr, s);
+      if (st != PACKR_OK) return st;
+      xa = p.xh;
+      ldx = ldK;
+    }
+    // reduction segments: x.dh  [+ x.dl  [+ xl.dh]]
+    gemm::Maps maps;
+    int nseg = 0;
+    auto add_seg = [&](const void* a, long long lda, const void* b) -> int {
+      int r = gemm::make_map(&maps.a[nseg], a, K, M, lda * 2, 64);
+      if (r == PACKR_OK) r = gemm::make_map(&maps.b[nseg], b, N, M, ldN * 2, 64);
+      ++nseg;
+      return r;
+    };
+    if ((st = add_seg(xa, ldx, p.dh)) != PACKR_OK) return st;
+    if (p.dl != nullptr) {
+      if ((st = add_seg(xa, ldx, p.dl)) != PACKR_OK) return st;
+      if (p.xl != nullptr && (st = add_seg(p.xl, ldK, p.dh)) != PACKR_OK) return st;
+    }
+    gemm::Params P{};
+    P.Mg = (int)K;
+    P.Ng = (int)N;
+    P.Kg = (int)M;
+    P.nseg = nseg;
+    P.out = dW_f;
+    P.ld_out = N;
+    P.hist_idx = want_dlut ? W_p : nullptr;
+    P.dlut_sum = p.dlut_sum;
+    if ((st = gemm::launch<gemm::DW>(P, maps, s)) != PACKR_OK) return st;
+  }
+  const int32_t* counts = lut_counts;
+  if (want_dlut && counts == nullptr) {
+    if ((st = prep::bincount256(W_p, K * N, p.counts, s)) != PACKR_OK) return st;
+    counts = p.counts;
+  }
+  return prep::finalize(dlut, p.dlut_sum, counts, dbias, p.colsum, N, s);
+}
+
+extern "C" int packr_bincount256(const uint8_t* W_p, int64_t n, int32_t* counts, void* stream) {
+  if (n < 0) return PACKR_ERR_SHAPE;
+  if ((n > 0 && W_p == nullptr) || counts == nullptr) return PACKR_ERR_INVALID_ARGUMENT;
+  if (!aligned(counts, 4)) return PACKR_ERR_ALIGNMENT;
+  int st = check_device();
+  if (st != PACKR_OK) return st;
+  return prep::bincount256(W_p, n, counts, as_stream(stream));
+}
+
+extern "C" int packr_lut_finalize(float* dlut, const float* dlut_sum, const int32_t* counts, void* stream) {
+  if (!dlut || !dlut_sum || !counts) return PACKR_ERR_INVALID_ARGUMENT;
+  int st = check_device();
+  if (st != PACKR_OK) return st;
+  return prep::finalize(dlut, dlut_sum, counts, nullptr, nullptr, 0, as_stream(stream));
+}
+
+extern "C" int packr_decode_bf16(const uint8_t* W_p, const uint16_t* W_f, const float* lut, uint16_t* out, int64_t K,
+                                 int64_t N, void* stream) {
+  if (K < 0 || N < 0 || K > 0x7FFFFFFFll || N > 0x7FFFFFFFll) return PACKR_ERR_SHAPE;
+  if (K * N == 0) return PACKR_OK;
+  if (!W_p || !W_f || !lut || !out) return PACKR_ERR_INVALID_ARGUMENT;
+  if (!aligned(W_f, 2) || !aligned(out, 2) || !aligned(lut, 4)) return PACKR_ERR_ALIGNMENT;
+  int st = check_device();
+  if (st != PACKR_OK) return st;
+  return gemm::decode_check(W_p, W_f, lut, out, K, N, as_stream(stream));
+}

@@ -1,0 +1,164 @@
+"""PackR matmul on B200: thin torch-facing wrappers over libpackr_b200.so.
+
+packr_matmul(x, W_p, W_f, lut, bias=None) keeps the signature, the float32
+[M, N] result and the assertions of reference packr/kernel.py:98-141, but the
+decode and the GEMM are one sm_100a kernel (tcgen05 tensor cores, TMEM
+accumulator) that decodes W = bf16(W_f + bf16(lut[W_p])) in shared memory.
+The operands are bf16: x (rounded to bf16 when it is f32) and the decoded W,
+accumulated in f32.
+
+forward() / backward() below are the raw entry points the autograd Function
+uses; they allocate outputs and the workspace through torch's caching
+allocator and launch on torch's current stream.  No CPU path exists: CPU
+tensors raise.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import torch
+
+from . import _lib
+
+# dW precision: "auto" = fp32-faithful split (x . dY_hi + x . dY_lo
+# [+ x_lo . dY_hi]) when x is f32, dY rounded to bf16 otherwise; "split" and
+# "bf16" force one or the other.
+DW_PRECISION = os.environ.get("PACKR_DW_PRECISION", "auto")
+
+
+def _stream(device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    if t.dtype == torch.bfloat16:
+        return _lib.PACKR_DTYPE_BF16
+    if t.dtype == torch.float32:
+        return _lib.PACKR_DTYPE_F32
+    raise TypeError(f"unsupported dtype {t.dtype}")
+
+
+def _ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _workspace(nbytes: int, device) -> torch.Tensor | None:
+    if nbytes == 0:
+        return None
+    return torch.empty(nbytes, dtype=torch.uint8, device=device)
+
+
+def _as_operand(x: torch.Tensor) -> torch.Tensor:
+    if x.dtype not in (torch.bfloat16, torch.float32):
+        x = x.float()
+    return x.contiguous()
+
+
+def forward(x: torch.Tensor, W_p: torch.Tensor, W_f: torch.Tensor, lut: torch.Tensor,
+            bias: torch.Tensor | None = None) -> torch.Tensor:
+    """out[M, N] float32 = x @ decode(W_p, W_f, lut) + bias, on the GPU."""
+    lib = _lib.load()
+    x = _as_operand(x)
+    M, K = x.shape
+    N = W_p.shape[1]
+    dev = x.device
+    W_f = W_f.contiguous()
+    lut = lut.detach().float().contiguous()
+    if bias is not None:
+        bias = bias.detach()
+        if bias.dtype not in (torch.bfloat16, torch.float32):
+            bias = bias.float()
+        bias = bias.contiguous()
+    out = torch.empty(M, N, dtype=torch.float32, device=dev)
+    xd = _dtype_code(x)
+    with torch.cuda.device(dev):
+        ws = _workspace(lib.packr_forward_workspace_bytes(M, K, N, xd), dev)
+        code = lib.packr_forward(_ptr(x), xd, _ptr(W_p), _ptr(W_f), _ptr(lut), _ptr(bias),
+                                 _dtype_code(bias) if bias is not None else 0, _ptr(out), M, K, N, _ptr(ws),
+                                 0 if ws is None else ws.numel(), _stream(dev))
+    _lib.check("packr_forward", code)
+    return out
+
+
+def bincount256(W_p: torch.Tensor) -> torch.Tensor:
+    """int32[256] counts of the byte values of W_p (on W_p's device)."""
+    lib = _lib.load()
+    W_p = W_p.contiguous()
+    counts = torch.empty(256, dtype=torch.int32, device=W_p.device)
+    with torch.cuda.device(W_p.device):
+        code = lib.packr_bincount256(_ptr(W_p), W_p.numel(), _ptr(counts), _stream(W_p.device))
+    _lib.check("packr_bincount256", code)
+    return counts
+
+
+def decode_bf16(W_p: torch.Tensor, W_f: torch.Tensor, lut: torch.Tensor) -> torch.Tensor:
+    """bf16(W_f + bf16(lut[W_p])) through the GEMM's own decode routine."""
+    lib = _lib.load()
+    K, N = W_p.shape
+    out = torch.empty(K, N, dtype=torch.bfloat16, device=W_p.device)
+    with torch.cuda.device(W_p.device):
+        code = lib.packr_decode_bf16(_ptr(W_p.contiguous()), _ptr(W_f.contiguous()),
+                                     _ptr(lut.detach().float().contiguous()), _ptr(out), K, N, _stream(W_p.device))
+    _lib.check("packr_decode_bf16", code)
+    return out
+
+
+def dw_split_for(x_dtype: torch.dtype) -> bool:
+    if DW_PRECISION == "split":
+        return True
+    if DW_PRECISION == "bf16":
+        return False
+    return x_dtype == torch.float32
+
+
+def backward(dY: torch.Tensor, x: torch.Tensor, W_p: torch.Tensor, W_f: torch.Tensor, lut: torch.Tensor,
+             counts: torch.Tensor | None, need_dx: bool, need_dw: bool, need_dlut: bool, need_dbias: bool):
+    """Returns (dX, dW_f, dlut, dbias); entries not requested are None."""
+    lib = _lib.load()
+    x = _as_operand(x)
+    M, K = x.shape
+    N = W_p.shape[1]
+    dev = x.device
+    dY = dY.float().contiguous()
+    dX = torch.empty(M, K, dtype=x.dtype, device=dev) if need_dx else None
+    dW = torch.empty(K, N, dtype=torch.bfloat16, device=dev) if need_dw else None
+    dlut = torch.empty(256, dtype=torch.float32, device=dev) if need_dlut else None
+    dbias = torch.empty(N, dtype=torch.bfloat16, device=dev) if need_dbias else None
+    if not (need_dx or need_dw or need_dlut or need_dbias):
+        return None, None, None, None
+    xd = _dtype_code(x)
+    flags = _lib.PACKR_BWD_DW_SPLIT if dw_split_for(x.dtype) else 0
+    with torch.cuda.device(dev):
+        ws = _workspace(lib.packr_backward_workspace_bytes(M, K, N, xd, flags), dev)
+        code = lib.packr_backward(_ptr(dY), _ptr(x), xd, _ptr(W_p), _ptr(W_f.contiguous()),
+                                  _ptr(lut.detach().float().contiguous()), _ptr(counts), _ptr(dX), _ptr(dW),
+                                  _ptr(dlut), _ptr(dbias), M, K, N, flags, _ptr(ws), 0 if ws is None else ws.numel(),
+                                  _stream(dev))
+    _lib.check("packr_backward", code)
+    return dX, dW, dlut, dbias
+
+
+def packr_matmul(x, W_p, W_f, lut, bias=None):
+    """PackR matmul: out = x @ (W_f + lut[W_p]) + bias  (float32 [M, N]).
+
+    Args:
+        x:    [M, K] fp32 or bf16 activations (CUDA)
+        W_p:  [K, N] uint8 byte indices (contiguous)
+        W_f:  [K, N] bf16 residual weights
+        lut:  [256]  fp32 lookup table
+        bias: [N] optional bias (bf16 or fp32)
+    """
+    assert x.is_cuda and W_p.is_cuda and W_f.is_cuda and lut.is_cuda
+    assert W_p.dtype == torch.uint8, f"W_p must be uint8, got {W_p.dtype}"
+    assert W_p.is_contiguous(), "W_p must be contiguous"
+    M, K = x.shape
+    K2, N = W_f.shape
+    assert K2 == K, f"W_f rows ({K2}) != x cols ({K})"
+    assert W_f.dtype == torch.bfloat16, f"W_f must be bf16, got {W_f.dtype}"
+    assert tuple(W_p.shape) == (K, N)
+    return forward(x, W_p, W_f, lut, bias)
+
+
+# Legacy alias (reference packr/__init__.py:33)
+phr_matmul = packr_matmul

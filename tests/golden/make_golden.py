@@ -83,8 +83,7 @@ def run_reference(case: dict, three_d: bool = False) -> dict:
     return res
 
 
-SMALL = {
-    # name: (M, K, N, x dtype, bias, 3-D input)
+SMALL = {  # name: (M, K, N, x dtype, bias, 3-D input)
     "f32_ragged": (33, 96, 160, torch.float32, True, False),
     "bf16_tiles": (64, 128, 256, torch.bfloat16, True, False),
     "bf16_m1": (1, 64, 48, torch.bfloat16, False, False),
@@ -122,6 +121,18 @@ def main() -> None:
     out["cfg0/in_checksum"] = np.array([case["x"].double().sum().item(), case["W_p"].double().sum().item(),
                                         case["lut"].double().sum().item(), case["W_f"].double().sum().item(),
                                         case["dY"].double().sum().item()])
+    # from_linear: the reference's compression of seeded nn.Linear layers
+    for name, (i, o, b) in {"fl_small": (64, 48, True), "fl_wide": (96, 320, False)}.items():
+        torch.manual_seed(21 + i)
+        lin = torch.nn.Linear(i, o, bias=b)
+        pl = packr.PackRLinear.from_linear(lin)
+        out[f"{name}/weight"] = lin.weight.detach().numpy().copy()
+        if b:
+            out[f"{name}/bias"] = lin.bias.detach().numpy().copy()
+            out[f"{name}/bias_f"] = bits(pl.bias_f)
+        out[f"{name}/W_p"] = bits(pl.W_p)
+        out[f"{name}/lut"] = bits(pl.lut)
+        out[f"{name}/W_f"] = bits(pl.W_f)
     dst = Path(__file__).resolve().parent / "packr_linear_golden.npz"
     np.savez_compressed(dst, **out)
     print(dst, dst.stat().st_size)

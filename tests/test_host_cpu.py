@@ -1,0 +1,118 @@
+"""Host-side logic that needs no GPU: model surgery, from_linear against the
+reference's own compression (golden), config, API surface and the loud
+failure of the GPU-only ops on CPU tensors."""
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import packr_b200 as packr
+from packr_b200 import PackRConfig, PackRLinear, compress_model
+from packr_b200.layer import _build_codebook, _quantile_abs
+
+GOLD = np.load(Path(__file__).resolve().parent / "golden" / "packr_linear_golden.npz")
+
+
+def bits(t):
+    t = t.detach().contiguous()
+    if t.dtype == torch.bfloat16:
+        return t.view(torch.int16).numpy().view(np.uint16)
+    return t.numpy()
+
+
+@pytest.mark.parametrize("name", ["fl_small", "fl_wide"])
+def test_from_linear_matches_reference(name):
+    w = torch.from_numpy(GOLD[f"{name}/weight"].copy())
+    has_b = f"{name}/bias" in GOLD.files
+    lin = torch.nn.Linear(w.shape[1], w.shape[0], bias=has_b)
+    with torch.no_grad():
+        lin.weight.copy_(w)
+        if has_b:
+            lin.bias.copy_(torch.from_numpy(GOLD[f"{name}/bias"].copy()))
+    pl = PackRLinear.from_linear(lin)
+    assert np.array_equal(bits(pl.W_p), GOLD[f"{name}/W_p"])
+    assert np.array_equal(bits(pl.lut), GOLD[f"{name}/lut"])
+    assert np.array_equal(bits(pl.W_f), GOLD[f"{name}/W_f"])
+    if has_b:
+        assert np.array_equal(bits(pl.bias_f), GOLD[f"{name}/bias_f"])
+    assert not pl.W_p.requires_grad and pl.W_f.dtype == torch.bfloat16 and pl.lut.dtype == torch.float32
+
+
+def test_codebook_definition():
+    cb = _build_codebook()
+    for i in (0, 15, 16, 255, 0x5A):
+        g, s = i & 15, (i >> 4) & 15
+        assert cb[i].item() == np.float32(((g - 7.5) / 7.5) * ((s + 1.0) / 10.0))
+
+
+def test_quantile_above_torch_limit_matches_order_statistics():
+    g = torch.Generator().manual_seed(0)
+    w = torch.randn((1 << 24) + 5, generator=g)
+    q = _quantile_abs(w, 0.99).item()
+    a = np.sort(np.abs(w.numpy()).astype(np.float64))
+    pos = 0.99 * (a.size - 1)
+    lo = int(np.floor(pos))
+    want = a[lo] + (a[lo + 1] - a[lo]) * (pos - lo)
+    assert abs(q - want) <= 1e-6 * want
+
+
+def test_compress_model_scopes():
+    class Block(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.attention = torch.nn.Module()
+            self.attention.query = torch.nn.Linear(16, 16)
+            self.attention.output = torch.nn.Module()
+            self.attention.output.dense = torch.nn.Linear(16, 16)
+            self.intermediate = torch.nn.Module()
+            self.intermediate.dense = torch.nn.Linear(16, 64)
+            self.output = torch.nn.Module()
+            self.output.dense = torch.nn.Linear(64, 16)
+    m = compress_model(Block(), PackRConfig(layer_scope="ffn", gradient_checkpointing=False))
+    assert isinstance(m.intermediate.dense, PackRLinear) and isinstance(m.output.dense, PackRLinear)
+    assert isinstance(m.attention.query, torch.nn.Linear)
+    assert isinstance(m.attention.output.dense, torch.nn.Linear)  # attention output is not FFN
+    m = compress_model(Block(), PackRConfig(layer_scope="attention", gradient_checkpointing=False))
+    assert isinstance(m.attention.query, PackRLinear) and isinstance(m.intermediate.dense, torch.nn.Linear)
+    m = compress_model(torch.nn.Sequential(torch.nn.Linear(8, 4)), PackRConfig(layer_scope="all", learnable_lut=False))
+    assert isinstance(m[0], PackRLinear) and not m[0].lut.requires_grad
+
+
+def test_api_surface_matches_reference():
+    for name in ["PackRConfig", "PackRLinear", "PackRMatmulFunction", "packr_matmul", "compress_model", "SchemeType",
+                 "FusedQuantizedAdam", "PHRConfig", "PHRLinear", "PHRMatmulFunction", "phr_matmul"]:
+        assert hasattr(packr, name), name
+    from packr_b200.cuda_adam import CUDA8BitAdam  # noqa: F401
+    cfg = PackRConfig()
+    assert (cfg.mode, cfg.layer_scope, cfg.block_size, cfg.optimizer_type) == ("packr", "ffn", 256, "triton8")
+
+
+def test_compress_model_source_has_no_zstandard():
+    import inspect
+    from packr_b200.layer_patcher import compress_model as cm
+    assert "zstandard" not in inspect.getsource(cm)
+
+
+def test_gpu_ops_refuse_cpu_tensors():
+    """No CPU fallback: the product path fails loudly on CPU tensors."""
+    x = torch.randn(4, 64)
+    W_p = torch.randint(0, 256, (64, 32), dtype=torch.uint8)
+    W_f = torch.randn(64, 32, dtype=torch.bfloat16)
+    lut = torch.randn(256)
+    with pytest.raises(AssertionError):
+        packr.packr_matmul(x, W_p, W_f, lut)
+    layer = PackRLinear(64, 32)
+    with pytest.raises(RuntimeError):
+        layer(x)
+    p = torch.nn.Parameter(torch.randn(10))
+    p.grad = torch.randn(10)
+    with pytest.raises(RuntimeError):
+        packr.CUDA8BitAdam([p]).step()
+
+
+def test_fused_quantized_adam_block_size():
+    p = torch.nn.Parameter(torch.randn(10))
+    with pytest.raises(ValueError):
+        packr.FusedQuantizedAdam([p], block_size=128)
+    packr.FusedQuantizedAdam([p], block_size=256, flat_buffer=True)

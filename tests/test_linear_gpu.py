@@ -1,0 +1,191 @@
+"""PackRLinear on the GPU against the CPU oracle (and, at Llama-FFN sizes the
+oracle cannot finish quickly, a torch fp32 GPU reference of the same math).
+
+Bars (north_star): decoded weights bit-exact with bf16(W_f + bf16(lut[W_p]));
+out / dX / dW_f / dbias within 1e-2 max-relative, dlut within 1e-3, where
+max-relative = max|a-b| / max|b| as in the reference tests."""
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from packr_b200 import kernel as K
+from packr_b200.synthetic import linear_case
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-2       # out, dX, dW_f, dbias
+TOL_LUT = 1e-3   # dlut
+GOLD = np.load(Path(__file__).resolve().parent / "golden" / "packr_linear_golden.npz")
+
+
+def bits(t):
+    t = t.detach().cpu().contiguous()
+    if t.dtype == torch.bfloat16:
+        return t.view(torch.int16).numpy().view(np.uint16).copy()
+    return t.numpy().copy()
+
+
+def f32(a):
+    return oracle.bf16_to_f32(a) if a.dtype == np.uint16 else a.astype(np.float32)
+
+
+def to_cuda(c):
+    return {k: (v.cuda() if v is not None else None) for k, v in c.items()}
+
+
+def run_ours(c, need=(True, True, True, True)):
+    out = K.forward(c["x"], c["W_p"], c["W_f"], c["lut"], c["bias"])
+    counts = K.bincount256(c["W_p"])
+    dX, dW, dlut, dbias = K.backward(c["dY"], c["x"], c["W_p"], c["W_f"], c["lut"], counts, need[0], need[1],
+                                     need[2], need[3] and c["bias"] is not None)
+    torch.cuda.synchronize()
+    return out, dX, dW, dlut, dbias
+
+
+def check_against_oracle(c_cpu, label=""):
+    c = to_cuda(c_cpu)
+    isbf = c_cpu["x"].dtype == torch.bfloat16
+    n = {k: bits(v) for k, v in c_cpu.items() if v is not None}
+    ref_out = oracle.linear_forward(n["x"], n["W_p"], n["W_f"], n["lut"], n.get("bias"), x_is_bf16=isbf)
+    ref = oracle.linear_backward(n["dY"], n["x"], n["W_p"], n["W_f"], n["lut"], has_bias="bias" in n,
+                                 x_is_bf16=isbf)
+    out, dX, dW, dlut, dbias = run_ours(c)
+    errs = {"out": oracle.max_rel(bits(out), ref_out),
+            "dX": oracle.max_rel(f32(bits(dX)), f32(ref["dX"])),
+            "dW_f": oracle.max_rel(f32(bits(dW)), f32(ref["dW_f"])),
+            "dlut": oracle.max_rel(bits(dlut), ref["dlut"])}
+    if "bias" in n:
+        errs["dbias"] = oracle.max_rel(f32(bits(dbias)), f32(ref["dbias"]))
+    print(label, {k: f"{v:.2e}" for k, v in errs.items()})
+    assert out.dtype == torch.float32 and tuple(out.shape) == ref_out.shape
+    assert dX.dtype == c["x"].dtype and dW.dtype == torch.bfloat16
+    for k, v in errs.items():
+        assert v <= (TOL_LUT if k == "dlut" else TOL), (label, k, v)
+    return errs
+
+
+@pytest.mark.parametrize("shape", [(64, 256), (100, 300), (768, 3072), (3072, 768), (8, 8), (1, 5)])
+def test_decode_bit_exact(cuda, shape):
+    Kd, Nd = shape
+    c = linear_case(1, Kd, Nd, seed=11)
+    W_p, W_f, lut = c["W_p"].cuda(), c["W_f"].cuda(), c["lut"].cuda()
+    got = bits(K.decode_bf16(W_p, W_f, lut))
+    want = oracle.decode_bf16(bits(c["W_p"]), bits(c["W_f"]), bits(c["lut"]))
+    assert np.array_equal(got, want)
+    # and against torch's own bf16 arithmetic, as the reference writes it (autograd.py:66-67)
+    torch_ref = bits(W_f + lut[W_p.long()].to(torch.bfloat16))
+    assert np.array_equal(got, torch_ref)
+
+
+def test_decode_bit_exact_extreme_lut(cuda):
+    """lut entries that round to bf16 ties, subnormals, +-0, large values."""
+    c = linear_case(1, 64, 512, seed=12)
+    lut = torch.tensor([0.0, -0.0, 1e-40, -1e-40, 3.0e38, -3.0e38, 1.0 + 2 ** -8, 1.0 + 3 * 2 ** -8] +
+                       list(np.linspace(-1, 1, 248)), dtype=torch.float32)
+    W_f = (torch.randn(64, 512) * 10.0).to(torch.bfloat16)
+    got = bits(K.decode_bf16(c["W_p"].cuda(), W_f.cuda(), lut.cuda()))
+    want = oracle.decode_bf16(bits(c["W_p"]), bits(W_f), bits(lut))
+    assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("n", [0, 1, 15, 16, 1000, 768 * 3072 + 3])
+def test_bincount(cuda, n):
+    g = torch.Generator().manual_seed(n)
+    w = torch.randint(0, 256, (n,), generator=g, dtype=torch.uint8)
+    got = K.bincount256(w.cuda()).cpu().numpy()
+    assert np.array_equal(got, np.bincount(w.numpy(), minlength=256))
+
+
+@pytest.mark.parametrize("name", sorted({k.split("/")[0] for k in GOLD.files} - {"cfg0"}))
+def test_golden_cases(cuda, name):
+    M, Kd, Nd, isbf, hasb, _, _ = (int(v) for v in GOLD[f"{name}/meta"])
+    g = lambda k: GOLD[f"{name}/in_{k}"]
+    t = lambda a: torch.from_numpy(a.view(np.int16)).view(torch.bfloat16) if a.dtype == np.uint16 else torch.from_numpy(a.copy())
+    c = {"x": t(g("x")), "W_p": t(g("W_p")), "lut": t(g("lut")), "W_f": t(g("W_f")),
+         "bias": t(g("bias")) if hasb else None, "dY": t(g("dY"))}
+    c["x"] = c["x"].reshape(M, Kd)
+    c["dY"] = c["dY"].reshape(M, Nd)
+    out, dX, dW, dlut, dbias = run_ours(to_cuda(c))
+    # against the reference's own outputs
+    assert oracle.max_rel(bits(out), GOLD[f"{name}/ref_out"].reshape(M, Nd)) <= TOL
+    assert oracle.max_rel(f32(bits(dX)), f32(GOLD[f"{name}/ref_dX"]).reshape(M, Kd)) <= TOL
+    assert oracle.max_rel(f32(bits(dW)), f32(GOLD[f"{name}/ref_dW_f"])) <= TOL
+    assert oracle.max_rel(bits(dlut), GOLD[f"{name}/ref_dlut"]) <= TOL_LUT
+    if hasb:
+        assert oracle.max_rel(f32(bits(dbias)), f32(GOLD[f"{name}/ref_dbias"])) <= TOL
+
+
+CASES = [
+    # (M, K, N, x dtype, bias)
+    (1024, 768, 3072, torch.float32, True),     # the 768->3072 parity configuration
+    (33, 96, 160, torch.float32, True),        # ragged: partial M, K, N tiles
+    (1, 64, 48, torch.bfloat16, False),        # single token
+    (257, 200, 264, torch.bfloat16, True),     # K, N not multiples of 64 / 256
+    (130, 100, 36, torch.float32, False),      # K % 8 != 0 (padded activation copy)
+    (512, 1024, 512, torch.bfloat16, True),
+    (16, 4096, 11008, torch.bfloat16, True),   # Llama-7B gate/up, decode-bound M
+    (16, 11008, 4096, torch.bfloat16, True),   # Llama-7B down
+]
+
+
+@pytest.mark.parametrize("M,Kd,Nd,dt,bias", CASES)
+def test_against_oracle(cuda, M, Kd, Nd, dt, bias):
+    c = linear_case(M, Kd, Nd, x_dtype=dt, bias=bias, seed=M + Kd, fanin_scaled=Kd > 768)
+    check_against_oracle(c, f"{M}x{Kd}x{Nd} {dt}")
+
+
+def test_768x3072_matches_reference_golden(cuda):
+    """The 768->3072 fp32 case against the REFERENCE's outputs (sampled)."""
+    M, Kd, Nd = (int(v) for v in GOLD["cfg0/meta"][:3])
+    c = to_cuda(linear_case(M, Kd, Nd, x_dtype=torch.float32, bias=True, seed=0))
+    out, dX, dW, dlut, dbias = run_ours(c)
+    assert oracle.max_rel(bits(dlut), GOLD["cfg0/dlut"]) <= TOL_LUT
+    assert oracle.max_rel(f32(bits(dbias)), f32(GOLD["cfg0/dbias"])) <= TOL
+    for k, arr in (("out", out), ("dX", dX), ("dW_f", dW)):
+        flat = f32(bits(arr)).reshape(-1)
+        ref = f32(GOLD[f"cfg0/{k}_val"])
+        assert np.abs(flat[GOLD[f"cfg0/{k}_idx"]] - ref).max() <= TOL * np.abs(ref).max(), k
+
+
+def torch_reference(c):
+    """fp32 torch reference on the GPU (TF32 off) of the same math."""
+    torch.backends.cuda.matmul.allow_tf32 = False
+    x = c["x"].float()
+    Wfull = c["W_f"].float() + c["lut"][c["W_p"].long()].half().float()
+    out = x @ Wfull
+    if c["bias"] is not None:
+        out = out + c["bias"].float()
+    Wb = (c["W_f"] + c["lut"][c["W_p"].long()].to(torch.bfloat16)).float()
+    dX = (c["dY"].to(torch.bfloat16).float() @ Wb.T).to(torch.bfloat16)
+    dW = x.T @ c["dY"]
+    cnt = torch.bincount(c["W_p"].reshape(-1).long(), minlength=256).float()
+    s = torch.zeros(256, device=x.device).scatter_add_(0, c["W_p"].reshape(-1).long(), dW.reshape(-1))
+    return out, dX, dW, s / (cnt + 1e-8)
+
+
+@pytest.mark.parametrize("M,Kd,Nd", [(4096, 4096, 11008), (4096, 11008, 4096)])
+def test_llama_ffn_full_size(cuda, M, Kd, Nd):
+    c = to_cuda(linear_case(M, Kd, Nd, x_dtype=torch.bfloat16, bias=False, seed=1, device="cpu", fanin_scaled=True))
+    out, dX, dW, dlut, _ = run_ours(c)
+    r_out, r_dX, r_dW, r_dlut = torch_reference(c)
+    mr = lambda a, b: ((a.float() - b.float()).abs().max() / b.float().abs().max()).item()
+    errs = {"out": mr(out, r_out), "dX": mr(dX, r_dX), "dW_f": mr(dW, r_dW), "dlut": mr(dlut, r_dlut)}
+    print(errs)
+    assert errs["out"] <= TOL and errs["dX"] <= TOL and errs["dW_f"] <= TOL and errs["dlut"] <= TOL_LUT
+    # size-independent property: the bf16 dW_f is the rounding of an fp32 sum
+    # whose bin sums reproduce dlut * (count + 1e-8)
+    cnt = torch.bincount(c["W_p"].reshape(-1).long(), minlength=256).float()
+    assert torch.allclose(dlut * (cnt + 1e-8), r_dlut * (cnt + 1e-8), rtol=0, atol=TOL_LUT * (r_dlut * cnt).abs().max().item())
+
+
+def test_empty_batch(cuda):
+    c = to_cuda(linear_case(1, 64, 32, seed=3))
+    x = c["x"][:0]
+    out = K.forward(x, c["W_p"], c["W_f"], c["lut"], c["bias"])
+    assert out.shape == (0, 32)
+    dX, dW, dlut, dbias = K.backward(c["dY"][:0], x, c["W_p"], c["W_f"], c["lut"], None, True, True, True, True)
+    torch.cuda.synchronize()
+    assert dX.shape == (0, 64) and (dW.float() == 0).all() and (dlut == 0).all() and (dbias.float() == 0).all()
