@@ -7,6 +7,12 @@ per GPU (NCCL); every rank runs the same per-GPU workload (weak scaling) and
 the step time is the max over ranks of CUDA-event time.
 
 Workloads (synthetic, seeded; no dataset exists for this path):
+  ffn    (default) PackRLinear forward+backward of the Llama-7B FFN shapes:
+         gate 4096->11008, up 4096->11008, down 11008->4096, M = 4096 tokens
+         of bf16 activations per GPU, f32 upstream gradients holding
+         bf16-exact values; one step = the three layers' forward and backward
+         through autograd (out, dX, dW_f, dlut); metric TFLOP/s over
+         6*M*K*N per layer.  Per step the operands (~0.9 GB) exceed L2.
   adam8  CUDA8BitAdam step over one flat 110,000,000-element bf16 parameter
          (lr 2e-5, betas (0.9, 0.999), eps 1e-8, wd 0.01, block 256); metric
          Gparam/s.  Per step the inputs (1.1 GB) exceed L2 (126 MB).
@@ -270,6 +276,162 @@ def bench_adam8(args, world, rank, peaks, peak_kind):
     return line
 
 
+# ---------------------------------------------------------------- ffn workload
+FFN_HIDDEN, FFN_INTER, FFN_M = 4096, 11008, 4096
+FFN_LAYERS = (("gate", FFN_HIDDEN, FFN_INTER), ("up", FFN_HIDDEN, FFN_INTER), ("down", FFN_INTER, FFN_HIDDEN))
+
+
+def ffn_flops(M: int) -> float:
+    return float(sum(6 * M * k * n for _, k, n in FFN_LAYERS))
+
+
+def load_traffic(kernel: str, workload: str):
+    """dram bytes per launch of `kernel` from the committed ncu summary, or None."""
+    f = REPO / "profiles" / "traffic.json"
+    if not f.exists():
+        return None
+    try:
+        return json.loads(f.read_text()).get(workload, {}).get(kernel)
+    except Exception:
+        return None
+
+
+def cpu_linear_port(budget_s: float, M: int = 1024):
+    """Times the reference PackRLinear forward + backward arithmetic on the
+    host (oracle/reference_port.py: torch CPU, the reference's own op sequence
+    of packr/kernel.py:127-139 and packr/autograd.py:65-83, all host threads)
+    on one gate-shaped layer (4096 -> 11008) at M tokens per sample."""
+    from oracle import reference_port as rp
+    from packr_b200.synthetic import linear_case
+    K, N = FFN_HIDDEN, FFN_INTER
+    c = linear_case(M, K, N, x_dtype=torch.bfloat16, bias=False, seed=0, fanin_scaled=True)
+
+    def run():
+        rp.forward(c["x"], c["W_p"], c["W_f"], c["lut"])
+        rp.backward(c["dY"], c["x"], c["W_p"], c["W_f"], c["lut"])
+    run()
+    times = []
+    t0 = time.perf_counter()
+    while len(times) < 2 or time.perf_counter() - t0 < budget_s:
+        a = time.perf_counter()
+        run()
+        times.append(time.perf_counter() - a)
+    sec = statistics.median(times)
+    return {"value": 6.0 * M * K * N / sec / 1e12, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+            "kind": "port", "sample": f"one 4096->11008 layer, M={M}, fwd+bwd, {len(times)} timed samples (median); "
+                                      "torch-CPU restatement of the reference path (oracle/reference_port.py)",
+            "host_cores": os.cpu_count()}
+
+
+def bench_ffn(args, world, rank, peaks, peak_kind):
+    from packr_b200 import PackRLinear
+    from packr_b200 import kernel as K
+    M = args.tokens
+    dev = torch.device("cuda", torch.cuda.current_device())
+    layers, xs, dys = [], [], []
+    for i, (name, k, n) in enumerate(FFN_LAYERS):
+        lay = PackRLinear.synthetic(k, n, bias=False, device=dev, seed=100 + i, lut_std=0.02 * math.sqrt(768 / k),
+                                    wf_std=0.002 * math.sqrt(768 / k))
+        g = torch.Generator(device=dev).manual_seed(1000 * rank + i)
+        xs.append(torch.randn(M, k, generator=g, device=dev).to(torch.bfloat16).requires_grad_(True))
+        dys.append(torch.randn(M, n, generator=g, device=dev).to(torch.bfloat16).float())
+        layers.append(lay)
+
+    def step():
+        for lay, x, dy in zip(layers, xs, dys):
+            out = lay(x)
+            out.backward(dy)
+
+    def zero():
+        for lay, x in zip(layers, xs):
+            lay.W_f.grad = None
+            lay.lut.grad = None
+            x.grad = None
+
+    def step_z():
+        zero()
+        step()
+
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        total_ms, per = timed(step_z, args.steps, args.warmup, world, warm_seconds=1.5)
+    ms_step = total_ms / args.steps
+    flops = ffn_flops(M)
+    value = world * flops / (ms_step * 1e-3) / 1e12
+    # dominant kernel: the forward GEMM of the gate layer, timed alone
+    lay, x = layers[0], xs[0].detach()
+    fwd = lambda: K.forward(x, lay.W_p, lay.W_f, lay.lut, None)
+    f_total, f_per = timed(fwd, max(args.steps, 10), 3, 1)
+    f_ms = statistics.mean(f_per)
+    f_flops = 2.0 * M * FFN_HIDDEN * FFN_INTER
+    achieved = f_flops / (f_ms * 1e-3) / 1e12
+    # phase split of one layer (gate): forward vs backward launches
+    out0 = K.forward(x, lay.W_p, lay.W_f, lay.lut, None)
+    cnt = lay.lut_counts()
+    bwd = lambda: K.backward(dys[0], x, lay.W_p, lay.W_f, lay.lut, cnt, True, True, True, False)
+    b_total, b_per = timed(bwd, max(args.steps, 10), 3, 1)
+    del out0
+    # end to end: inputs from pinned host memory, dlut read back each step
+    hx = [t.detach().cpu().pin_memory() for t in xs]
+    hdy = [t.cpu().pin_memory() for t in dys]
+    hres = torch.empty(len(layers), 256, dtype=torch.float32, pin_memory=True)
+    dx_in = [torch.empty_like(t) for t in xs]
+    ddy_in = [torch.empty_like(t) for t in dys]
+
+    def e2e_step():
+        zero()
+        for i, (lay, hxi, hdyi) in enumerate(zip(layers, hx, hdy)):
+            dx_in[i].copy_(hxi, non_blocking=True)
+            ddy_in[i].copy_(hdyi, non_blocking=True)
+            xi = dx_in[i].detach().requires_grad_(True)
+            lay(xi).backward(ddy_in[i])
+            hres[i].copy_(lay.lut.grad, non_blocking=True)
+    e2e_total, _ = timed(e2e_step, args.steps, max(args.warmup, 1), world)
+    e2e_val = world * flops / (e2e_total / args.steps * 1e-3) / 1e12
+    h2d = sum(t.numel() * t.element_size() for t in hx) + sum(t.numel() * t.element_size() for t in hdy)
+    line = {
+        "metric": "PackRLinear fwd+bwd TFLOP/s (Llama FFN shapes)", "value": round(value, 2), "unit": "TFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 operands, f32 accumulate",
+        "data": "synthetic (seeded; bf16 x ~ N(0,1), bf16-valued f32 dY ~ N(0,1), uniform W_p, fan-in scaled lut/W_f)",
+        "config": {"workload": f"ffn: Llama-7B FFN gate/up/down (4096<->11008) PackRLinear fwd+bwd, M={M} tokens per GPU",
+                   "hidden": FFN_HIDDEN, "intermediate": FFN_INTER, "tokens_per_gpu": M,
+                   "flops_per_step_per_gpu": flops, "l2": "inputs larger than L2 (~0.9 GB of operands per step)",
+                   "parallelism": "data-parallel replicas" if world > 1 else "single GPU"},
+        "phases_ms_gate_layer": {"forward": round(f_ms, 4), "backward": round(statistics.mean(b_per), 4)},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peaks["bf16_tflops"],
+                     "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
+                     "traffic": load_traffic("packr_gemm_kernel<FWD>", "ffn_gate_M%d" % M),
+                     "peak_source": f"{peak_kind} bf16_tflops (burst; kernel timed alone)",
+                     "kernel": "packr_gemm_kernel<FWD> (gate 4096->11008)",
+                     "algorithmic_flops_per_launch": f_flops},
+        "e2e": {"value": round(e2e_val, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": hres.numel() * 4},
+        "gpu_launches": args.steps * len(layers) * 5,
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_linear_port(args.cpu_seconds)
+    return line
+
+
+def profile_once(args):
+    """One forward and one backward of the gate layer (4096 -> 11008, M
+    tokens), then one CUDA8BitAdam step over its W_f: the launch sequence an
+    ncu capture of this workload sees (forward GEMM first)."""
+    from packr_b200 import PackRLinear
+    from packr_b200.cuda_adam import CUDA8BitAdam
+    dev = torch.device("cuda", torch.cuda.current_device())
+    M = args.tokens
+    lay = PackRLinear.synthetic(FFN_HIDDEN, FFN_INTER, bias=True, device=dev, seed=100)
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn(M, FFN_HIDDEN, generator=g, device=dev).to(torch.bfloat16).requires_grad_(True)
+    dy = torch.randn(M, FFN_INTER, generator=g, device=dev).to(torch.bfloat16).float()
+    lay.lut_counts()
+    lay(x).backward(dy)
+    CUDA8BitAdam([lay.W_f, lay.lut], lr=2e-5, weight_decay=0.01).step()
+    torch.cuda.synchronize()
+
+
 def reference_arm(args, world, rank):
     if rank != 0:
         return None
@@ -282,6 +444,16 @@ def reference_arm(args, world, rank):
                 "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
                 "e2e": {"value": round(cb["value"], 5), "unit": "Gparam/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
+    if args.workload == "ffn":
+        cb = cpu_linear_port(max(5.0, 0.5 * args.steps))
+        return {"impl": "reference", "metric": "PackRLinear fwd+bwd TFLOP/s (Llama FFN shapes)",
+                "value": round(cb["value"], 5), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "f32 (bf16-valued operands)", "data": "synthetic",
+                "config": {"workload": "ffn: Llama-7B FFN PackRLinear fwd+bwd (bounded CPU sample)"},
+                "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                "e2e": {"value": round(cb["value"], 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
     raise SystemExit(f"unknown workload {args.workload}")
 
 
@@ -290,10 +462,13 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="adam8", choices=["adam8"])
+    ap.add_argument("--workload", default="ffn", choices=["ffn", "adam8"])
+    ap.add_argument("--tokens", type=int, default=FFN_M, help="ffn: tokens per GPU")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-once", action="store_true",
+                    help="ffn: run each kernel of one gate-layer step once (for ncu captures), print nothing")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -305,7 +480,10 @@ def main():
         return
     world, rank, local = dist_setup()
     peaks, peak_kind = load_peaks()
-    line = bench_adam8(args, world, rank, peaks, peak_kind)
+    if args.profile_once:
+        profile_once(args)
+        return
+    line = (bench_ffn if args.workload == "ffn" else bench_adam8)(args, world, rank, peaks, peak_kind)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

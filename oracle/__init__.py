@@ -107,8 +107,10 @@ def linear_backward(dY, x, W_p, W_f, lut, has_bias=False, x_is_bf16=False):
     dX = dX16 if x_is_bf16 else bf16_to_f32(dX16)
     dW = np.matmul(xf.T, dY, dtype=np.float32)
     counts = bincount256(W_p).astype(np.float32)
-    sums = np.zeros(256, dtype=np.float32)
-    np.add.at(sums, W_p.reshape(-1).astype(np.int64), dW.reshape(-1))
+    # scatter_add of fp32 dW by W_p; bins summed in float64 then rounded (the
+    # reference's fp32 atomics have no fixed order; this is their exact value
+    # to within one rounding)
+    sums = np.bincount(W_p.reshape(-1), weights=dW.reshape(-1).astype(np.float64), minlength=256).astype(np.float32)
     dlut = (sums / (counts + np.float32(1e-8))).astype(np.float32)
     res = {"dX": dX, "dW_f": f32_to_bf16(dW), "dW": dW, "dlut": dlut}
     if has_bias:

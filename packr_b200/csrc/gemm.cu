@@ -16,14 +16,22 @@
 // bf16 operand into the 128-byte-swizzled shared-memory tile the tensor core
 // reads.  Activations (x, dY) arrive by TMA.
 //
-// Roles (one CTA per SM, persistent over output tiles of 128 x 256):
-//   warp 0      TMA producer (activation tiles; both operands for DW)
-//   warp 1      TMEM owner + single-thread tcgen05.mma issuer
+// Tiles and roles.  A cluster of two CTAs (one per SM) computes a 256 x 256
+// output tile with tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 16 per
+// instruction): each CTA holds 128 rows of A and 128 columns of B in its own
+// shared memory, and each CTA's TMEM holds its 128 output rows x 256 columns.
+// Per CTA:
+//   warp 0      TMA producer (activation tiles; both operands for DW); its
+//               loads complete on the even CTA's mbarrier (.cta_group::2, no
+//               multicast)
+//   warp 1      TMEM owner; in the even CTA also the single-thread MMA issuer
 //   warps 2-5   epilogue: tcgen05.ld of the f32 accumulator, bias / rounding /
 //               lut-gradient histogram, global stores
-//   warps 6-13  weight decode (FWD, DX only)
-// Shared memory: 4 stages x (A 16 KB + B 32 KB) + 32 KB lut copy (decode
-// modes) or 4 KB of per-warp lut-gradient histograms (DW).  TMEM: two
+//   warps 6-13  weight decode (FWD, DX only): a 3-deep register ring of W_f/W_p
+//               loads, lut lookup, bf16 add, swizzled store of this CTA's half
+//               of the B tile
+// Shared memory per CTA: 6 stages x (A 16 KB + B 16 KB) + 32 KB lut copy
+// (decode modes) or 4 KB of per-warp lut-gradient histograms (DW).  TMEM: two
 // 128 x 256 f32 accumulators (512 columns) so the epilogue of tile i overlaps
 // the mainloop of tile i+1.  Every mbarrier wait is bounded (2 s); a wait that
 // gives up sets the CTA abort word and the device timeout word, every role
@@ -39,17 +47,22 @@ namespace gemm {
 
 using namespace sm100;
 
-constexpr int BM = 128, BN = 256, BK = 64, UK = 16;
-constexpr int STAGES = 4;
-constexpr int A_BYTES = BM * BK * 2;  // 16 KB
-constexpr int B_BYTES = BN * BK * 2;  // 32 KB
+constexpr int BM = 128;          // A rows per CTA (MMA M = 256 per pair)
+constexpr int BN = 256;          // MMA N (output columns per tile)
+constexpr int BN_CTA = 128;      // B columns held by each CTA
+constexpr int BK = 64, UK = 16;
+constexpr int STAGES = 6;
+constexpr int A_BYTES = BM * BK * 2;      // 16 KB
+constexpr int B_BYTES = BN_CTA * BK * 2;  // 16 KB
 constexpr int EPI_WARPS = 4;
 constexpr int DEC_WARPS = 8;
 constexpr int DEC_THREADS = DEC_WARPS * 32;
+constexpr int CHUNKS = BN_CTA * BK / 8 / DEC_THREADS;  // 4 chunks of 8 weights per thread per stage
 constexpr int LUT_BYTES = 256 * 32 * 4;  // one u32 per (entry, lane)
 constexpr int HIST_BYTES = EPI_WARPS * 256 * 4;
 constexpr int ACC_COLS = BN;
 constexpr int TMEM_COLS = 2 * ACC_COLS;
+constexpr uint16_t PAIR_MASK = 0x3;
 
 enum Mode { FWD = 0, DX = 1, DW = 2 };
 
@@ -63,7 +76,8 @@ struct Cfg {
   static constexpr int kAuxBytes = kDecode ? LUT_BYTES : HIST_BYTES;
   static constexpr int kBarOff = STAGES * (A_BYTES + B_BYTES) + kAuxBytes;
   static constexpr int kSmemBytes = kBarOff + 256 + 1024;  // barriers + alignment slack
-  static constexpr uint32_t kIdesc = idesc_bf16_f32(BM, BN, kAmn, kBmn);
+  static constexpr uint32_t kIdesc = idesc_bf16_f32(2 * BM, BN, kAmn, kBmn);
+  static constexpr uint32_t kTxBytes = 2 * (kDecode ? A_BYTES : A_BYTES + B_BYTES);  // both CTAs
 };
 
 struct Params {
@@ -95,13 +109,16 @@ struct Maps {
   CUtensorMap b[3];
 };
 
+// Barriers live at the same offset in both CTAs of a pair.  full / bfull /
+// tempty are used in the even CTA only (the odd CTA's producers arrive there
+// remotely); empty / tfull / drain receive the even CTA's multicast commits.
 struct Bars {
-  uint64_t full[STAGES];    // TMA bytes landed
-  uint64_t bfull[STAGES];   // decoded B written (decode modes)
-  uint64_t empty[STAGES];   // MMA done reading the stage
-  uint64_t tfull[2];        // accumulator complete
-  uint64_t tempty[2];       // accumulator drained by the epilogue
-  uint64_t drain;           // final commit before TMEM release
+  uint64_t full[STAGES];    // TMA bytes of both CTAs landed        (count 1 + tx)
+  uint64_t bfull[STAGES];   // decoded B written by both CTAs       (count 2*DEC_WARPS)
+  uint64_t empty[STAGES];   // MMAs done reading the stage          (count 1)
+  uint64_t tfull[2];        // accumulator complete                 (count 1)
+  uint64_t tempty[2];       // accumulator drained by both CTAs     (count 2*EPI_WARPS)
+  uint64_t drain;           // every MMA complete                   (count 1)
   uint32_t tmem_base;
   int abort;
 };
@@ -119,42 +136,52 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
 }
 
 // ------------------------------------------------------------------ decode
-// One decode thread moves 8 chunks of 8 consecutive weights per stage.
+// One decode thread moves CHUNKS chunks of 8 consecutive weights per stage.
 struct Chunks {
-  uint4 wf[8];
-  uint2 wp[8];
+  uint4 wf[CHUNKS];
+  uint2 wp[CHUNKS];
   uint32_t nvalid;  // 4 bits per chunk: number of valid weights (0..8)
 };
 
-// FWD: chunk i of thread t covers B rows k = t/32 + 8i (reduction), columns
-//      n = 8*(t%32) .. +7 of the 256-wide tile (W row = k, W cols = n).
-// DX : chunk i covers B row r = t/8 + 32i (output column = W row) and
-//      reduction columns 8*(t%8) .. +7 (W cols).
+// FWD: the CTA's B half is 64 reduction rows x 128 columns: chunk i of
+//      thread t covers row k = t/16 + 16i and columns 8*(t%16) .. +7
+//      (W row = k, W columns = n).
+// DX : the B half is 128 output columns (W rows) x 64 reduction columns:
+//      chunk i covers B row r = t/8 + 32i and reduction columns 8*(t%8) .. +7.
 template <int MODE>
 __device__ __forceinline__ void chunk_coords(int t, int i, int& brow, int& bcol8) {
   if (MODE == FWD) {
-    brow = (t >> 5) + 8 * i;
-    bcol8 = t & 31;
+    brow = (t >> 4) + 16 * i;
+    bcol8 = t & 15;
   } else {
     brow = (t >> 3) + 32 * i;
     bcol8 = t & 7;
   }
 }
 
+// Shared-memory byte offset of a chunk inside the CTA's B stage (128-byte
+// swizzle: 16-byte chunk index XOR row-within-8).
 template <int MODE>
-__device__ __forceinline__ void decode_load(Chunks& c, const Params& P, int t, int m_or_n0, int k0) {
+__device__ __forceinline__ uint32_t chunk_smem_off(int brow, int bcol8) {
+  if (MODE == FWD)  // MN-major: two 64-column blocks of 64 rows x 128 B
+    return (uint32_t)((bcol8 >> 3) * 8192 + brow * 128 + (((bcol8 & 7) ^ (brow & 7)) << 4));
+  return (uint32_t)(brow * 128 + ((bcol8 ^ (brow & 7)) << 4));  // K-major: one 128 B row per column
+}
+
+template <int MODE>
+__device__ __forceinline__ void decode_load(Chunks& c, const Params& P, int t, int nb0, int k0) {
   c.nvalid = 0;
   const bool vec_ok = P.w_vec != 0;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
+  for (int i = 0; i < CHUNKS; ++i) {
     int brow, bcol8;
     chunk_coords<MODE>(t, i, brow, bcol8);
     long long wr, wc;
     if (MODE == FWD) {
       wr = (long long)k0 + brow;
-      wc = (long long)m_or_n0 + 8 * bcol8;
+      wc = (long long)nb0 + 8 * bcol8;
     } else {
-      wr = (long long)m_or_n0 + brow;
+      wr = (long long)nb0 + brow;
       wc = (long long)k0 + 8 * bcol8;
     }
     int nv = 0;
@@ -187,14 +214,10 @@ __device__ __forceinline__ uint32_t lut_fetch(uint32_t lut_lane, uint32_t idx_by
 template <int MODE>
 __device__ __forceinline__ void decode_store(const Chunks& c, uint32_t b_stage, uint32_t lut_lane, int t) {
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
+  for (int i = 0; i < CHUNKS; ++i) {
     int brow, bcol8;
     chunk_coords<MODE>(t, i, brow, bcol8);
-    uint32_t off;
-    if (MODE == FWD)  // MN-major: 64-wide column blocks of 8 KB, one 128 B row per k
-      off = (uint32_t)((bcol8 >> 3) * 8192 + brow * 128 + (((bcol8 & 7) ^ (brow & 7)) << 4));
-    else  // K-major: one 128 B row per output column
-      off = (uint32_t)(brow * 128 + ((bcol8 ^ (brow & 7)) << 4));
+    const uint32_t off = chunk_smem_off<MODE>(brow, bcol8);
     const uint32_t w[2] = {c.wp[i].x, c.wp[i].y};
     const uint32_t f[4] = {c.wf[i].x, c.wf[i].y, c.wf[i].z, c.wf[i].w};
     uint32_t r[4];
@@ -234,18 +257,21 @@ __global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();  // 0: issues the MMAs, 1: its peer
+  const int pair = blockIdx.x >> 1;
+  const int npairs = gridDim.x >> 1;
   const int num_tiles = P.m_tiles * P.n_tiles;
   const int kb_total = P.nseg * P.k_blocks;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&bars->full[s], 1);
-      mbar_init(&bars->bfull[s], DEC_WARPS);
+      mbar_init(&bars->bfull[s], 2 * DEC_WARPS);
       mbar_init(&bars->empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&bars->tfull[a], 1);
-      mbar_init(&bars->tempty[a], EPI_WARPS);
+      mbar_init(&bars->tempty[a], 2 * EPI_WARPS);
     }
     mbar_init(&bars->drain, 1);
     bars->abort = 0;
@@ -262,8 +288,8 @@ __global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
     for (int i = threadIdx.x - 64; i < EPI_WARPS * 256; i += EPI_WARPS * 32) hist[i] = 0.0f;
   }
   if (warp == 1) {
-    tmem_alloc(&bars->tmem_base, TMEM_COLS);
-    tmem_relinquish();
+    tmem_alloc_pair(&bars->tmem_base, TMEM_COLS);
+    tmem_relinquish_pair();
   }
   if (C::kDecode && warp >= 2 + EPI_WARPS) {
     // Lane-replicated bf16 lut: word (e*32 + l) holds bf16_rne(lut[e]) for lane l.
@@ -272,94 +298,88 @@ __global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
     for (int e = dw; e < 256; e += DEC_WARPS) lut_s[e * 32 + lane] = f32_to_bf16_rne(__ldg(P.lut + e));
   }
   tc_fence_before();
-  __syncthreads();
+  __syncwarp();
+  cluster_sync();  // barriers of both CTAs initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = bars->tmem_base;
 
   if (warp == 0) {
-    // ------------------------------------------------ TMA producer
+    // ------------------------------------------------ TMA producer (both CTAs)
     if (lane == 0) {
       int it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        const int m0 = (tile % P.m_tiles) * BM;
-        const int n0 = (tile / P.m_tiles) * BN;
+      for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
+        const int m0 = (tile % P.m_tiles) * (2 * BM) + (int)rank * BM;
+        const int n0 = (tile / P.m_tiles) * BN + (int)rank * BN_CTA;
         for (int kk = 0; kk < kb_total; ++kk, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
           if (!mbar_wait(&bars->empty[s], ph ^ 1u, abort_flag)) { ok = false; break; }
           const int seg = kk / P.k_blocks;
           const int k0 = (kk % P.k_blocks) * BK;
+          if (rank == 0) mbar_arrive_expect_tx(&bars->full[s], C::kTxBytes);
+          const uint32_t fbar = mapa(smem_u32(&bars->full[s]), 0);
           uint8_t* a_dst = sA + s * A_BYTES;
           if (MODE == DW) {
-            mbar_arrive_expect_tx(&bars->full[s], A_BYTES + B_BYTES);
-            tma_load_2d(a_dst, &maps.a[seg], &bars->full[s], m0, k0);
-            tma_load_2d(a_dst + 8192, &maps.a[seg], &bars->full[s], m0 + 64, k0);
+            tma_load_2d_pair(a_dst, &maps.a[seg], fbar, m0, k0);
+            tma_load_2d_pair(a_dst + 8192, &maps.a[seg], fbar, m0 + 64, k0);
             uint8_t* b_dst = sB + s * B_BYTES;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) tma_load_2d(b_dst + j * 8192, &maps.b[seg], &bars->full[s], n0 + 64 * j, k0);
+            tma_load_2d_pair(b_dst, &maps.b[seg], fbar, n0, k0);
+            tma_load_2d_pair(b_dst + 8192, &maps.b[seg], fbar, n0 + 64, k0);
           } else {
-            mbar_arrive_expect_tx(&bars->full[s], A_BYTES);
-            tma_load_2d(a_dst, &maps.a[seg], &bars->full[s], k0, m0);
+            tma_load_2d_pair(a_dst, &maps.a[seg], fbar, k0, m0);
           }
         }
       }
-      // Drain: every load this thread issued must land before smem is released.
-      if (!ok) {
-        for (int j = (it > STAGES ? it - STAGES : 0); j < it; ++j) {
-          volatile int no_abort = 0;
-          mbar_wait(&bars->full[j % STAGES], (uint32_t)(j / STAGES) & 1u, &no_abort);
-        }
-      }
+      (void)ok;
     }
   } else if (warp == 1) {
-    // ------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // ------------------------------------------------ MMA issuer (even CTA)
+    if (lane == 0 && rank == 0) {
       int it = 0, t_local = 0;
       bool ok = true;
       const uint32_t sA0 = smem_u32(sA), sB0 = smem_u32(sB);
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++t_local) {
+      for (int tile = pair; tile < num_tiles && ok; tile += npairs, ++t_local) {
         const int acc = t_local & 1;
         const uint32_t aph = (uint32_t)(t_local >> 1) & 1u;
-        if (!mbar_wait(&bars->tempty[acc], aph ^ 1u, abort_flag)) { ok = false; break; }
+        if (!mbar_wait_cluster(&bars->tempty[acc], aph ^ 1u, abort_flag)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * ACC_COLS);
         for (int kk = 0; kk < kb_total; ++kk, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
           if (!mbar_wait(&bars->full[s], ph, abort_flag)) { ok = false; break; }
-          if (C::kDecode && !mbar_wait(&bars->bfull[s], ph, abort_flag)) { ok = false; break; }
+          if (C::kDecode && !mbar_wait_cluster(&bars->bfull[s], ph, abort_flag)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a_s = sA0 + s * A_BYTES, b_s = sB0 + s * B_BYTES;
 #pragma unroll
           for (int k = 0; k < BK / UK; ++k) {
             const uint64_t ad = C::kAmn ? sdesc_sw128(a_s + k * 2048, 8192, 1024) : sdesc_sw128(a_s + k * 32, 16, 1024);
             const uint64_t bd = C::kBmn ? sdesc_sw128(b_s + k * 2048, 8192, 1024) : sdesc_sw128(b_s + k * 32, 16, 1024);
-            umma_bf16_ss(d_tmem, ad, bd, C::kIdesc, (kk | k) != 0 ? 1u : 0u);
+            umma_bf16_pair(d_tmem, ad, bd, C::kIdesc, (kk | k) != 0 ? 1u : 0u);
           }
-          umma_commit(&bars->empty[s]);
+          umma_commit_pair(&bars->empty[s], PAIR_MASK);
         }
         if (!ok) break;
-        umma_commit(&bars->tfull[acc]);
+        umma_commit_pair(&bars->tfull[acc], PAIR_MASK);
       }
-      // Every MMA issued must complete before TMEM is released.
-      umma_commit(&bars->drain);
-      volatile int no_abort = 0;
-      mbar_wait(&bars->drain, 0, &no_abort);
+      umma_commit_pair(&bars->drain, PAIR_MASK);
     }
   } else if (warp < 2 + EPI_WARPS) {
-    // ------------------------------------------------ epilogue
+    // ------------------------------------------------ epilogue (both CTAs)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int row = q * 32 + lane;
     float* hist = reinterpret_cast<float*>(sAux) + (warp - 2) * 256;
+    const uint32_t tempty0 = mapa(smem_u32(&bars->tempty[0]), 0);
+    const uint32_t tempty1 = mapa(smem_u32(&bars->tempty[1]), 0);
     int t_local = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++t_local) {
+    for (int tile = pair; tile < num_tiles; tile += npairs, ++t_local) {
       const int acc = t_local & 1;
       const uint32_t aph = (uint32_t)(t_local >> 1) & 1u;
       // every lane waits; the warp proceeds only if all lanes saw the phase
       if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bars->tfull[acc], aph, abort_flag))) break;
       tc_fence_after();
-      const int m0 = (tile % P.m_tiles) * BM;
+      const int m0 = (tile % P.m_tiles) * (2 * BM) + (int)rank * BM;
       const int n0 = (tile / P.m_tiles) * BN;
       const long long gm = (long long)m0 + row;
       const bool row_ok = gm < P.Mg;
@@ -452,7 +472,7 @@ __global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->tempty[acc]);
+      if (lane == 0) mbar_arrive_cluster(acc ? tempty1 : tempty0);
     }
     if (MODE == DW && P.dlut_sum != nullptr) {
       asm volatile("bar.sync 1, %0;" ::"n"(EPI_WARPS * 32) : "memory");
@@ -466,19 +486,19 @@ __global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
       }
     }
   } else if (C::kDecode) {
-    // ------------------------------------------------ weight decode
+    // ------------------------------------------------ weight decode (both CTAs)
     const int t = threadIdx.x - (2 + EPI_WARPS) * 32;
     const uint32_t lut_lane = smem_u32(sAux) + (uint32_t)lane * 4u;
     const uint32_t sB0 = smem_u32(sB);
-    const int my_tiles = blockIdx.x < num_tiles ? (num_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    const int my_tiles = pair < num_tiles ? (num_tiles - 1 - pair) / npairs + 1 : 0;
     const int total = my_tiles * kb_total;
-    auto coords = [&](int it, int& mn0, int& k0) {
+    auto load = [&](Chunks& c, int it) {
       const int tl = it / kb_total;
       const int kk = it % kb_total;
-      const int tile = blockIdx.x + tl * gridDim.x;
-      // the decoded operand spans the output-column (n) tile of FWD / DX
-      mn0 = (tile / P.m_tiles) * BN;
-      k0 = (kk % P.k_blocks) * BK;
+      const int tile = pair + tl * npairs;
+      // this CTA's half of the decoded operand: 128 output columns of the tile
+      const int nb0 = (tile / P.m_tiles) * BN + (int)rank * BN_CTA;
+      decode_load<MODE>(c, P, t, nb0, (kk % P.k_blocks) * BK);
     };
     auto process = [&](const Chunks& c, int it) -> bool {
       const int s = it % STAGES;
@@ -487,35 +507,38 @@ __global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
       decode_store<MODE>(c, sB0 + s * B_BYTES, lut_lane, t);
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->bfull[s]);
+      if (lane == 0) mbar_arrive_cluster(mapa(smem_u32(&bars->bfull[s]), 0));
       return true;
     };
-    Chunks c0, c1;
-    int mn0, k0;
-    if (total > 0) {
-      coords(0, mn0, k0);
-      decode_load<MODE>(c0, P, t, mn0, k0);
-    }
-    for (int it = 0; it < total; it += 2) {
-      if (it + 1 < total) {
-        coords(it + 1, mn0, k0);
-        decode_load<MODE>(c1, P, t, mn0, k0);
-      }
-      if (!process(c0, it)) break;
+    // 3-deep ring: loads for items it+1 and it+2 are in flight while item it
+    // is decoded.
+    Chunks r0, r1, r2;
+    if (total > 0) load(r0, 0);
+    if (total > 1) load(r1, 1);
+    for (int it = 0; it < total; it += 3) {
+      if (it + 2 < total) load(r2, it + 2);
+      if (!process(r0, it)) break;
       if (it + 1 >= total) break;
-      if (it + 2 < total) {
-        coords(it + 2, mn0, k0);
-        decode_load<MODE>(c0, P, t, mn0, k0);
-      }
-      if (!process(c1, it + 1)) break;
+      if (it + 3 < total) load(r0, it + 3);
+      if (!process(r1, it + 1)) break;
+      if (it + 2 >= total) break;
+      if (it + 4 < total) load(r1, it + 4);
+      if (!process(r2, it + 2)) break;
     }
   }
 
+  // Every MMA issued must complete before TMEM is released (both CTAs wait
+  // for the even CTA's final multicast commit).
+  if (warp == 1 && lane == 0) {
+    volatile int no_abort = 0;
+    mbar_wait(&bars->drain, 0, &no_abort);
+  }
   tc_fence_before();
-  __syncthreads();
+  __syncwarp();
+  cluster_sync();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, TMEM_COLS);
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
   }
 }
 
@@ -566,13 +589,29 @@ int launch(Params P, const Maps& maps, cudaStream_t stream) {
   P.w_vec = (P.ldw & 7) == 0 && aligned(P.W_f, 16) && aligned(P.W_p, 8);
   P.out_vec = aligned(P.out, 16);
   P.idx_vec = aligned(P.hist_idx, 16);
-  P.m_tiles = (P.Mg + BM - 1) / BM;
+  P.m_tiles = (P.Mg + 2 * BM - 1) / (2 * BM);
   P.n_tiles = (P.Ng + BN - 1) / BN;
   P.k_blocks = (P.Kg + BK - 1) / BK;
   const int tiles = P.m_tiles * P.n_tiles;
   if (tiles == 0) return PACKR_OK;
-  const int grid = tiles < sm_count() ? tiles : sm_count();
-  packr_gemm_kernel<MODE><<<grid, C::kThreads, C::kSmemBytes, stream>>>(P, maps);
+  const int max_pairs = sm_count() / 2;
+  const int pairs = tiles < max_pairs ? tiles : max_pairs;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.blockDim = dim3(C::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, packr_gemm_kernel<MODE>, P, maps) != cudaSuccess) {
+    cudaGetLastError();
+    return PACKR_ERR_LAUNCH;
+  }
   return launch_status();
 }
 
@@ -584,7 +623,7 @@ namespace gemm {
 
 // Stand-alone decode of W = bf16(W_f + bf16(lut[W_p])) into a row-major
 // [K, N] bf16 array, through exactly the load / lookup / add / swizzled store
-// routines the FWD GEMM's decode warps run, one 64 x 256 tile at a time.
+// routines the FWD GEMM's decode warps run, one 64 x 128 half-tile at a time.
 __global__ void __launch_bounds__(DEC_THREADS) decode_check_kernel(const Params P, uint16_t* __restrict__ out,
                                                                   int k_tiles, int n_tiles) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -596,16 +635,16 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_check_kernel(const Params 
   __syncthreads();
   const uint32_t lut_lane = smem_u32(lut_s) + (uint32_t)lane * 4u;
   for (int idx = blockIdx.x; idx < k_tiles * n_tiles; idx += gridDim.x) {
-    const int k0 = (idx % k_tiles) * BK, n0 = (idx / k_tiles) * BN;
+    const int k0 = (idx % k_tiles) * BK, n0 = (idx / k_tiles) * BN_CTA;
     Chunks c;
     decode_load<FWD>(c, P, t, n0, k0);
     decode_store<FWD>(c, smem_u32(tile), lut_lane, t);
     __syncthreads();
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
+    for (int i = 0; i < CHUNKS; ++i) {
       int brow, bcol8;
       chunk_coords<FWD>(t, i, brow, bcol8);
-      const uint32_t off = (uint32_t)((bcol8 >> 3) * 8192 + brow * 128 + (((bcol8 & 7) ^ (brow & 7)) << 4));
+      const uint32_t off = chunk_smem_off<FWD>(brow, bcol8);
       const uint4 q = *reinterpret_cast<const uint4*>(tile + off);
       const uint32_t w[4] = {q.x, q.y, q.z, q.w};
       const long long r = (long long)k0 + brow, c0 = (long long)n0 + 8 * bcol8;
@@ -636,7 +675,7 @@ int decode_check(const uint8_t* W_p, const uint16_t* W_f, const float* lut, uint
   P.w_rows = (int)K;
   P.w_cols = (int)N;
   P.w_vec = (N & 7) == 0 && aligned(W_f, 16) && aligned(W_p, 8);
-  const long long kt = (K + BK - 1) / BK, nt = (N + BN - 1) / BN;
+  const long long kt = (K + BK - 1) / BK, nt = (N + BN_CTA - 1) / BN_CTA;
   if (kt * nt == 0) return PACKR_OK;
   const long long grid = kt * nt < 4 * sm_count() ? kt * nt : 4 * sm_count();
   decode_check_kernel<<<(int)grid, DEC_THREADS, smem, st>>>(P, out, (int)kt, (int)nt);

@@ -1,0 +1,136 @@
+"""Data-parallel sharded 8-bit AdamW (packr_b200.dp.ShardedAdam8): host-side
+logic on CPU with gloo, world_size 2 and 3, the optimizer arithmetic played
+by the oracle.  The N-rank step must equal the single-process step on the
+rank-averaged gradient, element for element, and every rank must end with
+identical parameters."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+import oracle
+from packr_b200.dp import ShardedAdam8
+
+
+def _np(t):
+    return t.view(torch.int16).numpy().view(np.uint16) if t.dtype == torch.bfloat16 else t.numpy()
+
+
+def oracle_adam_fn(entries, lr, b1, b2, eps, bc1, bc2, wd):
+    for p, g, m, v, ms, vs in entries:
+        oracle.adam8_step(_np(p), _np(g).copy(), m.numpy(), v.numpy(), ms.numpy(), vs.numpy(), lr, b1, b2, eps, bc1,
+                          bc2, wd)
+
+
+SHAPES = [((96, 40), torch.bfloat16), ((256,), torch.float32), ((40,), torch.bfloat16), ((300, 7), torch.bfloat16),
+          ((1,), torch.float32)]
+
+
+def make_params():
+    g = torch.Generator().manual_seed(0)
+    return [torch.nn.Parameter((torch.randn(*s, generator=g) * 0.02).to(dt)) for s, dt in SHAPES]
+
+
+def make_grads(rank, step):
+    """(B + rank*D) * 2^-12 with small integers B, D: every partial sum over
+    ranks and the average (B + D*(world-1)/2 for world 2 and 3 with even D...)
+    is exact in bf16 and f32, so the reduce-scatter average is exact."""
+    g = torch.Generator().manual_seed(step)
+    out = []
+    for s, dt in SHAPES:
+        B = torch.randint(-48, 49, s, generator=g).float()
+        D = 2 * torch.randint(-4, 5, s, generator=g).float()
+        out.append(((B + rank * D) * 2.0 ** -12).to(dt))
+    return out
+
+
+def _worker(rank, world, port, steps, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        params = make_params()
+        opt = ShardedAdam8(params, lr=1e-3, weight_decay=0.01, adam_fn=oracle_adam_fn)
+        for s in range(1, steps + 1):
+            for p, gr in zip(params, make_grads(rank, s)):
+                p.grad = gr
+            opt.step()
+        q.put((rank, [_np(p.detach()).copy() for p in params], opt.shard_numel))
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def expected(world, steps):
+    """Single process: the exact rank-average of the gradients, then the
+    oracle step per parameter."""
+    params = [p.detach().clone() for p in make_params()]
+    state = [(np.zeros(p.numel(), np.int8), np.zeros(p.numel(), np.int8),
+              np.ones((p.numel() + 255) // 256, np.float32), np.ones((p.numel() + 255) // 256, np.float32))
+             for p in params]
+    for s in range(1, steps + 1):
+        grads = [make_grads(r, s) for r in range(world)]
+        bc1, bc2 = oracle.adam8_bias_corrections(0.9, 0.999, s)
+        for i, p in enumerate(params):
+            avg = (sum(grads[r][i].double() for r in range(world)) / world).to(p.dtype)
+            m, v, ms, vs = state[i]
+            oracle.adam8_step(_np(p), _np(avg.contiguous()).copy(), m, v, ms, vs, 1e-3, 0.9, 0.999, 1e-8, bc1, bc2,
+                              0.01)
+    return [_np(p).copy() for p in params]
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_sharded_step_equals_single_process(world):
+    steps = 3
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, steps, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    for _ in range(world):
+        r, ps, shard = q.get(timeout=120)
+        results[r] = (ps, shard)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    want = expected(world, steps)
+    for r in range(world):
+        for a, b in zip(results[r][0], results[0][0]):
+            assert np.array_equal(a, b), "ranks disagree"
+    total_state = sum(results[r][1] for r in range(world))
+    assert total_state == sum(results[0][1] for _ in range(world))  # equal shards
+    for i, (got, exp) in enumerate(zip(results[0][0], want)):
+        if got.dtype == np.uint16:
+            gf, ef = oracle.bf16_to_f32(got), oracle.bf16_to_f32(exp)
+        else:
+            gf, ef = got, exp
+        assert np.array_equal(got, exp), i
+
+
+def test_single_process_layout_and_views():
+    params = make_params()
+    before = [p.detach().clone() for p in params]
+    opt = ShardedAdam8(params, lr=1e-3, adam_fn=oracle_adam_fn)
+    # parameters now live in the flat buffers, values unchanged, 256-aligned starts
+    for p, b in zip(params, before):
+        assert torch.equal(p.detach(), b)
+    for g in opt.groups.values():
+        for s in g.slots:
+            assert s.offset % 256 == 0
+            assert s.param.data_ptr() == g.flat[s.offset:].data_ptr()
+    for p, gr in zip(params, make_grads(0, 1)):
+        p.grad = gr
+    opt.step()
+    assert opt.step_count == 1
+    assert all(not torch.equal(p.detach(), b) for p, b in zip(params, before))
