@@ -47,6 +47,21 @@ namespace gemm {
 
 using namespace sm100;
 
+// Event trace for pipeline studies: compiled to nothing unless the library is
+// built with -DPACKR_TRACE, in which case the build provides
+// packr_trace(kind, index) recording timestamps of CTA pair 0.
+#ifdef PACKR_TRACE
+__device__ void packr_trace(int kind, int index);
+#define PACKR_TRACE_EVENT(kind, index) \
+  do {                                 \
+    if (blockIdx.x < 2) packr_trace((kind), (index)); \
+  } while (0)
+#else
+#define PACKR_TRACE_EVENT(kind, index) \
+  do {                                 \
+  } while (0)
+#endif
+
 constexpr int BM = 128;          // A rows per CTA (MMA M = 256 per pair)
 constexpr int BN = 256;          // MMA N (output columns per tile)
 constexpr int BN_CTA = 128;      // B columns held by each CTA
@@ -54,12 +69,11 @@ constexpr int BK = 64, UK = 16;
 constexpr int STAGES = 6;
 constexpr int A_BYTES = BM * BK * 2;      // 16 KB
 constexpr int B_BYTES = BN_CTA * BK * 2;  // 16 KB
-constexpr int EPI_WARPS = 4;
 constexpr int DEC_WARPS = 8;
 constexpr int DEC_THREADS = DEC_WARPS * 32;
 constexpr int CHUNKS = BN_CTA * BK / 8 / DEC_THREADS;  // 4 chunks of 8 weights per thread per stage
 constexpr int LUT_BYTES = 256 * 32 * 4;  // one u32 per (entry, lane)
-constexpr int HIST_BYTES = EPI_WARPS * 256 * 4;
+constexpr int HIST_COPIES = 4;  // lut-gradient histogram copies per epilogue warp (lane & 3)
 constexpr int ACC_COLS = BN;
 constexpr int TMEM_COLS = 2 * ACC_COLS;
 constexpr uint16_t PAIR_MASK = 0x3;
@@ -69,11 +83,18 @@ enum Mode { FWD = 0, DX = 1, DW = 2 };
 template <int MODE>
 struct Cfg {
   static constexpr bool kDecode = MODE != DW;
-  static constexpr int kWarps = 2 + EPI_WARPS + (kDecode ? DEC_WARPS : 0);
+  // DW's histogram epilogue is the heavier one: two warps per TMEM lane
+  // quarter, each taking half of the tile's columns.
+  static constexpr int kEpiWarps = kDecode ? 4 : 8;
+  static constexpr int kChunksPerEpiWarp = (BN / 32) / (kEpiWarps / 4);
+  static constexpr int kDecWarp0 = 2 + kEpiWarps;             // first decode warp
+  static constexpr int kSignalWarp = kDecWarp0 + DEC_WARPS;   // decode-completion signaller
+  static constexpr int kWarps = 2 + kEpiWarps + (kDecode ? DEC_WARPS + 1 : 0);
   static constexpr int kThreads = kWarps * 32;
   static constexpr bool kAmn = MODE == DW;   // A stored MN-major in smem
   static constexpr bool kBmn = MODE != DX;   // B stored MN-major in smem
-  static constexpr int kAuxBytes = kDecode ? LUT_BYTES : HIST_BYTES;
+  static constexpr int kHistBytes = kEpiWarps * HIST_COPIES * 256 * 4;
+  static constexpr int kAuxBytes = kDecode ? LUT_BYTES : kHistBytes;
   static constexpr int kBarOff = STAGES * (A_BYTES + B_BYTES) + kAuxBytes;
   static constexpr int kSmemBytes = kBarOff + 256 + 1024;  // barriers + alignment slack
   static constexpr uint32_t kIdesc = idesc_bf16_f32(2 * BM, BN, kAmn, kBmn);
@@ -114,10 +135,10 @@ struct Maps {
 // remotely); empty / tfull / drain receive the even CTA's multicast commits.
 struct Bars {
   uint64_t full[STAGES];    // TMA bytes of both CTAs landed        (count 1 + tx)
-  uint64_t bfull[STAGES];   // decoded B written by both CTAs       (count 2*DEC_WARPS)
+  uint64_t bfull[STAGES];   // decoded B written by both CTAs       (count 2)
   uint64_t empty[STAGES];   // MMAs done reading the stage          (count 1)
   uint64_t tfull[2];        // accumulator complete                 (count 1)
-  uint64_t tempty[2];       // accumulator drained by both CTAs     (count 2*EPI_WARPS)
+  uint64_t tempty[2];       // accumulator drained by both CTAs     (count 2*epilogue warps)
   uint64_t drain;           // every MMA complete                   (count 1)
   uint32_t tmem_base;
   int abort;
@@ -266,12 +287,12 @@ __global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&bars->full[s], 1);
-      mbar_init(&bars->bfull[s], 2 * DEC_WARPS);
+      mbar_init(&bars->bfull[s], 2);
       mbar_init(&bars->empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&bars->tfull[a], 1);
-      mbar_init(&bars->tempty[a], 2 * EPI_WARPS);
+      mbar_init(&bars->tempty[a], 2 * C::kEpiWarps);
     }
     mbar_init(&bars->drain, 1);
     bars->abort = 0;
@@ -283,18 +304,18 @@ __global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
       if (MODE == DW) prefetch_tmap(&maps.b[s]);
     }
   }
-  if (MODE == DW && warp >= 2 && warp < 2 + EPI_WARPS) {
+  if (MODE == DW && warp >= 2 && warp < C::kDecWarp0) {
     float* hist = reinterpret_cast<float*>(sAux);
-    for (int i = threadIdx.x - 64; i < EPI_WARPS * 256; i += EPI_WARPS * 32) hist[i] = 0.0f;
+    for (int i = threadIdx.x - 64; i < C::kHistBytes / 4; i += C::kEpiWarps * 32) hist[i] = 0.0f;
   }
   if (warp == 1) {
     tmem_alloc_pair(&bars->tmem_base, TMEM_COLS);
     tmem_relinquish_pair();
   }
-  if (C::kDecode && warp >= 2 + EPI_WARPS) {
+  if (C::kDecode && warp >= C::kDecWarp0 && warp < C::kSignalWarp) {
     // Lane-replicated bf16 lut: word (e*32 + l) holds bf16_rne(lut[e]) for lane l.
     uint32_t* lut_s = reinterpret_cast<uint32_t*>(sAux);
-    const int dw = warp - (2 + EPI_WARPS);
+    const int dw = warp - C::kDecWarp0;
     for (int e = dw; e < 256; e += DEC_WARPS) lut_s[e * 32 + lane] = f32_to_bf16_rne(__ldg(P.lut + e));
   }
   tc_fence_before();
@@ -315,6 +336,7 @@ __global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
           const int s = it % STAGES;
           const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
           if (!mbar_wait(&bars->empty[s], ph ^ 1u, abort_flag)) { ok = false; break; }
+          PACKR_TRACE_EVENT(0, it);
           const int seg = kk / P.k_blocks;
           const int k0 = (kk % P.k_blocks) * BK;
           if (rank == 0) mbar_arrive_expect_tx(&bars->full[s], C::kTxBytes);
@@ -343,13 +365,16 @@ __global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
         const int acc = t_local & 1;
         const uint32_t aph = (uint32_t)(t_local >> 1) & 1u;
         if (!mbar_wait_cluster(&bars->tempty[acc], aph ^ 1u, abort_flag)) { ok = false; break; }
+        PACKR_TRACE_EVENT(3, t_local);
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * ACC_COLS);
         for (int kk = 0; kk < kb_total; ++kk, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
           if (!mbar_wait(&bars->full[s], ph, abort_flag)) { ok = false; break; }
+          PACKR_TRACE_EVENT(1, it);
           if (C::kDecode && !mbar_wait_cluster(&bars->bfull[s], ph, abort_flag)) { ok = false; break; }
+          PACKR_TRACE_EVENT(2, it);
           tc_fence_after();
           const uint32_t a_s = sA0 + s * A_BYTES, b_s = sB0 + s * B_BYTES;
 #pragma unroll
@@ -365,26 +390,56 @@ __global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
       }
       umma_commit_pair(&bars->drain, PAIR_MASK);
     }
-  } else if (warp < 2 + EPI_WARPS) {
+  } else if (warp < C::kDecWarp0) {
     // ------------------------------------------------ epilogue (both CTAs)
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int q = warp & 3;                    // TMEM lane quarter this warp may access
+    const int cc0 = ((warp - 2) >> 2) * C::kChunksPerEpiWarp;  // first 32-column chunk
     const int row = q * 32 + lane;
-    float* hist = reinterpret_cast<float*>(sAux) + (warp - 2) * 256;
     const uint32_t tempty0 = mapa(smem_u32(&bars->tempty[0]), 0);
     const uint32_t tempty1 = mapa(smem_u32(&bars->tempty[1]), 0);
+    const uint32_t hist_lane = smem_u32(sAux) + (uint32_t)(((warp - 2) * HIST_COPIES + (lane & 3)) * 1024);
+    // DW: the W_p bytes of the next tile's chunks are fetched before its
+    // accumulator is ready (they do not depend on it)
+    uint4 wpa[C::kChunksPerEpiWarp], wpb[C::kChunksPerEpiWarp];
+    auto fetch_idx = [&](int tile) {
+      const long long gm = (long long)((tile % P.m_tiles) * (2 * BM) + (int)rank * BM + row);
+      const int n0 = (tile / P.m_tiles) * BN;
+#pragma unroll
+      for (int c = 0; c < C::kChunksPerEpiWarp; ++c) {
+        const int gn0 = n0 + (cc0 + c) * 32;
+        uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        if (gm < P.Mg && gn0 < P.Ng) {
+          const uint8_t* ip = P.hist_idx + gm * P.ld_out + gn0;
+          const int nval = min(32, P.Ng - gn0);
+          if (nval == 32 && (P.ld_out & 15) == 0 && P.idx_vec) {
+            const uint4 a = __ldg(reinterpret_cast<const uint4*>(ip));
+            const uint4 b = __ldg(reinterpret_cast<const uint4*>(ip + 16));
+            w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w; w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
+          } else {
+            for (int j = 0; j < nval; ++j) w[j >> 2] |= (uint32_t)__ldg(ip + j) << (8 * (j & 3));
+          }
+        }
+        wpa[c] = make_uint4(w[0], w[1], w[2], w[3]);
+        wpb[c] = make_uint4(w[4], w[5], w[6], w[7]);
+      }
+    };
+    const bool want_hist = MODE == DW && P.hist_idx != nullptr;
+    if (want_hist && pair < num_tiles) fetch_idx(pair);
     int t_local = 0;
     for (int tile = pair; tile < num_tiles; tile += npairs, ++t_local) {
       const int acc = t_local & 1;
       const uint32_t aph = (uint32_t)(t_local >> 1) & 1u;
       // every lane waits; the warp proceeds only if all lanes saw the phase
       if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bars->tfull[acc], aph, abort_flag))) break;
+      if (warp == 2 && lane == 0) PACKR_TRACE_EVENT(4, t_local);
       tc_fence_after();
       const int m0 = (tile % P.m_tiles) * (2 * BM) + (int)rank * BM;
       const int n0 = (tile / P.m_tiles) * BN;
       const long long gm = (long long)m0 + row;
       const bool row_ok = gm < P.Mg;
-#pragma unroll 1
-      for (int cc = 0; cc < BN / 32; ++cc) {
+#pragma unroll
+      for (int c = 0; c < C::kChunksPerEpiWarp; ++c) {
+        const int cc = cc0 + c;
         uint32_t v[32];
         tmem_ld_32x32b_x32(tmem_base + (uint32_t)(acc * ACC_COLS + cc * 32) + ((uint32_t)(q * 32) << 16), v);
         tmem_ld_wait();
@@ -411,83 +466,79 @@ __global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
           } else {
             for (int j = 0; j < nval; ++j) o[j] = f[j];
           }
-        } else if (MODE == DX) {
-          uint32_t h[32];
+        } else {  // DX: bf16(acc) as bf16 or f32;  DW: bf16(acc) (+ histogram)
+          uint32_t h[16];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) h[j] = f32_to_bf16_rne(__uint_as_float(v[j]));
-          if (P.out_f32) {
-            float* o = static_cast<float*>(P.out) + gm * P.ld_out + gn0;
-            if (nval == 32 && (P.ld_out & 3) == 0 && P.out_vec) {
-#pragma unroll
-              for (int j = 0; j < 32; j += 4)
-                __stcs(reinterpret_cast<float4*>(o + j), make_float4(bf16_to_f32(h[j]), bf16_to_f32(h[j + 1]),
-                                                                      bf16_to_f32(h[j + 2]), bf16_to_f32(h[j + 3])));
-            } else {
-              for (int j = 0; j < nval; ++j) o[j] = bf16_to_f32(h[j]);
-            }
-          } else {
-            uint16_t* o = static_cast<uint16_t*>(P.out) + gm * P.ld_out + gn0;
-            if (nval == 32 && (P.ld_out & 7) == 0 && P.out_vec) {
-#pragma unroll
-              for (int j = 0; j < 32; j += 8)
-                __stcs(reinterpret_cast<uint4*>(o + j), make_uint4(h[j] | (h[j + 1] << 16), h[j + 2] | (h[j + 3] << 16),
-                                                                    h[j + 4] | (h[j + 5] << 16), h[j + 6] | (h[j + 7] << 16)));
-            } else {
-              for (int j = 0; j < nval; ++j) o[j] = (uint16_t)h[j];
-            }
-          }
-        } else {  // DW
+          for (int j = 0; j < 16; ++j) h[j] = pack_bf16x2_rne(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
           if (P.out != nullptr) {
-            uint16_t* o = static_cast<uint16_t*>(P.out) + gm * P.ld_out + gn0;
-            uint32_t h[32];
+            if (MODE == DX && P.out_f32) {
+              float* o = static_cast<float*>(P.out) + gm * P.ld_out + gn0;
+              if (nval == 32 && (P.ld_out & 3) == 0 && P.out_vec) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) h[j] = f32_to_bf16_rne(__uint_as_float(v[j]));
-            if (nval == 32 && (P.ld_out & 7) == 0 && P.out_vec) {
-#pragma unroll
-              for (int j = 0; j < 32; j += 8)
-                __stcs(reinterpret_cast<uint4*>(o + j), make_uint4(h[j] | (h[j + 1] << 16), h[j + 2] | (h[j + 3] << 16),
-                                                                    h[j + 4] | (h[j + 5] << 16), h[j + 6] | (h[j + 7] << 16)));
+                for (int j = 0; j < 16; j += 2)
+                  __stcs(reinterpret_cast<float4*>(o + 2 * j),
+                         make_float4(__uint_as_float(h[j] << 16), __uint_as_float(h[j] & 0xFFFF0000u),
+                                     __uint_as_float(h[j + 1] << 16), __uint_as_float(h[j + 1] & 0xFFFF0000u)));
+              } else {
+                for (int j = 0; j < nval; ++j) o[j] = bf16_to_f32((h[j >> 1] >> (16 * (j & 1))) & 0xFFFFu);
+              }
             } else {
-              for (int j = 0; j < nval; ++j) o[j] = (uint16_t)h[j];
+              uint16_t* o = static_cast<uint16_t*>(P.out) + gm * P.ld_out + gn0;
+              if (nval == 32 && (P.ld_out & 7) == 0 && P.out_vec) {
+#pragma unroll
+                for (int j = 0; j < 16; j += 4)
+                  __stcs(reinterpret_cast<uint4*>(o + 2 * j), make_uint4(h[j], h[j + 1], h[j + 2], h[j + 3]));
+              } else {
+                for (int j = 0; j < nval; ++j) o[j] = (uint16_t)(h[j >> 1] >> (16 * (j & 1)));
+              }
             }
           }
-          if (P.hist_idx != nullptr) {
-            const uint8_t* ip = P.hist_idx + gm * P.ld_out + gn0;
-            uint32_t w[8];
-            if (nval == 32 && (P.ld_out & 15) == 0 && P.idx_vec) {
-              const uint4 a = __ldg(reinterpret_cast<const uint4*>(ip));
-              const uint4 b = __ldg(reinterpret_cast<const uint4*>(ip + 16));
-              w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w; w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
-            } else {
-#pragma unroll
-              for (int j = 0; j < 8; ++j) w[j] = 0;
-              for (int j = 0; j < nval; ++j) w[j >> 2] |= (uint32_t)__ldg(ip + j) << (8 * (j & 3));
-            }
+          if (MODE == DW && want_hist) {
+            const uint32_t w[8] = {wpa[c].x, wpa[c].y, wpa[c].z, wpa[c].w, wpb[c].x, wpb[c].y, wpb[c].z, wpb[c].w};
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
-              if (j < nval) atomicAdd(hist + ((w[j >> 2] >> (8 * (j & 3))) & 0xFFu), __uint_as_float(v[j]));
+              if (j < nval) {
+                const uint32_t bin = (w[j >> 2] >> (8 * (j & 3))) & 0xFFu;
+                asm volatile("red.shared.add.f32 [%0], %1;" ::"r"(hist_lane + bin * 4), "f"(__uint_as_float(v[j]))
+                             : "memory");
+              }
             }
           }
         }
       }
       tc_fence_before();
       __syncwarp();
+      if (warp == 2 && lane == 0) PACKR_TRACE_EVENT(5, t_local);
       if (lane == 0) mbar_arrive_cluster(acc ? tempty1 : tempty0);
+      if (want_hist && tile + npairs < num_tiles) fetch_idx(tile + npairs);
     }
     if (MODE == DW && P.dlut_sum != nullptr) {
-      asm volatile("bar.sync 1, %0;" ::"n"(EPI_WARPS * 32) : "memory");
+      asm volatile("bar.sync 1, %0;" ::"n"(C::kEpiWarps * 32) : "memory");
       const float* h0 = reinterpret_cast<const float*>(sAux);
       const int et = threadIdx.x - 64;
-      for (int b = et; b < 256; b += EPI_WARPS * 32) {
+      for (int b = et; b < 256; b += C::kEpiWarps * 32) {
         float s = 0.0f;
 #pragma unroll
-        for (int w = 0; w < EPI_WARPS; ++w) s += h0[w * 256 + b];
+        for (int w = 0; w < C::kEpiWarps * HIST_COPIES; ++w) s += h0[w * 256 + b];
         if (s != 0.0f) atomicAdd(P.dlut_sum + b, s);
       }
     }
+  } else if (C::kDecode && warp == C::kSignalWarp) {
+    // ------------------------------------------------ decode-completion signaller
+    // The decode warps keep global loads of later stages in flight; a release
+    // at cluster scope issued by them would wait for those loads.  They hand
+    // each finished stage to this warp through a named barrier instead, and
+    // this warp (no loads outstanding) arrives on the even CTA's bfull.
+    const int my_tiles = pair < num_tiles ? (num_tiles - 1 - pair) / npairs + 1 : 0;
+    const int total = my_tiles * kb_total;
+    for (int it = 0; it < total; ++it) {
+      const int s = it % STAGES;
+      asm volatile("bar.sync %0, %1;" ::"r"(2 + s), "n"(DEC_THREADS + 32) : "memory");
+      if (lane == 0 && !*abort_flag) mbar_arrive_cluster(mapa(smem_u32(&bars->bfull[s]), 0));
+    }
   } else if (C::kDecode) {
     // ------------------------------------------------ weight decode (both CTAs)
-    const int t = threadIdx.x - (2 + EPI_WARPS) * 32;
+    const int t = threadIdx.x - C::kDecWarp0 * 32;
     const uint32_t lut_lane = smem_u32(sAux) + (uint32_t)lane * 4u;
     const uint32_t sB0 = smem_u32(sB);
     const int my_tiles = pair < num_tiles ? (num_tiles - 1 - pair) / npairs + 1 : 0;
@@ -500,15 +551,20 @@ __global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
       const int nb0 = (tile / P.m_tiles) * BN + (int)rank * BN_CTA;
       decode_load<MODE>(c, P, t, nb0, (kk % P.k_blocks) * BK);
     };
-    auto process = [&](const Chunks& c, int it) -> bool {
+    // Every decode thread arrives on the hand-off barrier for every item, also
+    // after an abort (then without decoding), so the signal warp's bar.sync
+    // always completes.
+    auto process = [&](const Chunks& c, int it) {
       const int s = it % STAGES;
       const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
-      if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bars->empty[s], ph ^ 1u, abort_flag))) return false;
-      decode_store<MODE>(c, sB0 + s * B_BYTES, lut_lane, t);
-      fence_proxy_async_smem();
+      if (!*abort_flag && __all_sync(0xFFFFFFFFu, mbar_wait(&bars->empty[s], ph ^ 1u, abort_flag))) {
+        if (t == 0) PACKR_TRACE_EVENT(6, it);
+        decode_store<MODE>(c, sB0 + s * B_BYTES, lut_lane, t);
+        fence_proxy_async_smem();
+        if (t == 0) PACKR_TRACE_EVENT(7, it);
+      }
       __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(mapa(smem_u32(&bars->bfull[s]), 0));
-      return true;
+      asm volatile("bar.arrive %0, %1;" ::"r"(2 + s), "n"(DEC_THREADS + 32) : "memory");
     };
     // 3-deep ring: loads for items it+1 and it+2 are in flight while item it
     // is decoded.
@@ -517,13 +573,13 @@ __global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
     if (total > 1) load(r1, 1);
     for (int it = 0; it < total; it += 3) {
       if (it + 2 < total) load(r2, it + 2);
-      if (!process(r0, it)) break;
+      process(r0, it);
       if (it + 1 >= total) break;
       if (it + 3 < total) load(r0, it + 3);
-      if (!process(r1, it + 1)) break;
+      process(r1, it + 1);
       if (it + 2 >= total) break;
       if (it + 4 < total) load(r1, it + 4);
-      if (!process(r2, it + 2)) break;
+      process(r2, it + 2);
     }
   }
 
