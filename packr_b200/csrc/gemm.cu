@@ -66,7 +66,7 @@ constexpr int BM = 128;          // A rows per CTA (MMA M = 256 per pair)
 constexpr int BN = 256;          // MMA N (output columns per tile)
 constexpr int BN_CTA = 128;      // B columns held by each CTA
 constexpr int BK = 64, UK = 16;
-constexpr int STAGES = 6;
+constexpr int MAX_STAGES = 6;
 constexpr int A_BYTES = BM * BK * 2;      // 16 KB
 constexpr int B_BYTES = BN_CTA * BK * 2;  // 16 KB
 constexpr int DEC_WARPS = 8;
@@ -80,25 +80,34 @@ constexpr uint16_t PAIR_MASK = 0x3;
 
 enum Mode { FWD = 0, DX = 1, DW = 2 };
 
-template <int MODE>
+// WTMA (decode modes): W_f and W_p tiles arrive by TMA into shared memory
+// and are decoded in place; otherwise (rows of W_p not a multiple of 16
+// bytes) the decode warps load them into a register ring.
+template <int MODE, bool WTMA>
 struct Cfg {
   static constexpr bool kDecode = MODE != DW;
+  static constexpr bool kWtma = kDecode && WTMA;
+  static constexpr int kStages = kWtma ? 4 : 6;
+  static constexpr int kWpBytes = kWtma ? BN_CTA * BK : 0;  // u8 W_p tile per stage
+  static constexpr int kStageBytes = A_BYTES + B_BYTES + kWpBytes;
   // DW's histogram epilogue is the heavier one: two warps per TMEM lane
   // quarter, each taking half of the tile's columns.
   static constexpr int kEpiWarps = kDecode ? 4 : 8;
   static constexpr int kChunksPerEpiWarp = (BN / 32) / (kEpiWarps / 4);
   static constexpr int kDecWarp0 = 2 + kEpiWarps;             // first decode warp
-  static constexpr int kSignalWarp = kDecWarp0 + DEC_WARPS;   // decode-completion signaller
-  static constexpr int kWarps = 2 + kEpiWarps + (kDecode ? DEC_WARPS + 1 : 0);
+  static constexpr int kSignalWarp = kDecWarp0 + DEC_WARPS;   // decode-completion signaller (register ring only)
+  static constexpr int kWarps = 2 + kEpiWarps + (kDecode ? DEC_WARPS + (kWtma ? 0 : 1) : 0);
   static constexpr int kThreads = kWarps * 32;
   static constexpr bool kAmn = MODE == DW;   // A stored MN-major in smem
   static constexpr bool kBmn = MODE != DX;   // B stored MN-major in smem
   static constexpr int kHistBytes = kEpiWarps * HIST_COPIES * 256 * 4;
   static constexpr int kAuxBytes = kDecode ? LUT_BYTES : kHistBytes;
-  static constexpr int kBarOff = STAGES * (A_BYTES + B_BYTES) + kAuxBytes;
+  static constexpr int kBarOff = kStages * kStageBytes + kAuxBytes;
   static constexpr int kSmemBytes = kBarOff + 256 + 1024;  // barriers + alignment slack
   static constexpr uint32_t kIdesc = idesc_bf16_f32(2 * BM, BN, kAmn, kBmn);
   static constexpr uint32_t kTxBytes = 2 * (kDecode ? A_BYTES : A_BYTES + B_BYTES);  // both CTAs
+  static constexpr uint32_t kWTxBytes = B_BYTES + kWpBytes;                          // this CTA's W tiles
+  static constexpr uint32_t kBfullCount = kWtma ? 2 * DEC_WARPS : 2;
 };
 
 struct Params {
@@ -128,15 +137,18 @@ struct Params {
 struct Maps {
   CUtensorMap a[3];
   CUtensorMap b[3];
+  CUtensorMap wf;  // W_f (bf16), decode modes with TMA-staged weights
+  CUtensorMap wp;  // W_p (u8)
 };
 
 // Barriers live at the same offset in both CTAs of a pair.  full / bfull /
 // tempty are used in the even CTA only (the odd CTA's producers arrive there
 // remotely); empty / tfull / drain receive the even CTA's multicast commits.
 struct Bars {
-  uint64_t full[STAGES];    // TMA bytes of both CTAs landed        (count 1 + tx)
-  uint64_t bfull[STAGES];   // decoded B written by both CTAs       (count 2)
-  uint64_t empty[STAGES];   // MMAs done reading the stage          (count 1)
+  uint64_t full[MAX_STAGES];    // A (DW: A and B) bytes of both CTAs landed  (count 1 + tx)
+  uint64_t bfull[MAX_STAGES];   // decoded B written by both CTAs              (count kBfullCount)
+  uint64_t empty[MAX_STAGES];   // MMAs done reading the stage                 (count 1)
+  uint64_t wfull[MAX_STAGES];   // this CTA's W_f / W_p tiles landed           (count 1 + tx)
   uint64_t tfull[2];        // accumulator complete                 (count 1)
   uint64_t tempty[2];       // accumulator drained by both CTAs     (count 2*epilogue warps)
   uint64_t drain;           // every MMA complete                   (count 1)
@@ -263,16 +275,64 @@ __device__ __forceinline__ void decode_store(const Chunks& c, uint32_t b_stage, 
   }
 }
 
-// ------------------------------------------------------------------ kernel
+// Decode of a TMA-staged stage in place: W_f already sits in the B tile in
+// its swizzled layout, W_p in a row-major u8 tile (FWD: 64 rows x 128,
+// DX: 128 rows x 64).  Elements outside W (zero-filled by TMA) are stored as
+// zero rather than decoded.
 template <int MODE>
-__global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
+__device__ __forceinline__ void decode_in_place(const Params& P, uint32_t b_stage, uint32_t wp_stage,
+                                                uint32_t lut_lane, int t, int nb0, int k0) {
+#pragma unroll
+  for (int i = 0; i < CHUNKS; ++i) {
+    int brow, bcol8;
+    chunk_coords<MODE>(t, i, brow, bcol8);
+    const uint32_t off = chunk_smem_off<MODE>(brow, bcol8);
+    const uint32_t wpoff = (uint32_t)(brow * (MODE == FWD ? BN_CTA : BK) + 8 * bcol8);
+    long long wr, wc;
+    if (MODE == FWD) {
+      wr = (long long)k0 + brow;
+      wc = (long long)nb0 + 8 * bcol8;
+    } else {
+      wr = (long long)nb0 + brow;
+      wc = (long long)k0 + 8 * bcol8;
+    }
+    const int nv = (wr < P.w_rows && wc < P.w_cols) ? (int)min(8ll, (long long)P.w_cols - wc) : 0;
+    uint32_t f[4], w[2];
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(f[0]), "=r"(f[1]), "=r"(f[2]), "=r"(f[3]) : "r"(b_stage + off));
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(w[0]), "=r"(w[1]) : "r"(wp_stage + wpoff));
+    uint32_t r[4];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const uint32_t word = w[p >> 1];
+      const int sh = 16 * (p & 1);
+      const uint32_t e0 = ((word >> sh) & 0xFFu) << 7;
+      const uint32_t e1 = ((word >> (sh + 8)) & 0xFFu) << 7;
+      const uint32_t l = prmt(lut_fetch(lut_lane, e0), lut_fetch(lut_lane, e1), 0x5410u);
+      r[p] = bf16x2_add(f[p], l);
+    }
+    if (nv < 8) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (j >= nv) r[j >> 1] &= (j & 1) ? 0x0000FFFFu : 0xFFFF0000u;
+    }
+    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(b_stage + off), "r"(r[0]), "r"(r[1]),
+                 "r"(r[2]), "r"(r[3])
+                 : "memory");
+  }
+}
+
+// ------------------------------------------------------------------ kernel
+template <int MODE, bool WTMA>
+__global__ void __launch_bounds__(Cfg<MODE, WTMA>::kThreads, 1)
     packr_gemm_kernel(const Params P, const __grid_constant__ Maps maps) {
-  using C = Cfg<MODE>;
+  using C = Cfg<MODE, WTMA>;
+  constexpr int STAGES = C::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
-  uint8_t* sAux = smem + STAGES * (A_BYTES + B_BYTES);
+  uint8_t* sWp = smem + STAGES * (A_BYTES + B_BYTES);
+  uint8_t* sAux = smem + STAGES * C::kStageBytes;
   Bars* bars = reinterpret_cast<Bars*>(smem + C::kBarOff);
   volatile int* abort_flag = &bars->abort;
 
@@ -287,8 +347,9 @@ __global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&bars->full[s], 1);
-      mbar_init(&bars->bfull[s], 2);
+      mbar_init(&bars->bfull[s], C::kBfullCount);
       mbar_init(&bars->empty[s], 1);
+      mbar_init(&bars->wfull[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&bars->tfull[a], 1);
@@ -303,6 +364,10 @@ __global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
       prefetch_tmap(&maps.a[s]);
       if (MODE == DW) prefetch_tmap(&maps.b[s]);
     }
+    if (C::kWtma) {
+      prefetch_tmap(&maps.wf);
+      prefetch_tmap(&maps.wp);
+    }
   }
   if (MODE == DW && warp >= 2 && warp < C::kDecWarp0) {
     float* hist = reinterpret_cast<float*>(sAux);
@@ -312,7 +377,7 @@ __global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
     tmem_alloc_pair(&bars->tmem_base, TMEM_COLS);
     tmem_relinquish_pair();
   }
-  if (C::kDecode && warp >= C::kDecWarp0 && warp < C::kSignalWarp) {
+  if (C::kDecode && warp >= C::kDecWarp0 && warp < C::kDecWarp0 + DEC_WARPS) {
     // Lane-replicated bf16 lut: word (e*32 + l) holds bf16_rne(lut[e]) for lane l.
     uint32_t* lut_s = reinterpret_cast<uint32_t*>(sAux);
     const int dw = warp - C::kDecWarp0;
@@ -350,6 +415,21 @@ __global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
             tma_load_2d_pair(b_dst + 8192, &maps.b[seg], fbar, n0 + 64, k0);
           } else {
             tma_load_2d_pair(a_dst, &maps.a[seg], fbar, k0, m0);
+            if (C::kWtma) {
+              // this CTA's W_f / W_p tiles (its 128 columns of B) onto its own wfull
+              const int nb0 = (tile / P.m_tiles) * BN + (int)rank * BN_CTA;
+              uint8_t* b_dst = sB + s * B_BYTES;
+              uint8_t* p_dst = sWp + s * C::kWpBytes;
+              mbar_arrive_expect_tx(&bars->wfull[s], C::kWTxBytes);
+              if (MODE == FWD) {
+                tma_load_2d(b_dst, &maps.wf, &bars->wfull[s], nb0, k0);
+                tma_load_2d(b_dst + 8192, &maps.wf, &bars->wfull[s], nb0 + 64, k0);
+                tma_load_2d(p_dst, &maps.wp, &bars->wfull[s], nb0, k0);
+              } else {
+                tma_load_2d(b_dst, &maps.wf, &bars->wfull[s], k0, nb0);
+                tma_load_2d(p_dst, &maps.wp, &bars->wfull[s], k0, nb0);
+              }
+            }
           }
         }
       }
@@ -364,7 +444,7 @@ __global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
       for (int tile = pair; tile < num_tiles && ok; tile += npairs, ++t_local) {
         const int acc = t_local & 1;
         const uint32_t aph = (uint32_t)(t_local >> 1) & 1u;
-        if (!mbar_wait_cluster(&bars->tempty[acc], aph ^ 1u, abort_flag)) { ok = false; break; }
+        if (!mbar_wait(&bars->tempty[acc], aph ^ 1u, abort_flag)) { ok = false; break; }
         PACKR_TRACE_EVENT(3, t_local);
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * ACC_COLS);
@@ -373,7 +453,7 @@ __global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
           const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
           if (!mbar_wait(&bars->full[s], ph, abort_flag)) { ok = false; break; }
           PACKR_TRACE_EVENT(1, it);
-          if (C::kDecode && !mbar_wait_cluster(&bars->bfull[s], ph, abort_flag)) { ok = false; break; }
+          if (C::kDecode && !mbar_wait(&bars->bfull[s], ph, abort_flag)) { ok = false; break; }
           PACKR_TRACE_EVENT(2, it);
           tc_fence_after();
           const uint32_t a_s = sA0 + s * A_BYTES, b_s = sB0 + s * B_BYTES;
@@ -384,6 +464,7 @@ __global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
             umma_bf16_pair(d_tmem, ad, bd, C::kIdesc, (kk | k) != 0 ? 1u : 0u);
           }
           umma_commit_pair(&bars->empty[s], PAIR_MASK);
+          PACKR_TRACE_EVENT(10, it);
         }
         if (!ok) break;
         umma_commit_pair(&bars->tfull[acc], PAIR_MASK);
@@ -523,21 +604,45 @@ __global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
         if (s != 0.0f) atomicAdd(P.dlut_sum + b, s);
       }
     }
-  } else if (C::kDecode && warp == C::kSignalWarp) {
+  } else if (C::kDecode && !C::kWtma && warp == C::kSignalWarp) {
     // ------------------------------------------------ decode-completion signaller
-    // The decode warps keep global loads of later stages in flight; a release
-    // at cluster scope issued by them would wait for those loads.  They hand
-    // each finished stage to this warp through a named barrier instead, and
-    // this warp (no loads outstanding) arrives on the even CTA's bfull.
+    // The decode warps keep global loads of later stages in flight; a memory
+    // fence issued by them would wait for those loads.  They hand each
+    // finished stage (after fence.proxy.async) to this warp through a named
+    // barrier instead, and this warp (no loads outstanding) arrives on the
+    // even CTA's bfull.
     const int my_tiles = pair < num_tiles ? (num_tiles - 1 - pair) / npairs + 1 : 0;
     const int total = my_tiles * kb_total;
     for (int it = 0; it < total; ++it) {
       const int s = it % STAGES;
       asm volatile("bar.sync %0, %1;" ::"r"(2 + s), "n"(DEC_THREADS + 32) : "memory");
+      if (lane == 0) PACKR_TRACE_EVENT(8, it);
       if (lane == 0 && !*abort_flag) mbar_arrive_cluster(mapa(smem_u32(&bars->bfull[s]), 0));
+      if (lane == 0) PACKR_TRACE_EVENT(9, it);
+    }
+  } else if (C::kWtma) {
+    // ------------------------------------------------ weight decode, TMA-staged (both CTAs)
+    const int t = threadIdx.x - C::kDecWarp0 * 32;
+    const uint32_t lut_lane = smem_u32(sAux) + (uint32_t)lane * 4u;
+    const uint32_t sB0 = smem_u32(sB), sWp0 = smem_u32(sWp);
+    const int my_tiles = pair < num_tiles ? (num_tiles - 1 - pair) / npairs + 1 : 0;
+    const int total = my_tiles * kb_total;
+    for (int it = 0; it < total; ++it) {
+      const int s = it % STAGES;
+      const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+      if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bars->wfull[s], ph, abort_flag))) break;
+      if (t == 0) PACKR_TRACE_EVENT(6, it);
+      const int tile = pair + (it / kb_total) * npairs;
+      const int nb0 = (tile / P.m_tiles) * BN + (int)rank * BN_CTA;
+      decode_in_place<MODE>(P, sB0 + s * B_BYTES, sWp0 + s * C::kWpBytes, lut_lane, t, nb0,
+                            ((it % kb_total) % P.k_blocks) * BK);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (t == 0) PACKR_TRACE_EVENT(7, it);
+      if (lane == 0) mbar_arrive_cluster(mapa(smem_u32(&bars->bfull[s]), 0));
     }
   } else if (C::kDecode) {
-    // ------------------------------------------------ weight decode (both CTAs)
+    // ------------------------------------------------ weight decode, register ring (both CTAs)
     const int t = threadIdx.x - C::kDecWarp0 * 32;
     const uint32_t lut_lane = smem_u32(sAux) + (uint32_t)lane * 4u;
     const uint32_t sB0 = smem_u32(sB);
@@ -573,6 +678,7 @@ __global__ void __launch_bounds__(Cfg<MODE>::kThreads, 1)
     if (total > 1) load(r1, 1);
     for (int it = 0; it < total; it += 3) {
       if (it + 2 < total) load(r2, it + 2);
+      if (t == 0) PACKR_TRACE_EVENT(11, it);
       process(r0, it);
       if (it + 1 >= total) break;
       if (it + 3 < total) load(r0, it + 3);
@@ -630,24 +736,36 @@ int make_map(CUtensorMap* m, const void* base, long long inner, long long rows, 
   return r == CUDA_SUCCESS ? PACKR_OK : PACKR_ERR_INVALID_ARGUMENT;
 }
 
-template <int MODE>
-int launch(Params P, const Maps& maps, cudaStream_t stream) {
-  using C = Cfg<MODE>;
+// u8 2-D map over [rows, inner] (row stride in bytes), no swizzle, box
+// {box_inner, box_rows}; out-of-range elements read as zero.
+int make_map_u8(CUtensorMap* m, const void* base, long long inner, long long rows, long long row_stride_bytes,
+                int box_inner, int box_rows) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return PACKR_ERR_CUDA;
+  if (!aligned(base, 16) || (row_stride_bytes & 15) != 0) return PACKR_ERR_ALIGNMENT;
+  if (inner <= 0 || rows <= 0) return PACKR_ERR_SHAPE;
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)row_stride_bytes};
+  cuuint32_t box[2] = {(cuuint32_t)box_inner, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? PACKR_OK : PACKR_ERR_INVALID_ARGUMENT;
+}
+
+template <int MODE, bool WTMA>
+int launch_impl(Params P, const Maps& maps, cudaStream_t stream) {
+  using C = Cfg<MODE, WTMA>;
   static std::once_flag attr_once[64];
   int dev = 0;
   cudaGetDevice(&dev);
   int attr_rc = 0;
   std::call_once(attr_once[dev & 63], [&] {
-    attr_rc = cudaFuncSetAttribute(packr_gemm_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    attr_rc = cudaFuncSetAttribute(packr_gemm_kernel<MODE, WTMA>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    C::kSmemBytes) != cudaSuccess;
   });
   if (attr_rc) return PACKR_ERR_CUDA;
-  P.w_vec = (P.ldw & 7) == 0 && aligned(P.W_f, 16) && aligned(P.W_p, 8);
-  P.out_vec = aligned(P.out, 16);
-  P.idx_vec = aligned(P.hist_idx, 16);
-  P.m_tiles = (P.Mg + 2 * BM - 1) / (2 * BM);
-  P.n_tiles = (P.Ng + BN - 1) / BN;
-  P.k_blocks = (P.Kg + BK - 1) / BK;
   const int tiles = P.m_tiles * P.n_tiles;
   if (tiles == 0) return PACKR_OK;
   const int max_pairs = sm_count() / 2;
@@ -664,11 +782,33 @@ int launch(Params P, const Maps& maps, cudaStream_t stream) {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, packr_gemm_kernel<MODE>, P, maps) != cudaSuccess) {
+  if (cudaLaunchKernelEx(&cfg, packr_gemm_kernel<MODE, WTMA>, P, maps) != cudaSuccess) {
     cudaGetLastError();
     return PACKR_ERR_LAUNCH;
   }
   return launch_status();
+}
+
+// Launches one GEMM.  Decode modes stage W_f / W_p by TMA when W's rows are
+// 16-byte multiples of u8 (N % 16 == 0) and both bases are 16-byte aligned;
+// otherwise the decode warps load them through a register ring.
+template <int MODE>
+int launch(Params P, Maps maps, cudaStream_t stream) {
+  P.w_vec = (P.ldw & 7) == 0 && aligned(P.W_f, 16) && aligned(P.W_p, 8);
+  P.out_vec = aligned(P.out, 16);
+  P.idx_vec = aligned(P.hist_idx, 16);
+  P.m_tiles = (P.Mg + 2 * BM - 1) / (2 * BM);
+  P.n_tiles = (P.Ng + BN - 1) / BN;
+  P.k_blocks = (P.Kg + BK - 1) / BK;
+  if (MODE == DW) return launch_impl<MODE, false>(P, maps, stream);
+  const bool wtma = (P.ldw & 15) == 0 && aligned(P.W_f, 16) && aligned(P.W_p, 16);
+  if (!wtma) return launch_impl<MODE, false>(P, maps, stream);
+  int st = make_map(&maps.wf, P.W_f, P.w_cols, P.w_rows, P.ldw * 2, MODE == FWD ? BK : BN_CTA);
+  if (st == PACKR_OK)
+    st = MODE == FWD ? make_map_u8(&maps.wp, P.W_p, P.w_cols, P.w_rows, P.ldw, BN_CTA, BK)
+                     : make_map_u8(&maps.wp, P.W_p, P.w_cols, P.w_rows, P.ldw, BK, BN_CTA);
+  if (st != PACKR_OK) return st;
+  return launch_impl<MODE, true>(P, maps, stream);
 }
 
 }  // namespace gemm

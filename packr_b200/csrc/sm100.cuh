@@ -183,9 +183,11 @@ __device__ __forceinline__ uint32_t mapa(uint32_t smem_addr, uint32_t rank) {
   return r;
 }
 
-// Arrive (release at cluster scope) on an mbarrier given by its shared::cluster address.
+// Arrive (default .release.cta semantics) on an mbarrier given by its
+// shared::cluster address, possibly in the peer CTA.  Writers of shared
+// memory that the tensor core reads issue fence.proxy.async before it.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
