@@ -69,9 +69,10 @@ constexpr int BK = 64, UK = 16;
 constexpr int MAX_STAGES = 6;
 constexpr int A_BYTES = BM * BK * 2;      // 16 KB
 constexpr int B_BYTES = BN_CTA * BK * 2;  // 16 KB
-constexpr int DEC_WARPS = 8;
+constexpr int DEC_WARPS = 8;           // decode warps, register-ring path (and the decode check)
+constexpr int DEC_WARPS_TMA = 8;       // decode warps, TMA-staged path
 constexpr int DEC_THREADS = DEC_WARPS * 32;
-constexpr int CHUNKS = BN_CTA * BK / 8 / DEC_THREADS;  // 4 chunks of 8 weights per thread per stage
+constexpr int CHUNKS = BN_CTA * BK / 8 / DEC_THREADS;  // chunks of 8 weights per thread per stage (ring path)
 constexpr int LUT_BYTES = 256 * 32 * 4;  // one u32 per (entry, lane)
 constexpr int HIST_COPIES = 4;  // lut-gradient histogram copies per epilogue warp (lane & 3)
 constexpr int ACC_COLS = BN;
@@ -95,8 +96,9 @@ struct Cfg {
   static constexpr int kEpiWarps = kDecode ? 4 : 8;
   static constexpr int kChunksPerEpiWarp = (BN / 32) / (kEpiWarps / 4);
   static constexpr int kDecWarp0 = 2 + kEpiWarps;             // first decode warp
-  static constexpr int kSignalWarp = kDecWarp0 + DEC_WARPS;   // decode-completion signaller (register ring only)
-  static constexpr int kWarps = 2 + kEpiWarps + (kDecode ? DEC_WARPS + (kWtma ? 0 : 1) : 0);
+  static constexpr int kDecWarps = kWtma ? DEC_WARPS_TMA : DEC_WARPS;
+  static constexpr int kSignalWarp = kDecWarp0 + kDecWarps;   // decode-completion signaller (register ring only)
+  static constexpr int kWarps = 2 + kEpiWarps + (kDecode ? kDecWarps + (kWtma ? 0 : 1) : 0);
   static constexpr int kThreads = kWarps * 32;
   static constexpr bool kAmn = MODE == DW;   // A stored MN-major in smem
   static constexpr bool kBmn = MODE != DX;   // B stored MN-major in smem
@@ -107,7 +109,7 @@ struct Cfg {
   static constexpr uint32_t kIdesc = idesc_bf16_f32(2 * BM, BN, kAmn, kBmn);
   static constexpr uint32_t kTxBytes = 2 * (kDecode ? A_BYTES : A_BYTES + B_BYTES);  // both CTAs
   static constexpr uint32_t kWTxBytes = B_BYTES + kWpBytes;                          // this CTA's W tiles
-  static constexpr uint32_t kBfullCount = kWtma ? 2 * DEC_WARPS : 2;
+  static constexpr uint32_t kBfullCount = kWtma ? 2 * kDecWarps : 2;
 };
 
 struct Params {
@@ -177,17 +179,18 @@ struct Chunks {
 };
 
 // FWD: the CTA's B half is 64 reduction rows x 128 columns: chunk i of
-//      thread t covers row k = t/16 + 16i and columns 8*(t%16) .. +7
-//      (W row = k, W columns = n).
+//      thread t (of NT decode threads) covers row k = t/16 + (NT/16)*i and
+//      columns 8*(t%16) .. +7 (W row = k, W columns = n).
 // DX : the B half is 128 output columns (W rows) x 64 reduction columns:
-//      chunk i covers B row r = t/8 + 32i and reduction columns 8*(t%8) .. +7.
-template <int MODE>
+//      chunk i covers B row r = t/8 + (NT/8)*i and reduction columns
+//      8*(t%8) .. +7.
+template <int MODE, int NT = DEC_THREADS>
 __device__ __forceinline__ void chunk_coords(int t, int i, int& brow, int& bcol8) {
   if (MODE == FWD) {
-    brow = (t >> 4) + 16 * i;
+    brow = (t >> 4) + (NT / 16) * i;
     bcol8 = t & 15;
   } else {
-    brow = (t >> 3) + 32 * i;
+    brow = (t >> 3) + (NT / 8) * i;
     bcol8 = t & 7;
   }
 }
@@ -279,15 +282,20 @@ __device__ __forceinline__ void decode_store(const Chunks& c, uint32_t b_stage, 
 // its swizzled layout, W_p in a row-major u8 tile (FWD: 64 rows x 128,
 // DX: 128 rows x 64).  Elements outside W (zero-filled by TMA) are stored as
 // zero rather than decoded.
-template <int MODE>
-__device__ __forceinline__ void decode_in_place(const Params& P, uint32_t b_stage, uint32_t wp_stage,
-                                                uint32_t lut_lane, int t, int nb0, int k0) {
+template <int MODE, int NT>
+__device__ __forceinline__ void decode_in_place(const Params& P, uint8_t* b_stage, const uint8_t* wp_stage,
+                                                const uint32_t* lut_lane, int t, int nb0, int k0) {
+  constexpr int NCH = BN_CTA * BK / 8 / NT;
+  uint4 f[NCH];
+  uint2 w[NCH];
+  int nv[NCH];
+  uint32_t off[NCH];
 #pragma unroll
-  for (int i = 0; i < CHUNKS; ++i) {
+  for (int i = 0; i < NCH; ++i) {  // all loads of the stage first
     int brow, bcol8;
-    chunk_coords<MODE>(t, i, brow, bcol8);
-    const uint32_t off = chunk_smem_off<MODE>(brow, bcol8);
-    const uint32_t wpoff = (uint32_t)(brow * (MODE == FWD ? BN_CTA : BK) + 8 * bcol8);
+    chunk_coords<MODE, NT>(t, i, brow, bcol8);
+    off[i] = chunk_smem_off<MODE>(brow, bcol8);
+    const int wpoff = brow * (MODE == FWD ? BN_CTA : BK) + 8 * bcol8;
     long long wr, wc;
     if (MODE == FWD) {
       wr = (long long)k0 + brow;
@@ -296,28 +304,29 @@ __device__ __forceinline__ void decode_in_place(const Params& P, uint32_t b_stag
       wr = (long long)nb0 + brow;
       wc = (long long)k0 + 8 * bcol8;
     }
-    const int nv = (wr < P.w_rows && wc < P.w_cols) ? (int)min(8ll, (long long)P.w_cols - wc) : 0;
-    uint32_t f[4], w[2];
-    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(f[0]), "=r"(f[1]), "=r"(f[2]), "=r"(f[3]) : "r"(b_stage + off));
-    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(w[0]), "=r"(w[1]) : "r"(wp_stage + wpoff));
+    nv[i] = (wr < P.w_rows && wc < P.w_cols) ? (int)min(8ll, (long long)P.w_cols - wc) : 0;
+    f[i] = *reinterpret_cast<const uint4*>(b_stage + off[i]);
+    w[i] = *reinterpret_cast<const uint2*>(wp_stage + wpoff);
+  }
+#pragma unroll
+  for (int i = 0; i < NCH; ++i) {
+    const uint32_t ww[2] = {w[i].x, w[i].y};
+    const uint32_t ff[4] = {f[i].x, f[i].y, f[i].z, f[i].w};
     uint32_t r[4];
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
-      const uint32_t word = w[p >> 1];
+      const uint32_t word = ww[p >> 1];
       const int sh = 16 * (p & 1);
-      const uint32_t e0 = ((word >> sh) & 0xFFu) << 7;
-      const uint32_t e1 = ((word >> (sh + 8)) & 0xFFu) << 7;
-      const uint32_t l = prmt(lut_fetch(lut_lane, e0), lut_fetch(lut_lane, e1), 0x5410u);
-      r[p] = bf16x2_add(f[p], l);
+      const uint32_t l0 = lut_lane[((word >> sh) & 0xFFu) * 32];
+      const uint32_t l1 = lut_lane[((word >> (sh + 8)) & 0xFFu) * 32];
+      r[p] = bf16x2_add(ff[p], prmt(l0, l1, 0x5410u));
     }
-    if (nv < 8) {
+    if (nv[i] < 8) {
 #pragma unroll
       for (int j = 0; j < 8; ++j)
-        if (j >= nv) r[j >> 1] &= (j & 1) ? 0x0000FFFFu : 0xFFFF0000u;
+        if (j >= nv[i]) r[j >> 1] &= (j & 1) ? 0x0000FFFFu : 0xFFFF0000u;
     }
-    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(b_stage + off), "r"(r[0]), "r"(r[1]),
-                 "r"(r[2]), "r"(r[3])
-                 : "memory");
+    *reinterpret_cast<uint4*>(b_stage + off[i]) = make_uint4(r[0], r[1], r[2], r[3]);
   }
 }
 
@@ -328,7 +337,9 @@ __global__ void __launch_bounds__(Cfg<MODE, WTMA>::kThreads, 1)
   using C = Cfg<MODE, WTMA>;
   constexpr int STAGES = C::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1024-byte aligned base for the 128-byte-swizzled tiles; offsetting the
+  // __shared__ array keeps the compiler emitting shared-memory accesses.
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
   uint8_t* sWp = smem + STAGES * (A_BYTES + B_BYTES);
@@ -377,11 +388,11 @@ __global__ void __launch_bounds__(Cfg<MODE, WTMA>::kThreads, 1)
     tmem_alloc_pair(&bars->tmem_base, TMEM_COLS);
     tmem_relinquish_pair();
   }
-  if (C::kDecode && warp >= C::kDecWarp0 && warp < C::kDecWarp0 + DEC_WARPS) {
+  if (C::kDecode && warp >= C::kDecWarp0 && warp < C::kDecWarp0 + C::kDecWarps) {
     // Lane-replicated bf16 lut: word (e*32 + l) holds bf16_rne(lut[e]) for lane l.
     uint32_t* lut_s = reinterpret_cast<uint32_t*>(sAux);
     const int dw = warp - C::kDecWarp0;
-    for (int e = dw; e < 256; e += DEC_WARPS) lut_s[e * 32 + lane] = f32_to_bf16_rne(__ldg(P.lut + e));
+    for (int e = dw; e < 256; e += C::kDecWarps) lut_s[e * 32 + lane] = f32_to_bf16_rne(__ldg(P.lut + e));
   }
   tc_fence_before();
   __syncwarp();
@@ -623,8 +634,7 @@ __global__ void __launch_bounds__(Cfg<MODE, WTMA>::kThreads, 1)
   } else if (C::kWtma) {
     // ------------------------------------------------ weight decode, TMA-staged (both CTAs)
     const int t = threadIdx.x - C::kDecWarp0 * 32;
-    const uint32_t lut_lane = smem_u32(sAux) + (uint32_t)lane * 4u;
-    const uint32_t sB0 = smem_u32(sB), sWp0 = smem_u32(sWp);
+    const uint32_t* lut_lane = reinterpret_cast<const uint32_t*>(sAux) + lane;
     const int my_tiles = pair < num_tiles ? (num_tiles - 1 - pair) / npairs + 1 : 0;
     const int total = my_tiles * kb_total;
     for (int it = 0; it < total; ++it) {
@@ -634,8 +644,8 @@ __global__ void __launch_bounds__(Cfg<MODE, WTMA>::kThreads, 1)
       if (t == 0) PACKR_TRACE_EVENT(6, it);
       const int tile = pair + (it / kb_total) * npairs;
       const int nb0 = (tile / P.m_tiles) * BN + (int)rank * BN_CTA;
-      decode_in_place<MODE>(P, sB0 + s * B_BYTES, sWp0 + s * C::kWpBytes, lut_lane, t, nb0,
-                            ((it % kb_total) % P.k_blocks) * BK);
+      decode_in_place<MODE, C::kDecWarps * 32>(P, sB + s * B_BYTES, sWp + s * C::kWpBytes, lut_lane, t, nb0,
+                                               ((it % kb_total) % P.k_blocks) * BK);
       fence_proxy_async_smem();
       __syncwarp();
       if (t == 0) PACKR_TRACE_EVENT(7, it);
@@ -823,7 +833,7 @@ namespace gemm {
 __global__ void __launch_bounds__(DEC_THREADS) decode_check_kernel(const Params P, uint16_t* __restrict__ out,
                                                                   int k_tiles, int n_tiles) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint32_t* lut_s = reinterpret_cast<uint32_t*>(smem);
   uint8_t* tile = smem + LUT_BYTES;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, t = threadIdx.x;
