@@ -124,6 +124,24 @@ int packr_lut_finalize(float* dlut, const float* dlut_sum, const int32_t* counts
 int packr_decode_bf16(const uint8_t* W_p, const uint16_t* W_f, const float* lut, uint16_t* out, int64_t K,
                       int64_t N, void* stream);
 
+/* packr_backward without a caller-provided workspace, for callers that cannot
+ * allocate device memory (a host runtime with a fixed device-memory budget
+ * and no allocator of its own, a binding that can pass tensors it was given
+ * but cannot obtain a temporary buffer).  No counterpart in the reference.
+ * Same arguments and results as packr_backward minus the workspace: the
+ * scratch is one static device array of PACKR_STATIC_SCRATCH_BYTES per GPU,
+ * held from the library's load until process exit.  Problems whose scratch
+ * need exceeds that size return PACKR_ERR_WORKSPACE before any launch (the
+ * need for bf16 x without PACKR_BWD_DW_SPLIT is about M*round8(N)*2 bytes).
+ * The first call on each device looks up the array's device address (make
+ * it before any stream capture).  Every call shares the array; calls that
+ * overlap on the GPU (different streams, different threads) race on it. */
+#define PACKR_STATIC_SCRATCH_BYTES (32u << 20)
+int packr_backward_static_scratch(const float* dY, const void* x, int x_dtype, const uint8_t* W_p,
+                                  const uint16_t* W_f, const float* lut, const int32_t* lut_counts, void* dX,
+                                  uint16_t* dW_f, float* dlut, uint16_t* dbias, int64_t M, int64_t K, int64_t N,
+                                  int flags, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

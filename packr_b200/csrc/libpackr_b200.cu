@@ -6,3 +6,4 @@
 #include "prep.cu"
 #include "gemm.cu"
 #include "linear.cu"
+#include "static_scratch.cu"
