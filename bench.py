@@ -263,7 +263,8 @@ def bench_adam8(args, world, rank, peaks, peak_kind):
                    "lr": 2e-5, "betas": [0.9, 0.999], "eps": 1e-8, "weight_decay": 0.01, "block": 256,
                    "l2": "inputs larger than L2 (1.1 GB per step)", "parallelism": f"replicas x{world}"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None,
+                     "frac": round(achieved / peaks["hbm_gbs"], 4),
+                     "traffic": load_traffic("adam8_multi_kernel", "adam8_110M"),
                      "peak_source": f"{peak_kind} hbm_gbs", "kernel": "adam8_multi_kernel",
                      "algorithmic_bytes_per_launch": n * ADAM_BYTES_PER_PARAM},
         "e2e": {"value": round(e2e_val, 3), "unit": "Gparam/s", "h2d_bytes_per_step": 2 * n,
