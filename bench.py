@@ -327,21 +327,20 @@ def cpu_linear_port(budget_s: float, M: int = 1024):
 def bench_ffn(args, world, rank, peaks, peak_kind):
     from packr_b200 import PackRLinear
     from packr_b200 import kernel as K
+    from packr_b200.dp import ShardedAdam8
     M = args.tokens
     dev = torch.device("cuda", torch.cuda.current_device())
     layers, xs, dys = [], [], []
     for i, (name, k, n) in enumerate(FFN_LAYERS):
+        # identical parameters on every rank (data parallel)
         lay = PackRLinear.synthetic(k, n, bias=False, device=dev, seed=100 + i, lut_std=0.02 * math.sqrt(768 / k),
                                     wf_std=0.002 * math.sqrt(768 / k))
-        g = torch.Generator(device=dev).manual_seed(1000 * rank + i)
+        g = torch.Generator(device=dev).manual_seed(1000 * rank + i)  # each rank its own micro-batch
         xs.append(torch.randn(M, k, generator=g, device=dev).to(torch.bfloat16).requires_grad_(True))
         dys.append(torch.randn(M, n, generator=g, device=dev).to(torch.bfloat16).float())
         layers.append(lay)
-
-    def step():
-        for lay, x, dy in zip(layers, xs, dys):
-            out = lay(x)
-            out.backward(dy)
+    params = [p for lay in layers for p in (lay.W_f, lay.lut)]
+    opt = ShardedAdam8(params, lr=2e-5, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01)
 
     def zero():
         for lay, x in zip(layers, xs):
@@ -349,29 +348,33 @@ def bench_ffn(args, world, rank, peaks, peak_kind):
             lay.lut.grad = None
             x.grad = None
 
-    def step_z():
+    def fwd_bwd():
         zero()
-        step()
+        for lay, x, dy in zip(layers, xs, dys):
+            lay(x).backward(dy)
+
+    def step():
+        fwd_bwd()
+        opt.step()
 
     with ClockSampler(torch.cuda.current_device()) as clk:
-        total_ms, per = timed(step_z, args.steps, args.warmup, world, warm_seconds=1.5)
+        total_ms, per = timed(step, args.steps, args.warmup, world, warm_seconds=1.5)
     ms_step = total_ms / args.steps
     flops = ffn_flops(M)
     value = world * flops / (ms_step * 1e-3) / 1e12
+    fb_total, _ = timed(fwd_bwd, args.steps, 2, world)
+    fb_ms = fb_total / args.steps
     # dominant kernel: the forward GEMM of the gate layer, timed alone
     lay, x = layers[0], xs[0].detach()
     fwd = lambda: K.forward(x, lay.W_p, lay.W_f, lay.lut, None)
-    f_total, f_per = timed(fwd, max(args.steps, 10), 3, 1)
+    _, f_per = timed(fwd, max(args.steps, 10), 3, 1)
     f_ms = statistics.mean(f_per)
     f_flops = 2.0 * M * FFN_HIDDEN * FFN_INTER
     achieved = f_flops / (f_ms * 1e-3) / 1e12
-    # phase split of one layer (gate): forward vs backward launches
-    out0 = K.forward(x, lay.W_p, lay.W_f, lay.lut, None)
     cnt = lay.lut_counts()
     bwd = lambda: K.backward(dys[0], x, lay.W_p, lay.W_f, lay.lut, cnt, True, True, True, False)
-    b_total, b_per = timed(bwd, max(args.steps, 10), 3, 1)
-    del out0
-    # end to end: inputs from pinned host memory, dlut read back each step
+    _, b_per = timed(bwd, max(args.steps, 10), 3, 1)
+    # end to end: every step copies x and dY from pinned host memory and reads dlut back
     hx = [t.detach().cpu().pin_memory() for t in xs]
     hdy = [t.cpu().pin_memory() for t in dys]
     hres = torch.empty(len(layers), 256, dtype=torch.float32, pin_memory=True)
@@ -386,6 +389,7 @@ def bench_ffn(args, world, rank, peaks, peak_kind):
             xi = dx_in[i].detach().requires_grad_(True)
             lay(xi).backward(ddy_in[i])
             hres[i].copy_(lay.lut.grad, non_blocking=True)
+        opt.step()
     e2e_total, _ = timed(e2e_step, args.steps, max(args.warmup, 1), world)
     e2e_val = world * flops / (e2e_total / args.steps * 1e-3) / 1e12
     h2d = sum(t.numel() * t.element_size() for t in hx) + sum(t.numel() * t.element_size() for t in hdy)
@@ -394,10 +398,15 @@ def bench_ffn(args, world, rank, peaks, peak_kind):
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 operands, f32 accumulate",
         "data": "synthetic (seeded; bf16 x ~ N(0,1), bf16-valued f32 dY ~ N(0,1), uniform W_p, fan-in scaled lut/W_f)",
-        "config": {"workload": f"ffn: Llama-7B FFN gate/up/down (4096<->11008) PackRLinear fwd+bwd, M={M} tokens per GPU",
+        "config": {"workload": f"ffn: Llama-7B FFN gate/up/down (4096<->11008) PackRLinear training step, "
+                               f"M={M} tokens per GPU",
+                   "step": "forward + backward of the three layers, then the data-parallel 8-bit AdamW update "
+                           "(gradient reduce-scatter, AdamW on this rank's 1/N state shard, W_f/lut all-gather; "
+                           "no collectives at N=1); value counts the 6*M*K*N GEMM FLOPs",
                    "hidden": FFN_HIDDEN, "intermediate": FFN_INTER, "tokens_per_gpu": M,
                    "flops_per_step_per_gpu": flops, "l2": "inputs larger than L2 (~0.9 GB of operands per step)",
-                   "parallelism": "data-parallel replicas" if world > 1 else "single GPU"},
+                   "parallelism": f"dp{world}, ZeRO-1 sharded 8-bit optimizer state"},
+        "fwd_bwd_only": {"tflops": round(world * flops / (fb_ms * 1e-3) / 1e12, 2), "ms_per_step": round(fb_ms, 4)},
         "phases_ms_gate_layer": {"forward": round(f_ms, 4), "backward": round(statistics.mean(b_per), 4)},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peaks["bf16_tflops"],
                      "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
@@ -407,7 +416,7 @@ def bench_ffn(args, world, rank, peaks, peak_kind):
                      "algorithmic_flops_per_launch": f_flops},
         "e2e": {"value": round(e2e_val, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": hres.numel() * 4},
-        "gpu_launches": args.steps * len(layers) * 5,
+        "gpu_launches": args.steps * (len(layers) * 5 + len(opt.groups)),
         "clocks": clk.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
