@@ -84,16 +84,27 @@ enum Mode { FWD = 0, DX = 1, DW = 2 };
 // WTMA (decode modes): W_f and W_p tiles arrive by TMA into shared memory
 // and are decoded in place; otherwise (rows of W_p not a multiple of 16
 // bytes) the decode warps load them into a register ring.
-template <int MODE, bool WTMA>
+// MSUB: output rows per pair tile = 256 * MSUB.  With MSUB = 2 every decoded
+// B stage feeds two pair MMAs (two 256-row subtiles), halving the decode and
+// lut traffic per FLOP; the two subtiles' accumulators then fill TMEM (no
+// double buffering across tiles, but each subtile is released separately).
+template <int MODE, bool WTMA, int MSUB>
 struct Cfg {
   static constexpr bool kDecode = MODE != DW;
   static constexpr bool kWtma = kDecode && WTMA;
-  static constexpr int kStages = kWtma ? 4 : 6;
+  static constexpr int kMSub = MSUB;
+  static constexpr int kStages = kWtma ? (MSUB == 2 ? 3 : 4) : 6;
+  static constexpr int kABytes = MSUB * A_BYTES;            // A subtiles per stage
   static constexpr int kWpBytes = kWtma ? BN_CTA * BK : 0;  // u8 W_p tile per stage
-  static constexpr int kStageBytes = A_BYTES + B_BYTES + kWpBytes;
+  static constexpr int kStageBytes = kABytes + B_BYTES + kWpBytes;
   // DW's histogram epilogue is the heavier one: two warps per TMEM lane
   // quarter, each taking half of the tile's columns.
   static constexpr int kEpiWarps = kDecode ? 4 : 8;
+  // TMA-staged decode modes pass each 32-row output block through a 4 KB
+  // per-warp shared-memory buffer, so that global stores cover whole rows
+  // segments of 128 (f32) or 64 (bf16) bytes instead of 16 bytes per row.
+  static constexpr bool kStageOut = kWtma;
+  static constexpr int kStgBytes = kStageOut ? kEpiWarps * 4096 : 0;
   static constexpr int kChunksPerEpiWarp = (BN / 32) / (kEpiWarps / 4);
   static constexpr int kDecWarp0 = 2 + kEpiWarps;             // first decode warp
   static constexpr int kDecWarps = kWtma ? DEC_WARPS_TMA : DEC_WARPS;
@@ -103,11 +114,11 @@ struct Cfg {
   static constexpr bool kAmn = MODE == DW;   // A stored MN-major in smem
   static constexpr bool kBmn = MODE != DX;   // B stored MN-major in smem
   static constexpr int kHistBytes = kEpiWarps * HIST_COPIES * 256 * 4;
-  static constexpr int kAuxBytes = kDecode ? LUT_BYTES : kHistBytes;
+  static constexpr int kAuxBytes = kDecode ? LUT_BYTES + kStgBytes : kHistBytes;
   static constexpr int kBarOff = kStages * kStageBytes + kAuxBytes;
   static constexpr int kSmemBytes = kBarOff + 256 + 1024;  // barriers + alignment slack
   static constexpr uint32_t kIdesc = idesc_bf16_f32(2 * BM, BN, kAmn, kBmn);
-  static constexpr uint32_t kTxBytes = 2 * (kDecode ? A_BYTES : A_BYTES + B_BYTES);  // both CTAs
+  static constexpr uint32_t kTxBytes = 2 * (kDecode ? kABytes : A_BYTES + B_BYTES);  // both CTAs
   static constexpr uint32_t kWTxBytes = B_BYTES + kWpBytes;                          // this CTA's W tiles
   static constexpr uint32_t kBfullCount = kWtma ? 2 * kDecWarps : 2;
 };
@@ -229,9 +240,12 @@ __device__ __forceinline__ void decode_load(Chunks& c, const Params& P, int t, i
       c.wp[i] = __ldg(reinterpret_cast<const uint2*>(P.W_p + off));
     } else {
       uint32_t f[4] = {0, 0, 0, 0}, p[2] = {0, 0};
-      for (int j = 0; j < nv; ++j) {
-        f[j >> 1] |= (uint32_t)__ldg(P.W_f + off + j) << (16 * (j & 1));
-        p[j >> 2] |= (uint32_t)__ldg(P.W_p + off + j) << (8 * (j & 3));
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (j < nv) {
+          f[j >> 1] |= (uint32_t)__ldg(P.W_f + off + j) << (16 * (j & 1));
+          p[j >> 2] |= (uint32_t)__ldg(P.W_p + off + j) << (8 * (j & 3));
+        }
       }
       c.wf[i] = make_uint4(f[0], f[1], f[2], f[3]);
       c.wp[i] = make_uint2(p[0], p[1]);
@@ -330,19 +344,60 @@ __device__ __forceinline__ void decode_in_place(const Params& P, uint8_t* b_stag
   }
 }
 
+// Row-coalesced store of a warp's 32 x 32 output block.  On entry lane l
+// holds row r0 + l: 32 values of ESIZE bytes packed in v (ESIZE 4: 32 words,
+// ESIZE 2: 16 words of bf16 pairs).  The rows are written to the warp's
+// staging buffer (RB = 32 * ESIZE bytes per row, 16-byte chunks XOR-swizzled
+// by row so both phases are free of bank conflicts), then read back so that
+// RB / 16 consecutive lanes store one row segment and each store instruction
+// writes 512 contiguous-by-row bytes (4 rows of 128 B or 8 rows of 64 B).
+// Rows at or beyond m_limit are skipped;
+// columns gn0 .. gn0 + 31 must lie inside the output.
+template <int ESIZE>
+__device__ __forceinline__ void store_rows_staged(uint32_t stg, const float* v, void* out, int r0, int m_limit,
+                                                  long long ld, int gn0) {
+  constexpr int RB = 32 * ESIZE;      // bytes per row
+  constexpr int CPR = RB / 16;        // 16-byte chunks per row (8 or 4)
+  constexpr int RPI = 32 / CPR;       // rows per store instruction (4 or 8)
+  const int lane = threadIdx.x & 31;
+  const int sw = ESIZE == 4 ? (lane & 7) : ((lane >> 1) & 3);
+#pragma unroll
+  for (int j = 0; j < CPR; ++j)
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(stg + (uint32_t)(lane * RB + ((j ^ sw) << 4))),
+                 "r"(__float_as_uint(v[4 * j])), "r"(__float_as_uint(v[4 * j + 1])), "r"(__float_as_uint(v[4 * j + 2])),
+                 "r"(__float_as_uint(v[4 * j + 3]))
+                 : "memory");
+  __syncwarp();
+  const int jc = lane % CPR;
+#pragma unroll
+  for (int i = 0; i < CPR; ++i) {
+    const int r = i * RPI + lane / CPR;
+    const int rsw = ESIZE == 4 ? (r & 7) : ((r >> 1) & 3);
+    uint4 d;
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(d.x), "=r"(d.y), "=r"(d.z), "=r"(d.w)
+                 : "r"(stg + (uint32_t)(r * RB + ((jc ^ rsw) << 4)))
+                 : "memory");
+    const long long gr = (long long)r0 + r;
+    if (gr < m_limit)
+      __stcs(reinterpret_cast<uint4*>(static_cast<uint8_t*>(out) + (gr * ld + gn0) * ESIZE + jc * 16), d);
+  }
+  __syncwarp();
+}
+
 // ------------------------------------------------------------------ kernel
-template <int MODE, bool WTMA>
-__global__ void __launch_bounds__(Cfg<MODE, WTMA>::kThreads, 1)
+template <int MODE, bool WTMA, int MSUB>
+__global__ void __launch_bounds__(Cfg<MODE, WTMA, MSUB>::kThreads, 1)
     packr_gemm_kernel(const Params P, const __grid_constant__ Maps maps) {
-  using C = Cfg<MODE, WTMA>;
+  using C = Cfg<MODE, WTMA, MSUB>;
   constexpr int STAGES = C::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte aligned base for the 128-byte-swizzled tiles; offsetting the
   // __shared__ array keeps the compiler emitting shared-memory accesses.
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* sA = smem;
-  uint8_t* sB = smem + STAGES * A_BYTES;
-  uint8_t* sWp = smem + STAGES * (A_BYTES + B_BYTES);
+  uint8_t* sB = smem + STAGES * C::kABytes;
+  uint8_t* sWp = sB + STAGES * B_BYTES;
   uint8_t* sAux = smem + STAGES * C::kStageBytes;
   Bars* bars = reinterpret_cast<Bars*>(smem + C::kBarOff);
   volatile int* abort_flag = &bars->abort;
@@ -406,7 +461,7 @@ __global__ void __launch_bounds__(Cfg<MODE, WTMA>::kThreads, 1)
       int it = 0;
       bool ok = true;
       for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
-        const int m0 = (tile % P.m_tiles) * (2 * BM) + (int)rank * BM;
+        const int m0 = (tile % P.m_tiles) * (2 * BM * MSUB) + (int)rank * BM;
         const int n0 = (tile / P.m_tiles) * BN + (int)rank * BN_CTA;
         for (int kk = 0; kk < kb_total; ++kk, ++it) {
           const int s = it % STAGES;
@@ -417,7 +472,7 @@ __global__ void __launch_bounds__(Cfg<MODE, WTMA>::kThreads, 1)
           const int k0 = (kk % P.k_blocks) * BK;
           if (rank == 0) mbar_arrive_expect_tx(&bars->full[s], C::kTxBytes);
           const uint32_t fbar = mapa(smem_u32(&bars->full[s]), 0);
-          uint8_t* a_dst = sA + s * A_BYTES;
+          uint8_t* a_dst = sA + s * C::kABytes;
           if (MODE == DW) {
             tma_load_2d_pair(a_dst, &maps.a[seg], fbar, m0, k0);
             tma_load_2d_pair(a_dst + 8192, &maps.a[seg], fbar, m0 + 64, k0);
@@ -425,7 +480,9 @@ __global__ void __launch_bounds__(Cfg<MODE, WTMA>::kThreads, 1)
             tma_load_2d_pair(b_dst, &maps.b[seg], fbar, n0, k0);
             tma_load_2d_pair(b_dst + 8192, &maps.b[seg], fbar, n0 + 64, k0);
           } else {
-            tma_load_2d_pair(a_dst, &maps.a[seg], fbar, k0, m0);
+#pragma unroll
+            for (int sub = 0; sub < MSUB; ++sub)
+              tma_load_2d_pair(a_dst + sub * A_BYTES, &maps.a[seg], fbar, k0, m0 + sub * 2 * BM);
             if (C::kWtma) {
               // this CTA's W_f / W_p tiles (its 128 columns of B) onto its own wfull
               const int nb0 = (tile / P.m_tiles) * BN + (int)rank * BN_CTA;
@@ -453,12 +510,13 @@ __global__ void __launch_bounds__(Cfg<MODE, WTMA>::kThreads, 1)
       bool ok = true;
       const uint32_t sA0 = smem_u32(sA), sB0 = smem_u32(sB);
       for (int tile = pair; tile < num_tiles && ok; tile += npairs, ++t_local) {
-        const int acc = t_local & 1;
-        const uint32_t aph = (uint32_t)(t_local >> 1) & 1u;
+        // accumulator slots (256 TMEM columns each): MSUB = 1 alternates the
+        // two slots between tiles; MSUB = 2 uses slot `sub` for subtile `sub`
+        const int acc = MSUB == 1 ? (t_local & 1) : 0;
+        const uint32_t aph = MSUB == 1 ? ((uint32_t)(t_local >> 1) & 1u) : ((uint32_t)t_local & 1u);
         if (!mbar_wait(&bars->tempty[acc], aph ^ 1u, abort_flag)) { ok = false; break; }
         PACKR_TRACE_EVENT(3, t_local);
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * ACC_COLS);
         for (int kk = 0; kk < kb_total; ++kk, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
@@ -467,18 +525,34 @@ __global__ void __launch_bounds__(Cfg<MODE, WTMA>::kThreads, 1)
           if (C::kDecode && !mbar_wait(&bars->bfull[s], ph, abort_flag)) { ok = false; break; }
           PACKR_TRACE_EVENT(2, it);
           tc_fence_after();
-          const uint32_t a_s = sA0 + s * A_BYTES, b_s = sB0 + s * B_BYTES;
+          const uint32_t a_s = sA0 + s * C::kABytes, b_s = sB0 + s * B_BYTES;
 #pragma unroll
-          for (int k = 0; k < BK / UK; ++k) {
-            const uint64_t ad = C::kAmn ? sdesc_sw128(a_s + k * 2048, 8192, 1024) : sdesc_sw128(a_s + k * 32, 16, 1024);
-            const uint64_t bd = C::kBmn ? sdesc_sw128(b_s + k * 2048, 8192, 1024) : sdesc_sw128(b_s + k * 32, 16, 1024);
-            umma_bf16_pair(d_tmem, ad, bd, C::kIdesc, (kk | k) != 0 ? 1u : 0u);
+          for (int sub = 0; sub < MSUB; ++sub) {
+            if (sub == 1 && kk == 0) {  // subtile 1's accumulator is released after subtile 0's
+              if (!mbar_wait(&bars->tempty[1], aph ^ 1u, abort_flag)) { ok = false; break; }
+              tc_fence_after();
+            }
+            const uint32_t a_sub = a_s + sub * A_BYTES;
+            const uint32_t d_tmem = tmem_base + (uint32_t)((MSUB == 1 ? acc : sub) * ACC_COLS);
+#pragma unroll
+            for (int k = 0; k < BK / UK; ++k) {
+              const uint64_t bd = C::kBmn ? sdesc_sw128(b_s + k * 2048, 8192, 1024) : sdesc_sw128(b_s + k * 32, 16, 1024);
+              const uint64_t ad = C::kAmn ? sdesc_sw128(a_sub + k * 2048, 8192, 1024) : sdesc_sw128(a_sub + k * 32, 16, 1024);
+              umma_bf16_pair(d_tmem, ad, bd, C::kIdesc, (kk | k) != 0 ? 1u : 0u);
+            }
+            // subtile 0 complete: its drain overlaps subtile 1's last MMAs
+            if (MSUB == 2 && sub == 0 && kk == kb_total - 1) umma_commit_pair(&bars->tfull[0], PAIR_MASK);
           }
+          if (!ok) break;
           umma_commit_pair(&bars->empty[s], PAIR_MASK);
           PACKR_TRACE_EVENT(10, it);
         }
         if (!ok) break;
-        umma_commit_pair(&bars->tfull[acc], PAIR_MASK);
+        if (MSUB == 1) {
+          umma_commit_pair(&bars->tfull[acc], PAIR_MASK);
+        } else {
+          umma_commit_pair(&bars->tfull[1], PAIR_MASK);
+        }
       }
       umma_commit_pair(&bars->drain, PAIR_MASK);
     }
@@ -490,11 +564,12 @@ __global__ void __launch_bounds__(Cfg<MODE, WTMA>::kThreads, 1)
     const uint32_t tempty0 = mapa(smem_u32(&bars->tempty[0]), 0);
     const uint32_t tempty1 = mapa(smem_u32(&bars->tempty[1]), 0);
     const uint32_t hist_lane = smem_u32(sAux) + (uint32_t)(((warp - 2) * HIST_COPIES + (lane & 3)) * 1024);
+    const uint32_t stg = smem_u32(sAux) + (uint32_t)(LUT_BYTES + (warp - 2) * 4096);
     // DW: the W_p bytes of the next tile's chunks are fetched before its
     // accumulator is ready (they do not depend on it)
     uint4 wpa[C::kChunksPerEpiWarp], wpb[C::kChunksPerEpiWarp];
     auto fetch_idx = [&](int tile) {
-      const long long gm = (long long)((tile % P.m_tiles) * (2 * BM) + (int)rank * BM + row);
+      const long long gm = (long long)((tile % P.m_tiles) * (2 * BM * MSUB) + (int)rank * BM + row);
       const int n0 = (tile / P.m_tiles) * BN;
 #pragma unroll
       for (int c = 0; c < C::kChunksPerEpiWarp; ++c) {
@@ -508,7 +583,9 @@ __global__ void __launch_bounds__(Cfg<MODE, WTMA>::kThreads, 1)
             const uint4 b = __ldg(reinterpret_cast<const uint4*>(ip + 16));
             w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w; w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
           } else {
-            for (int j = 0; j < nval; ++j) w[j >> 2] |= (uint32_t)__ldg(ip + j) << (8 * (j & 3));
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < nval) w[j >> 2] |= (uint32_t)__ldg(ip + j) << (8 * (j & 3));
           }
         }
         wpa[c] = make_uint4(w[0], w[1], w[2], w[3]);
@@ -518,14 +595,16 @@ __global__ void __launch_bounds__(Cfg<MODE, WTMA>::kThreads, 1)
     const bool want_hist = MODE == DW && P.hist_idx != nullptr;
     if (want_hist && pair < num_tiles) fetch_idx(pair);
     int t_local = 0;
-    for (int tile = pair; tile < num_tiles; tile += npairs, ++t_local) {
-      const int acc = t_local & 1;
-      const uint32_t aph = (uint32_t)(t_local >> 1) & 1u;
+    bool alive = true;
+    for (int tile = pair; tile < num_tiles && alive; tile += npairs, ++t_local)
+    for (int sub = 0; sub < MSUB; ++sub) {
+      const int acc = MSUB == 1 ? (t_local & 1) : sub;
+      const uint32_t aph = MSUB == 1 ? ((uint32_t)(t_local >> 1) & 1u) : ((uint32_t)t_local & 1u);
       // every lane waits; the warp proceeds only if all lanes saw the phase
-      if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bars->tfull[acc], aph, abort_flag))) break;
+      if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bars->tfull[acc], aph, abort_flag))) { alive = false; break; }
       if (warp == 2 && lane == 0) PACKR_TRACE_EVENT(4, t_local);
       tc_fence_after();
-      const int m0 = (tile % P.m_tiles) * (2 * BM) + (int)rank * BM;
+      const int m0 = (tile % P.m_tiles) * (2 * BM * MSUB) + sub * 2 * BM + (int)rank * BM;
       const int n0 = (tile / P.m_tiles) * BN;
       const long long gm = (long long)m0 + row;
       const bool row_ok = gm < P.Mg;
@@ -536,7 +615,9 @@ __global__ void __launch_bounds__(Cfg<MODE, WTMA>::kThreads, 1)
         tmem_ld_32x32b_x32(tmem_base + (uint32_t)(acc * ACC_COLS + cc * 32) + ((uint32_t)(q * 32) << 16), v);
         tmem_ld_wait();
         const int gn0 = n0 + cc * 32;
-        if (!row_ok || gn0 >= P.Ng) continue;
+        // warp-uniform skip; the staged stores are collective, the others per row
+        if (gn0 >= P.Ng || m0 + q * 32 >= P.Mg) continue;
+        if (!C::kStageOut && !row_ok) continue;
         const int nval = min(32, P.Ng - gn0);
         if (MODE == FWD) {
           float* o = static_cast<float*>(P.out) + gm * P.ld_out + gn0;
@@ -546,17 +627,26 @@ __global__ void __launch_bounds__(Cfg<MODE, WTMA>::kThreads, 1)
           if (P.bias != nullptr) {
             if (P.bias_f32) {
               const float* bp = static_cast<const float*>(P.bias) + gn0;
-              for (int j = 0; j < nval; ++j) f[j] = __fadd_rn(f[j], __ldg(bp + j));
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (j < nval) f[j] = __fadd_rn(f[j], __ldg(bp + j));
             } else {
               const uint16_t* bp = static_cast<const uint16_t*>(P.bias) + gn0;
-              for (int j = 0; j < nval; ++j) f[j] = __fadd_rn(f[j], bf16_to_f32(__ldg(bp + j)));
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (j < nval) f[j] = __fadd_rn(f[j], bf16_to_f32(__ldg(bp + j)));
             }
           }
-          if (nval == 32 && (P.ld_out & 3) == 0 && P.out_vec) {
+          if (C::kStageOut && nval == 32 && (P.ld_out & 3) == 0 && P.out_vec) {
+            store_rows_staged<4>(stg, f, P.out, m0 + q * 32, P.Mg, P.ld_out, gn0);
+          } else if (!row_ok) {
+          } else if (nval == 32 && (P.ld_out & 3) == 0 && P.out_vec) {
 #pragma unroll
             for (int j = 0; j < 32; j += 4) __stcs(reinterpret_cast<float4*>(o + j), make_float4(f[j], f[j + 1], f[j + 2], f[j + 3]));
           } else {
-            for (int j = 0; j < nval; ++j) o[j] = f[j];
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < nval) o[j] = f[j];
           }
         } else {  // DX: bf16(acc) as bf16 or f32;  DW: bf16(acc) (+ histogram)
           uint32_t h[16];
@@ -565,23 +655,39 @@ __global__ void __launch_bounds__(Cfg<MODE, WTMA>::kThreads, 1)
           if (P.out != nullptr) {
             if (MODE == DX && P.out_f32) {
               float* o = static_cast<float*>(P.out) + gm * P.ld_out + gn0;
-              if (nval == 32 && (P.ld_out & 3) == 0 && P.out_vec) {
+              if (C::kStageOut && nval == 32 && (P.ld_out & 3) == 0 && P.out_vec) {
+                float f[32];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                  f[2 * j] = __uint_as_float(h[j] << 16);
+                  f[2 * j + 1] = __uint_as_float(h[j] & 0xFFFF0000u);
+                }
+                store_rows_staged<4>(stg, f, P.out, m0 + q * 32, P.Mg, P.ld_out, gn0);
+              } else if (!row_ok) {
+              } else if (nval == 32 && (P.ld_out & 3) == 0 && P.out_vec) {
 #pragma unroll
                 for (int j = 0; j < 16; j += 2)
                   __stcs(reinterpret_cast<float4*>(o + 2 * j),
                          make_float4(__uint_as_float(h[j] << 16), __uint_as_float(h[j] & 0xFFFF0000u),
                                      __uint_as_float(h[j + 1] << 16), __uint_as_float(h[j + 1] & 0xFFFF0000u)));
               } else {
-                for (int j = 0; j < nval; ++j) o[j] = bf16_to_f32((h[j >> 1] >> (16 * (j & 1))) & 0xFFFFu);
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (j < nval) o[j] = bf16_to_f32((h[j >> 1] >> (16 * (j & 1))) & 0xFFFFu);
               }
             } else {
               uint16_t* o = static_cast<uint16_t*>(P.out) + gm * P.ld_out + gn0;
-              if (nval == 32 && (P.ld_out & 7) == 0 && P.out_vec) {
+              if (C::kStageOut && nval == 32 && (P.ld_out & 7) == 0 && P.out_vec) {
+                store_rows_staged<2>(stg, reinterpret_cast<const float*>(h), P.out, m0 + q * 32, P.Mg, P.ld_out, gn0);
+              } else if (!row_ok) {
+              } else if (nval == 32 && (P.ld_out & 7) == 0 && P.out_vec) {
 #pragma unroll
                 for (int j = 0; j < 16; j += 4)
                   __stcs(reinterpret_cast<uint4*>(o + 2 * j), make_uint4(h[j], h[j + 1], h[j + 2], h[j + 3]));
               } else {
-                for (int j = 0; j < nval; ++j) o[j] = (uint16_t)(h[j >> 1] >> (16 * (j & 1)));
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (j < nval) o[j] = (uint16_t)(h[j >> 1] >> (16 * (j & 1)));
               }
             }
           }
@@ -764,18 +870,19 @@ int make_map_u8(CUtensorMap* m, const void* base, long long inner, long long row
   return r == CUDA_SUCCESS ? PACKR_OK : PACKR_ERR_INVALID_ARGUMENT;
 }
 
-template <int MODE, bool WTMA>
+template <int MODE, bool WTMA, int MSUB = 1>
 int launch_impl(Params P, const Maps& maps, cudaStream_t stream) {
-  using C = Cfg<MODE, WTMA>;
+  using C = Cfg<MODE, WTMA, MSUB>;
   static std::once_flag attr_once[64];
   int dev = 0;
   cudaGetDevice(&dev);
   int attr_rc = 0;
   std::call_once(attr_once[dev & 63], [&] {
-    attr_rc = cudaFuncSetAttribute(packr_gemm_kernel<MODE, WTMA>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    attr_rc = cudaFuncSetAttribute(packr_gemm_kernel<MODE, WTMA, MSUB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    C::kSmemBytes) != cudaSuccess;
   });
   if (attr_rc) return PACKR_ERR_CUDA;
+  P.m_tiles = (P.Mg + 2 * BM * MSUB - 1) / (2 * BM * MSUB);
   const int tiles = P.m_tiles * P.n_tiles;
   if (tiles == 0) return PACKR_OK;
   const int max_pairs = sm_count() / 2;
@@ -792,7 +899,7 @@ int launch_impl(Params P, const Maps& maps, cudaStream_t stream) {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, packr_gemm_kernel<MODE, WTMA>, P, maps) != cudaSuccess) {
+  if (cudaLaunchKernelEx(&cfg, packr_gemm_kernel<MODE, WTMA, MSUB>, P, maps) != cudaSuccess) {
     cudaGetLastError();
     return PACKR_ERR_LAUNCH;
   }
@@ -801,16 +908,18 @@ int launch_impl(Params P, const Maps& maps, cudaStream_t stream) {
 
 // Launches one GEMM.  Decode modes stage W_f / W_p by TMA when W's rows are
 // 16-byte multiples of u8 (N % 16 == 0) and both bases are 16-byte aligned;
-// otherwise the decode warps load them through a register ring.
+// otherwise the decode warps load them through a register ring.  TMA-staged
+// decode with more than 256 output rows uses 512-row pair tiles.
 template <int MODE>
 int launch(Params P, Maps maps, cudaStream_t stream) {
   P.w_vec = (P.ldw & 7) == 0 && aligned(P.W_f, 16) && aligned(P.W_p, 8);
   P.out_vec = aligned(P.out, 16);
   P.idx_vec = aligned(P.hist_idx, 16);
-  P.m_tiles = (P.Mg + 2 * BM - 1) / (2 * BM);
   P.n_tiles = (P.Ng + BN - 1) / BN;
   P.k_blocks = (P.Kg + BK - 1) / BK;
-  if (MODE == DW) return launch_impl<MODE, false>(P, maps, stream);
+  if constexpr (MODE == DW) {
+    return launch_impl<MODE, false>(P, maps, stream);
+  } else {
   const bool wtma = (P.ldw & 15) == 0 && aligned(P.W_f, 16) && aligned(P.W_p, 16);
   if (!wtma) return launch_impl<MODE, false>(P, maps, stream);
   int st = make_map(&maps.wf, P.W_f, P.w_cols, P.w_rows, P.ldw * 2, MODE == FWD ? BK : BN_CTA);
@@ -818,7 +927,10 @@ int launch(Params P, Maps maps, cudaStream_t stream) {
     st = MODE == FWD ? make_map_u8(&maps.wp, P.W_p, P.w_cols, P.w_rows, P.ldw, BN_CTA, BK)
                      : make_map_u8(&maps.wp, P.W_p, P.w_cols, P.w_rows, P.ldw, BK, BN_CTA);
   if (st != PACKR_OK) return st;
-  return launch_impl<MODE, true>(P, maps, stream);
+  // more than one 256-row pair tile: two subtiles share each decoded stage
+  if (P.Mg > 2 * BM) return launch_impl<MODE, true, 2>(P, maps, stream);
+  return launch_impl<MODE, true, 1>(P, maps, stream);
+  }
 }
 
 }  // namespace gemm

@@ -126,6 +126,8 @@ CASES = [
     (257, 200, 264, torch.bfloat16, True),     # K, N not multiples of 64 / 256
     (130, 100, 36, torch.float32, False),      # K % 8 != 0 (padded activation copy)
     (512, 1024, 512, torch.bfloat16, True),
+    (600, 256, 512, torch.bfloat16, True),     # 512-row pair tiles: second tile's upper subtile empty
+    (300, 512, 1024, torch.float32, False),    # one 512-row tile, upper subtile partial
     (16, 4096, 11008, torch.bfloat16, True),   # Llama-7B gate/up, decode-bound M
     (16, 11008, 4096, torch.bfloat16, True),   # Llama-7B down
 ]
