@@ -79,7 +79,11 @@ int packr_adam8_multi(const packr_adam_tensor* tensors, int n_tensors, float lr,
 /* ---- PackRLinear ---------------------------------------------------------
  * out[M,N] (f32) = x[M,K] @ W + bias,  W = bf16(W_f + bf16(lut[W_p])),
  * computed on the tensor cores with x and W as bf16 operands and an f32
- * accumulator; W is decoded in shared memory and never written to HBM.
+ * accumulator.  Below 1024 rows W is decoded tile by tile in shared memory
+ * and never written to HBM; from 1024 rows on (N % 16 == 0, 16-byte aligned
+ * W_p / W_f) W is decoded once into the workspace and read back by TMA,
+ * provided the workspace holds it (packr_forward_workspace_bytes counts it;
+ * a smaller workspace that fits the fused route selects that route).
  * x is bf16 or f32 (f32 x is rounded to bf16 in the workspace first).
  * bias: [N] of bias_dtype (bf16 or f32, added in f32 in the epilogue) or
  * NULL.  M = 0 is a no-op; K, N >= 1.
@@ -104,7 +108,8 @@ int packr_forward(const void* x, int x_dtype, const uint8_t* W_p, const uint16_t
  * [+ x_lo.dY_hi]); without it dY is rounded to bf16 as the reference does for
  * dX.  A workspace of packr_backward_workspace_bytes(M, K, N, x_dtype, flags)
  * bytes (256-byte aligned) holds bf16(dY), its split parts, a bf16 copy of an
- * f32 x and the partial sums. */
+ * f32 x, the partial sums and, for dX from 1024 rows on, the decoded W (the
+ * same route choice as packr_forward). */
 #define PACKR_BWD_DW_SPLIT 1
 size_t packr_backward_workspace_bytes(int64_t M, int64_t K, int64_t N, int x_dtype, int flags);
 int packr_backward(const float* dY, const void* x, int x_dtype, const uint8_t* W_p, const uint16_t* W_f,
@@ -124,6 +129,12 @@ int packr_lut_finalize(float* dlut, const float* dlut_sum, const int32_t* counts
 int packr_decode_bf16(const uint8_t* W_p, const uint16_t* W_f, const float* lut, uint16_t* out, int64_t K,
                       int64_t N, void* stream);
 
+/* out[K,N] = bf16(W_f + bf16(lut[W_p])) by the streaming decode kernel that
+ * feeds the plain GEMMs (same bits as packr_decode_bf16).  N % 16 == 0;
+ * W_p, W_f and out 16-byte aligned. */
+int packr_predecode_bf16(const uint8_t* W_p, const uint16_t* W_f, const float* lut, uint16_t* out, int64_t K,
+                         int64_t N, void* stream);
+
 /* packr_backward without a caller-provided workspace, for callers that cannot
  * allocate device memory (a host runtime with a fixed device-memory budget
  * and no allocator of its own, a binding that can pass tensors it was given
@@ -132,7 +143,8 @@ int packr_decode_bf16(const uint8_t* W_p, const uint16_t* W_f, const float* lut,
  * scratch is one static device array of PACKR_STATIC_SCRATCH_BYTES per GPU,
  * held from the library's load until process exit.  Problems whose scratch
  * need exceeds that size return PACKR_ERR_WORKSPACE before any launch (the
- * need for bf16 x without PACKR_BWD_DW_SPLIT is about M*round8(N)*2 bytes).
+ * need for bf16 x without PACKR_BWD_DW_SPLIT is about M*round8(N)*2 bytes;
+ * dX then always takes the fused-decode route).
  * The first call on each device looks up the array's device address (make
  * it before any stream capture).  Every call shares the array; calls that
  * overlap on the GPU (different streams, different threads) race on it. */

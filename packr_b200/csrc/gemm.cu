@@ -76,24 +76,39 @@ constexpr int CHUNKS = BN_CTA * BK / 8 / DEC_THREADS;  // chunks of 8 weights pe
 constexpr int LUT_BYTES = 256 * 32 * 4;  // one u32 per (entry, lane)
 constexpr int HIST_COPIES = 4;  // lut-gradient histogram copies per epilogue warp (lane & 3)
 constexpr int ACC_COLS = BN;
+// FWD / DX switch from the fused decode to predecode + plain GEMM at this
+// many output rows (tokens): below it the decode traffic of the fused kernel
+// costs less than an extra HBM pass over W.
+#ifndef PACKR_PREDECODE_MIN_M
+#define PACKR_PREDECODE_MIN_M 1024
+#endif
+// Plain GEMMs use 512-row pair tiles from this many rows on.
+#ifndef PACKR_PLAIN_MSUB2_MIN_M
+#define PACKR_PLAIN_MSUB2_MIN_M 1024
+#endif
 constexpr int TMEM_COLS = 2 * ACC_COLS;
 constexpr uint16_t PAIR_MASK = 0x3;
 
 enum Mode { FWD = 0, DX = 1, DW = 2 };
+// Where the B operand of FWD / DX comes from: decoded on the fly from W_f /
+// W_p loaded through a register ring (B_RING) or by TMA (B_WTMA), or read by
+// TMA from a bf16 array the predecode kernel wrote (B_PLAIN).
+enum BSrc { B_RING = 0, B_WTMA = 1, B_PLAIN = 2 };
 
-// WTMA (decode modes): W_f and W_p tiles arrive by TMA into shared memory
-// and are decoded in place; otherwise (rows of W_p not a multiple of 16
-// bytes) the decode warps load them into a register ring.
+// B_WTMA (decode modes): W_f and W_p tiles arrive by TMA into shared memory
+// and are decoded in place; B_RING (rows of W_p not a multiple of 16 bytes):
+// the decode warps load them into a register ring.  B_PLAIN: no decode.
 // MSUB: output rows per pair tile = 256 * MSUB.  With MSUB = 2 every decoded
 // B stage feeds two pair MMAs (two 256-row subtiles), halving the decode and
 // lut traffic per FLOP; the two subtiles' accumulators then fill TMEM (no
 // double buffering across tiles, but each subtile is released separately).
-template <int MODE, bool WTMA, int MSUB>
+template <int MODE, int BSRC, int MSUB>
 struct Cfg {
-  static constexpr bool kDecode = MODE != DW;
-  static constexpr bool kWtma = kDecode && WTMA;
+  static constexpr bool kDecode = MODE != DW && BSRC != B_PLAIN;
+  static constexpr bool kWtma = kDecode && BSRC == B_WTMA;
+  static constexpr bool kPlainB = MODE != DW && BSRC == B_PLAIN;  // FWD / DX with B by TMA
   static constexpr int kMSub = MSUB;
-  static constexpr int kStages = kWtma ? (MSUB == 2 ? 3 : 4) : 6;
+  static constexpr int kStages = kWtma ? (MSUB == 2 ? 3 : 4) : (kPlainB && MSUB == 2 ? 4 : 6);
   static constexpr int kABytes = MSUB * A_BYTES;            // A subtiles per stage
   static constexpr int kWpBytes = kWtma ? BN_CTA * BK : 0;  // u8 W_p tile per stage
   static constexpr int kStageBytes = kABytes + B_BYTES + kWpBytes;
@@ -103,7 +118,7 @@ struct Cfg {
   // TMA-staged decode modes pass each 32-row output block through a 4 KB
   // per-warp shared-memory buffer, so that global stores cover whole rows
   // segments of 128 (f32) or 64 (bf16) bytes instead of 16 bytes per row.
-  static constexpr bool kStageOut = kWtma;
+  static constexpr bool kStageOut = kWtma || kPlainB;
   static constexpr int kStgBytes = kStageOut ? kEpiWarps * 4096 : 0;
   static constexpr int kChunksPerEpiWarp = (BN / 32) / (kEpiWarps / 4);
   static constexpr int kDecWarp0 = 2 + kEpiWarps;             // first decode warp
@@ -114,11 +129,12 @@ struct Cfg {
   static constexpr bool kAmn = MODE == DW;   // A stored MN-major in smem
   static constexpr bool kBmn = MODE != DX;   // B stored MN-major in smem
   static constexpr int kHistBytes = kEpiWarps * HIST_COPIES * 256 * 4;
-  static constexpr int kAuxBytes = kDecode ? LUT_BYTES + kStgBytes : kHistBytes;
+  static constexpr int kLutBytes = kDecode ? LUT_BYTES : 0;
+  static constexpr int kAuxBytes = MODE == DW ? kHistBytes : kLutBytes + kStgBytes;
   static constexpr int kBarOff = kStages * kStageBytes + kAuxBytes;
   static constexpr int kSmemBytes = kBarOff + 256 + 1024;  // barriers + alignment slack
   static constexpr uint32_t kIdesc = idesc_bf16_f32(2 * BM, BN, kAmn, kBmn);
-  static constexpr uint32_t kTxBytes = 2 * (kDecode ? kABytes : A_BYTES + B_BYTES);  // both CTAs
+  static constexpr uint32_t kTxBytes = 2 * (kDecode ? kABytes : kABytes + B_BYTES);  // both CTAs
   static constexpr uint32_t kWTxBytes = B_BYTES + kWpBytes;                          // this CTA's W tiles
   static constexpr uint32_t kBfullCount = kWtma ? 2 * kDecWarps : 2;
 };
@@ -386,10 +402,10 @@ __device__ __forceinline__ void store_rows_staged(uint32_t stg, const float* v, 
 }
 
 // ------------------------------------------------------------------ kernel
-template <int MODE, bool WTMA, int MSUB>
-__global__ void __launch_bounds__(Cfg<MODE, WTMA, MSUB>::kThreads, 1)
+template <int MODE, int BSRC, int MSUB>
+__global__ void __launch_bounds__(Cfg<MODE, BSRC, MSUB>::kThreads, 1)
     packr_gemm_kernel(const Params P, const __grid_constant__ Maps maps) {
-  using C = Cfg<MODE, WTMA, MSUB>;
+  using C = Cfg<MODE, BSRC, MSUB>;
   constexpr int STAGES = C::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte aligned base for the 128-byte-swizzled tiles; offsetting the
@@ -428,7 +444,7 @@ __global__ void __launch_bounds__(Cfg<MODE, WTMA, MSUB>::kThreads, 1)
   if (warp == 0 && lane == 0) {
     for (int s = 0; s < P.nseg; ++s) {
       prefetch_tmap(&maps.a[s]);
-      if (MODE == DW) prefetch_tmap(&maps.b[s]);
+      if (MODE == DW || C::kPlainB) prefetch_tmap(&maps.b[s]);
     }
     if (C::kWtma) {
       prefetch_tmap(&maps.wf);
@@ -483,6 +499,16 @@ __global__ void __launch_bounds__(Cfg<MODE, WTMA, MSUB>::kThreads, 1)
 #pragma unroll
             for (int sub = 0; sub < MSUB; ++sub)
               tma_load_2d_pair(a_dst + sub * A_BYTES, &maps.a[seg], fbar, k0, m0 + sub * 2 * BM);
+            if (C::kPlainB) {
+              // this CTA's 128 columns of the predecoded B
+              uint8_t* b_dst = sB + s * B_BYTES;
+              if (MODE == FWD) {  // W [K, N]: MN-major, two 64-column blocks
+                tma_load_2d_pair(b_dst, &maps.b[seg], fbar, n0, k0);
+                tma_load_2d_pair(b_dst + 8192, &maps.b[seg], fbar, n0 + 64, k0);
+              } else {            // W rows are dX columns: K-major
+                tma_load_2d_pair(b_dst, &maps.b[seg], fbar, k0, n0);
+              }
+            }
             if (C::kWtma) {
               // this CTA's W_f / W_p tiles (its 128 columns of B) onto its own wfull
               const int nb0 = (tile / P.m_tiles) * BN + (int)rank * BN_CTA;
@@ -564,7 +590,7 @@ __global__ void __launch_bounds__(Cfg<MODE, WTMA, MSUB>::kThreads, 1)
     const uint32_t tempty0 = mapa(smem_u32(&bars->tempty[0]), 0);
     const uint32_t tempty1 = mapa(smem_u32(&bars->tempty[1]), 0);
     const uint32_t hist_lane = smem_u32(sAux) + (uint32_t)(((warp - 2) * HIST_COPIES + (lane & 3)) * 1024);
-    const uint32_t stg = smem_u32(sAux) + (uint32_t)(LUT_BYTES + (warp - 2) * 4096);
+    const uint32_t stg = smem_u32(sAux) + (uint32_t)(C::kLutBytes + (warp - 2) * 4096);
     // DW: the W_p bytes of the next tile's chunks are fetched before its
     // accumulator is ready (they do not depend on it)
     uint4 wpa[C::kChunksPerEpiWarp], wpb[C::kChunksPerEpiWarp];
@@ -870,15 +896,15 @@ int make_map_u8(CUtensorMap* m, const void* base, long long inner, long long row
   return r == CUDA_SUCCESS ? PACKR_OK : PACKR_ERR_INVALID_ARGUMENT;
 }
 
-template <int MODE, bool WTMA, int MSUB = 1>
+template <int MODE, int BSRC, int MSUB = 1>
 int launch_impl(Params P, const Maps& maps, cudaStream_t stream) {
-  using C = Cfg<MODE, WTMA, MSUB>;
+  using C = Cfg<MODE, BSRC, MSUB>;
   static std::once_flag attr_once[64];
   int dev = 0;
   cudaGetDevice(&dev);
   int attr_rc = 0;
   std::call_once(attr_once[dev & 63], [&] {
-    attr_rc = cudaFuncSetAttribute(packr_gemm_kernel<MODE, WTMA, MSUB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    attr_rc = cudaFuncSetAttribute(packr_gemm_kernel<MODE, BSRC, MSUB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    C::kSmemBytes) != cudaSuccess;
   });
   if (attr_rc) return PACKR_ERR_CUDA;
@@ -899,11 +925,17 @@ int launch_impl(Params P, const Maps& maps, cudaStream_t stream) {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, packr_gemm_kernel<MODE, WTMA, MSUB>, P, maps) != cudaSuccess) {
+  if (cudaLaunchKernelEx(&cfg, packr_gemm_kernel<MODE, BSRC, MSUB>, P, maps) != cudaSuccess) {
     cudaGetLastError();
     return PACKR_ERR_LAUNCH;
   }
   return launch_status();
+}
+
+// W_f / W_p can be staged by TMA: rows of W_p a multiple of 16 bytes and both
+// bases 16-byte aligned.
+inline bool wtma_ok(const uint8_t* W_p, const uint16_t* W_f, long long ldw) {
+  return (ldw & 15) == 0 && aligned(W_f, 16) && aligned(W_p, 16);
 }
 
 // Launches one GEMM.  Decode modes stage W_f / W_p by TMA when W's rows are
@@ -918,19 +950,31 @@ int launch(Params P, Maps maps, cudaStream_t stream) {
   P.n_tiles = (P.Ng + BN - 1) / BN;
   P.k_blocks = (P.Kg + BK - 1) / BK;
   if constexpr (MODE == DW) {
-    return launch_impl<MODE, false>(P, maps, stream);
+    return launch_impl<MODE, B_RING>(P, maps, stream);
   } else {
-  const bool wtma = (P.ldw & 15) == 0 && aligned(P.W_f, 16) && aligned(P.W_p, 16);
-  if (!wtma) return launch_impl<MODE, false>(P, maps, stream);
+  if (!wtma_ok(P.W_p, P.W_f, P.ldw)) return launch_impl<MODE, B_RING>(P, maps, stream);
   int st = make_map(&maps.wf, P.W_f, P.w_cols, P.w_rows, P.ldw * 2, MODE == FWD ? BK : BN_CTA);
   if (st == PACKR_OK)
     st = MODE == FWD ? make_map_u8(&maps.wp, P.W_p, P.w_cols, P.w_rows, P.ldw, BN_CTA, BK)
                      : make_map_u8(&maps.wp, P.W_p, P.w_cols, P.w_rows, P.ldw, BK, BN_CTA);
   if (st != PACKR_OK) return st;
   // more than one 256-row pair tile: two subtiles share each decoded stage
-  if (P.Mg > 2 * BM) return launch_impl<MODE, true, 2>(P, maps, stream);
-  return launch_impl<MODE, true, 1>(P, maps, stream);
+  if (P.Mg > 2 * BM) return launch_impl<MODE, B_WTMA, 2>(P, maps, stream);
+  return launch_impl<MODE, B_WTMA, 1>(P, maps, stream);
   }
+}
+
+// FWD / DX over a predecoded bf16 W (maps.b[0] set by the caller: FWD an
+// [K, N] map with 64-row boxes, DX an [K, N] map with 128-row boxes).
+template <int MODE>
+int launch_plain(Params P, const Maps& maps, cudaStream_t stream) {
+  static_assert(MODE != DW, "DW has its own operands");
+  P.out_vec = aligned(P.out, 16);
+  P.idx_vec = 0;
+  P.n_tiles = (P.Ng + BN - 1) / BN;
+  P.k_blocks = (P.Kg + BK - 1) / BK;
+  if (P.Mg >= PACKR_PLAIN_MSUB2_MIN_M) return launch_impl<MODE, B_PLAIN, 2>(P, maps, stream);
+  return launch_impl<MODE, B_PLAIN, 1>(P, maps, stream);
 }
 
 }  // namespace gemm

@@ -5,5 +5,6 @@
 #include "adam8.cu"
 #include "prep.cu"
 #include "gemm.cu"
+#include "predecode.cu"
 #include "linear.cu"
 #include "static_scratch.cu"

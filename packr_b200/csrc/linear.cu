@@ -25,24 +25,33 @@ struct Carve {
 
 bool x_needs_copy(int x_dtype, long long K) { return x_dtype == PACKR_DTYPE_F32 || (K & 7) != 0; }
 
+// FWD / DX take the predecode + plain GEMM route for M >= PACKR_PREDECODE_MIN_M
+// when W's layout allows TMA (N % 16 == 0, 16-byte aligned W_p / W_f) and the
+// workspace holds the decoded W; otherwise the fused-decode GEMM runs.
+inline bool predecode_eligible(long long M, long long N) { return M >= PACKR_PREDECODE_MIN_M && (N & 15) == 0; }
+
 struct FwdPlan {
   uint16_t* xh;
+  uint16_t* wd;  // decoded W [K, N] (predecode route only)
 };
 
-size_t plan_forward(Carve& c, FwdPlan& p, long long M, long long K, int x_dtype) {
+size_t plan_forward(Carve& c, FwdPlan& p, long long M, long long K, long long N, int x_dtype, bool pre) {
   p.xh = x_needs_copy(x_dtype, K) ? c.take<uint16_t>((size_t)M * round8(K)) : nullptr;
+  p.wd = pre ? c.take<uint16_t>((size_t)K * N) : nullptr;
   return c.off;
 }
 
 struct BwdPlan {
   uint16_t *dh, *dl, *xh, *xl;
+  uint16_t* wd;  // decoded W [K, N] (predecode route for dX only)
   float *colsum, *dlut_sum;
   int32_t* counts;
 };
 
 size_t plan_backward(Carve& c, BwdPlan& p, long long M, long long K, long long N, int x_dtype, int flags,
-                     bool want_dx, bool want_dw, bool want_dlut, bool want_dbias, bool have_counts) {
+                     bool want_dx, bool want_dw, bool want_dlut, bool want_dbias, bool have_counts, bool pre) {
   const bool split = (flags & PACKR_BWD_DW_SPLIT) != 0 && (want_dw || want_dlut);
+  p.wd = pre && want_dx ? c.take<uint16_t>((size_t)K * N) : nullptr;
   p.dh = c.take<uint16_t>((size_t)M * round8(N));
   p.dl = split ? c.take<uint16_t>((size_t)M * round8(N)) : nullptr;
   const bool need_x = want_dw || want_dlut;
@@ -51,7 +60,6 @@ size_t plan_backward(Carve& c, BwdPlan& p, long long M, long long K, long long N
   p.colsum = want_dbias ? c.take<float>((size_t)N) : nullptr;
   p.dlut_sum = want_dlut ? c.take<float>(256) : nullptr;
   p.counts = want_dlut && !have_counts ? c.take<int32_t>(256) : nullptr;
-  (void)want_dx;
   return c.off;
 }
 
@@ -73,10 +81,12 @@ using namespace packr;
 using namespace packr::linear;
 
 extern "C" size_t packr_forward_workspace_bytes(int64_t M, int64_t K, int64_t N, int x_dtype) {
-  (void)N;
   Carve c{nullptr};
   FwdPlan p;
-  return plan_forward(c, p, M > 0 ? M : 0, K > 0 ? K : 0, x_dtype);
+  M = M > 0 ? M : 0;
+  K = K > 0 ? K : 0;
+  N = N > 0 ? N : 0;
+  return plan_forward(c, p, M, K, N, x_dtype, predecode_eligible(M, N));
 }
 
 extern "C" int packr_forward(const void* x, int x_dtype, const uint8_t* W_p, const uint16_t* W_f, const float* lut,
@@ -91,9 +101,15 @@ extern "C" int packr_forward(const void* x, int x_dtype, const uint8_t* W_p, con
   if ((st = check_device()) != PACKR_OK) return st;
   if (M == 0) return PACKR_OK;
   cudaStream_t s = as_stream(stream);
+  bool pre = predecode_eligible(M, N) && gemm::wtma_ok(W_p, W_f, N);
   Carve c{static_cast<uint8_t*>(workspace)};
   FwdPlan p;
-  const size_t need = plan_forward(c, p, M, K, x_dtype);
+  size_t need = plan_forward(c, p, M, K, N, x_dtype, pre);
+  if (pre && workspace_bytes < need) {  // workspace sized for the fused route
+    pre = false;
+    c = Carve{static_cast<uint8_t*>(workspace)};
+    need = plan_forward(c, p, M, K, N, x_dtype, false);
+  }
   if (need > 0 && (workspace == nullptr || workspace_bytes < need || !aligned(workspace, kAlign)))
     return PACKR_ERR_WORKSPACE;
   const void* a_ptr = x;
@@ -122,14 +138,21 @@ extern "C" int packr_forward(const void* x, int x_dtype, const uint8_t* W_p, con
   P.ld_out = N;
   P.bias = bias;
   P.bias_f32 = bias_dtype == PACKR_DTYPE_F32;
+  if (pre) {
+    if ((st = gemm::predecode(W_p, W_f, lut, p.wd, K, N, s)) != PACKR_OK) return st;
+    if ((st = gemm::make_map(&maps.b[0], p.wd, N, K, N * 2, 64)) != PACKR_OK) return st;
+    return gemm::launch_plain<gemm::FWD>(P, maps, s);
+  }
   return gemm::launch<gemm::FWD>(P, maps, s);
 }
 
 extern "C" size_t packr_backward_workspace_bytes(int64_t M, int64_t K, int64_t N, int x_dtype, int flags) {
   Carve c{nullptr};
   BwdPlan p;
-  return plan_backward(c, p, M > 0 ? M : 0, K > 0 ? K : 0, N > 0 ? N : 0, x_dtype, flags, true, true, true, true,
-                       false);
+  M = M > 0 ? M : 0;
+  K = K > 0 ? K : 0;
+  N = N > 0 ? N : 0;
+  return plan_backward(c, p, M, K, N, x_dtype, flags, true, true, true, true, false, predecode_eligible(M, N));
 }
 
 extern "C" int packr_backward(const float* dY, const void* x, int x_dtype, const uint8_t* W_p, const uint16_t* W_f,
@@ -154,10 +177,17 @@ extern "C" int packr_backward(const float* dY, const void* x, int x_dtype, const
     if (want_dbias && cudaMemsetAsync(dbias, 0, (size_t)N * 2, s) != cudaSuccess) return PACKR_ERR_CUDA;
     return PACKR_OK;
   }
+  bool pre = want_dx && predecode_eligible(M, N) && gemm::wtma_ok(W_p, W_f, N);
   Carve c{static_cast<uint8_t*>(workspace)};
   BwdPlan p;
-  const size_t need = plan_backward(c, p, M, K, N, x_dtype, flags, want_dx, want_dw, want_dlut, want_dbias,
-                                    lut_counts != nullptr);
+  size_t need = plan_backward(c, p, M, K, N, x_dtype, flags, want_dx, want_dw, want_dlut, want_dbias,
+                              lut_counts != nullptr, pre);
+  if (pre && workspace_bytes < need) {  // workspace sized for the fused route
+    pre = false;
+    c = Carve{static_cast<uint8_t*>(workspace)};
+    need = plan_backward(c, p, M, K, N, x_dtype, flags, want_dx, want_dw, want_dlut, want_dbias,
+                         lut_counts != nullptr, false);
+  }
   if (workspace == nullptr || workspace_bytes < need || !aligned(workspace, kAlign)) return PACKR_ERR_WORKSPACE;
   if (p.colsum && cudaMemsetAsync(p.colsum, 0, (size_t)N * 4, s) != cudaSuccess) return PACKR_ERR_CUDA;
   if (p.dlut_sum && cudaMemsetAsync(p.dlut_sum, 0, 256 * 4, s) != cudaSuccess) return PACKR_ERR_CUDA;
@@ -182,7 +212,14 @@ extern "C" int packr_backward(const float* dY, const void* x, int x_dtype, const
     P.out = dX;
     P.ld_out = K;
     P.out_f32 = x_dtype == PACKR_DTYPE_F32;
-    if ((st = gemm::launch<gemm::DX>(P, maps, s)) != PACKR_OK) return st;
+    if (pre) {
+      if ((st = gemm::predecode(W_p, W_f, lut, p.wd, K, N, s)) != PACKR_OK) return st;
+      if ((st = gemm::make_map(&maps.b[0], p.wd, N, K, N * 2, gemm::BN_CTA)) != PACKR_OK) return st;
+      st = gemm::launch_plain<gemm::DX>(P, maps, s);
+    } else {
+      st = gemm::launch<gemm::DX>(P, maps, s);
+    }
+    if (st != PACKR_OK) return st;
   }
   if (want_dw || want_dlut) {
     const void* xa = x;
@@ -240,6 +277,18 @@ extern "C" int packr_lut_finalize(float* dlut, const float* dlut_sum, const int3
   int st = check_device();
   if (st != PACKR_OK) return st;
   return prep::finalize(dlut, dlut_sum, counts, nullptr, nullptr, 0, as_stream(stream));
+}
+
+extern "C" int packr_predecode_bf16(const uint8_t* W_p, const uint16_t* W_f, const float* lut, uint16_t* out,
+                                    int64_t K, int64_t N, void* stream) {
+  if (K < 0 || N < 0 || K > 0x7FFFFFFFll || N > 0x7FFFFFFFll) return PACKR_ERR_SHAPE;
+  if (K * N == 0) return PACKR_OK;
+  if (!W_p || !W_f || !lut || !out) return PACKR_ERR_INVALID_ARGUMENT;
+  if ((N & 15) != 0) return PACKR_ERR_SHAPE;
+  if (!aligned(lut, 4)) return PACKR_ERR_ALIGNMENT;
+  int st = check_device();
+  if (st != PACKR_OK) return st;
+  return gemm::predecode(W_p, W_f, lut, out, K, N, as_stream(stream));
 }
 
 extern "C" int packr_decode_bf16(const uint8_t* W_p, const uint16_t* W_f, const float* lut, uint16_t* out, int64_t K,

@@ -45,7 +45,7 @@ extern "C" int packr_backward_static_scratch(const float* dY, const void* x, int
     linear::Carve c{nullptr};
     linear::BwdPlan p;
     const size_t need = linear::plan_backward(c, p, M, K, N, x_dtype, flags, dX != nullptr, dW_f != nullptr,
-                                              dlut != nullptr, dbias != nullptr, lut_counts != nullptr);
+                                              dlut != nullptr, dbias != nullptr, lut_counts != nullptr, false);
     if (need > (size_t)PACKR_STATIC_SCRATCH_BYTES) return PACKR_ERR_WORKSPACE;  // beyond the static maximum
   }
   void* scratch = nullptr;

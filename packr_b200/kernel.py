@@ -104,6 +104,19 @@ def decode_bf16(W_p: torch.Tensor, W_f: torch.Tensor, lut: torch.Tensor) -> torc
     return out
 
 
+def predecode_bf16(W_p: torch.Tensor, W_f: torch.Tensor, lut: torch.Tensor) -> torch.Tensor:
+    """bf16(W_f + bf16(lut[W_p])) through the streaming decode kernel that feeds
+    the plain GEMMs of large batches (N % 16 == 0)."""
+    lib = _lib.load()
+    K, N = W_p.shape
+    out = torch.empty(K, N, dtype=torch.bfloat16, device=W_p.device)
+    with torch.cuda.device(W_p.device):
+        code = lib.packr_predecode_bf16(_ptr(W_p.contiguous()), _ptr(W_f.contiguous()),
+                                        _ptr(lut.detach().float().contiguous()), _ptr(out), K, N, _stream(W_p.device))
+    _lib.check("packr_predecode_bf16", code)
+    return out
+
+
 def dw_split_for(x_dtype: torch.dtype) -> bool:
     if DW_PRECISION == "split":
         return True

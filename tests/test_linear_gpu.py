@@ -91,6 +91,47 @@ def test_decode_bit_exact_extreme_lut(cuda):
     assert np.array_equal(got, want)
 
 
+@pytest.mark.parametrize("shape", [(64, 256), (1, 16), (768, 3072), (3072, 768), (37, 4112)])
+def test_predecode_bit_exact(cuda, shape):
+    """The streaming decode that feeds the plain GEMMs of large batches."""
+    Kd, Nd = shape
+    c = linear_case(1, Kd, Nd, seed=13)
+    got = bits(K.predecode_bf16(c["W_p"].cuda(), c["W_f"].cuda(), c["lut"].cuda()))
+    want = oracle.decode_bf16(bits(c["W_p"]), bits(c["W_f"]), bits(c["lut"]))
+    assert np.array_equal(got, want)
+
+
+def test_predecode_bit_exact_extreme_lut(cuda):
+    c = linear_case(1, 64, 512, seed=12)
+    lut = torch.tensor([0.0, -0.0, 1e-40, -1e-40, 3.0e38, -3.0e38, 1.0 + 2 ** -8, 1.0 + 3 * 2 ** -8] +
+                       list(np.linspace(-1, 1, 248)), dtype=torch.float32)
+    W_f = (torch.randn(64, 512) * 10.0).to(torch.bfloat16)
+    got = bits(K.predecode_bf16(c["W_p"].cuda(), W_f.cuda(), lut.cuda()))
+    assert np.array_equal(got, oracle.decode_bf16(bits(c["W_p"]), bits(W_f), bits(lut)))
+
+
+def test_forward_route_follows_workspace(cuda):
+    """A workspace sized for the fused route (no room for the decoded W) makes
+    the forward fall back to it; both routes give the same bits."""
+    from packr_b200 import _lib
+    lib = _lib.load()
+    M, Kd, Nd = 1024, 256, 512
+    c = to_cuda(linear_case(M, Kd, Nd, x_dtype=torch.bfloat16, bias=True, seed=5))
+    full = lib.packr_forward_workspace_bytes(M, Kd, Nd, 1)
+    assert full >= Kd * Nd * 2
+    outs = []
+    for ws_bytes in (full, full - Kd * Nd * 2):
+        ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device="cuda")
+        out = torch.empty(M, Nd, dtype=torch.float32, device="cuda")
+        rc = lib.packr_forward(c["x"].data_ptr(), 1, c["W_p"].data_ptr(), c["W_f"].data_ptr(), c["lut"].data_ptr(),
+                               c["bias"].data_ptr(), 1, out.data_ptr(), M, Kd, Nd, ws.data_ptr(), ws_bytes,
+                               torch.cuda.current_stream().cuda_stream)
+        assert rc == 0
+        outs.append(out)
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])
+
+
 @pytest.mark.parametrize("n", [0, 1, 15, 16, 1000, 768 * 3072 + 3])
 def test_bincount(cuda, n):
     g = torch.Generator().manual_seed(n)
@@ -128,6 +169,8 @@ CASES = [
     (512, 1024, 512, torch.bfloat16, True),
     (600, 256, 512, torch.bfloat16, True),     # 512-row pair tiles: second tile's upper subtile empty
     (300, 512, 1024, torch.float32, False),    # one 512-row tile, upper subtile partial
+    (1500, 320, 528, torch.bfloat16, True),    # predecode + plain GEMM, ragged M / K / N tiles
+    (1100, 192, 264, torch.float32, True),     # large M but N % 16 != 0: fused register-ring route
     (16, 4096, 11008, torch.bfloat16, True),   # Llama-7B gate/up, decode-bound M
     (16, 11008, 4096, torch.bfloat16, True),   # Llama-7B down
 ]
