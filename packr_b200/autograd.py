@@ -22,6 +22,25 @@ import torch
 from . import kernel as _k
 
 
+def grad_sink(param: torch.Tensor) -> torch.Tensor | None:
+    """A fresh view of the gradient buffer an optimizer registered for
+    `param` (param._packr_grad_sink = (flat_buffer, element_offset)), or None.
+    Only offered while param.grad is None: the backward then writes the
+    gradient straight into the buffer and autograd adopts the view as
+    param.grad without a copy; with a gradient already present, autograd
+    accumulates into it as usual."""
+    if param is None or param.grad is not None:
+        return None
+    spec = getattr(param, "_packr_grad_sink", None)
+    if spec is None:
+        return None
+    buf, off = spec
+    n = param.numel()
+    if buf.dtype != param.dtype or buf.device != param.device or off + n > buf.numel():
+        return None
+    return buf[off:off + n].view(param.shape)
+
+
 class PackRLinearFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, W_p, W_f, lut, bias=None, counts=None, evict_cb=None):
@@ -30,6 +49,7 @@ class PackRLinearFunction(torch.autograd.Function):
         ctx.save_for_backward(x, W_p, W_f, lut, counts)
         ctx.has_bias = bias is not None
         ctx.evict_cb = evict_cb
+        ctx.wf_param = W_f
         return _k.forward(x, W_p, W_f, lut, bias)
 
     @staticmethod
@@ -37,7 +57,8 @@ class PackRLinearFunction(torch.autograd.Function):
         x, W_p, W_f, lut, counts = ctx.saved_tensors
         nx, _, nwf, nlut, nb = ctx.needs_input_grad[:5]
         dX, dW, dlut, dbias = _k.backward(grad_out, x, W_p, W_f, lut, counts, need_dx=nx, need_dw=nwf,
-                                          need_dlut=nlut, need_dbias=ctx.has_bias and nb)
+                                          need_dlut=nlut, need_dbias=ctx.has_bias and nb,
+                                          dW_out=grad_sink(ctx.wf_param) if nwf else None)
         if ctx.evict_cb is not None:
             ctx.evict_cb()
         if dX is not None and dX.dtype != x.dtype:
@@ -53,6 +74,7 @@ class PackRMatmulFunction(torch.autograd.Function):
     def forward(ctx, x, W_p, W_f, lut, evict_cb=None, layer_name=None, offload_mgr=None):
         ctx.save_for_backward(x, W_p, W_f, lut)
         ctx._evict_cb = evict_cb
+        ctx.wf_param = W_f
         return _k.packr_matmul(x, W_p, W_f, lut)
 
     @staticmethod
@@ -60,7 +82,7 @@ class PackRMatmulFunction(torch.autograd.Function):
         x, W_p, W_f, lut = ctx.saved_tensors
         nx, _, nwf, nlut = ctx.needs_input_grad[:4]
         dX, dW, dlut, _ = _k.backward(grad_out, x, W_p, W_f, lut, None, need_dx=nx, need_dw=nwf, need_dlut=nlut,
-                                      need_dbias=False)
+                                      need_dbias=False, dW_out=grad_sink(ctx.wf_param) if nwf else None)
         if ctx._evict_cb is not None:
             ctx._evict_cb()
         if dX is not None and dX.dtype != x.dtype:

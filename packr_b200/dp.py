@@ -13,13 +13,17 @@ blocks.  A parameter's `.data` becomes a view of its flat buffer, so the
 all-gather writes the updated values in place.
 
 Step (identical collective sequence on every rank):
-  1. copy each .grad into the flat gradient buffer (zeros where None)
+  1. copy each .grad into the flat gradient buffer (zeros where None).  Each
+     parameter carries `_packr_grad_sink = (flat_grad, offset)`: PackRLinear's
+     backward writes dW_f straight into that slice while .grad is None, and
+     the copy is skipped for a .grad that already is the slice
   2. reduce_scatter_tensor(op=AVG)   -> this rank's averaged gradient shard
   3. packr_adam8_multi over the parameter sub-ranges of the shard (the same
      per-block arithmetic as CUDA8BitAdam, so the result equals the
      single-process step on the averaged gradient)
   4. all_gather_into_tensor           -> every rank holds the new parameters
-With world_size 1 the collectives are skipped.
+With world_size 1 the collectives are skipped and the optimizer reads the
+flat gradient buffer itself.
 """
 from __future__ import annotations
 
@@ -102,9 +106,10 @@ class ShardedAdam8:
         for s in g.slots:
             g.flat[s.offset:s.offset + s.numel].copy_(s.param.detach().reshape(-1))
             s.param.data = g.flat[s.offset:s.offset + s.numel].view_as(s.param)
+            s.param._packr_grad_sink = (g.grad, s.offset)
         shard = total // self.world
         s0 = self.rank * shard
-        g.shard_grad = torch.zeros(shard, dtype=g.dtype, device=self.device)
+        g.shard_grad = g.grad if self.world == 1 else torch.zeros(shard, dtype=g.dtype, device=self.device)
         g.m = torch.zeros(shard, dtype=torch.int8, device=self.device)
         g.v = torch.zeros(shard, dtype=torch.int8, device=self.device)
         g.ms = torch.ones(shard // BLOCK, dtype=torch.float32, device=self.device)
@@ -136,12 +141,10 @@ class ShardedAdam8:
                 dst = g.grad[s.offset:s.offset + s.numel]
                 if s.param.grad is None:
                     dst.zero_()
-                else:
+                elif s.param.grad.data_ptr() != dst.data_ptr():  # not already the slice
                     dst.copy_(s.param.grad.reshape(-1))
             if self.world > 1:
                 dist.reduce_scatter_tensor(g.shard_grad, g.grad, op=dist.ReduceOp.AVG, group=self.pg)
-            else:
-                g.shard_grad.copy_(g.grad)
             if g.entries:
                 self.adam_fn(g.entries, self.lr, b1, b2, self.eps, bc1, bc2, self.weight_decay)
             if self.world > 1:

@@ -126,8 +126,11 @@ def dw_split_for(x_dtype: torch.dtype) -> bool:
 
 
 def backward(dY: torch.Tensor, x: torch.Tensor, W_p: torch.Tensor, W_f: torch.Tensor, lut: torch.Tensor,
-             counts: torch.Tensor | None, need_dx: bool, need_dw: bool, need_dlut: bool, need_dbias: bool):
-    """Returns (dX, dW_f, dlut, dbias); entries not requested are None."""
+             counts: torch.Tensor | None, need_dx: bool, need_dw: bool, need_dlut: bool, need_dbias: bool,
+             dW_out: torch.Tensor | None = None):
+    """Returns (dX, dW_f, dlut, dbias); entries not requested are None.
+    dW_out: optional contiguous bf16 [K, N] tensor the dW_f result is written
+    into (for example a view of an optimizer's flat gradient buffer)."""
     lib = _lib.load()
     x = _as_operand(x)
     M, K = x.shape
@@ -135,7 +138,13 @@ def backward(dY: torch.Tensor, x: torch.Tensor, W_p: torch.Tensor, W_f: torch.Te
     dev = x.device
     dY = dY.float().contiguous()
     dX = torch.empty(M, K, dtype=x.dtype, device=dev) if need_dx else None
-    dW = torch.empty(K, N, dtype=torch.bfloat16, device=dev) if need_dw else None
+    if need_dw and dW_out is not None:
+        if (dW_out.dtype != torch.bfloat16 or tuple(dW_out.shape) != (K, N) or not dW_out.is_contiguous()
+                or dW_out.device != dev):
+            raise ValueError("dW_out must be a contiguous bf16 [K, N] tensor on x's device")
+        dW = dW_out
+    else:
+        dW = torch.empty(K, N, dtype=torch.bfloat16, device=dev) if need_dw else None
     dlut = torch.empty(256, dtype=torch.float32, device=dev) if need_dlut else None
     dbias = torch.empty(N, dtype=torch.bfloat16, device=dev) if need_dbias else None
     if not (need_dx or need_dw or need_dlut or need_dbias):

@@ -144,3 +144,41 @@ def test_sharded_adam_and_training_on_two_gpus():
     u_dp = res[0][2]
     cos = float(np.dot(u_dp, upd) / (np.linalg.norm(u_dp) * np.linalg.norm(upd)))
     assert cos > 0.95, cos
+
+
+def test_grad_sink_single_gpu(cuda):
+    """World size 1: PackRLinear's backward writes dW_f straight into the
+    optimizer's flat gradient buffer (no copy), accumulation still adds, and
+    the step equals CUDA8BitAdam on the same gradients (W_f bit for bit; the
+    lut gradient is an atomic sum, reproducible to rounding only)."""
+    from packr_b200 import PackRLinear
+    from packr_b200.cuda_adam import CUDA8BitAdam
+    from packr_b200.dp import ShardedAdam8
+    dev = torch.device("cuda")
+    lays = [PackRLinear.synthetic(256, 512, bias=False, device=dev, seed=3),
+            PackRLinear.synthetic(512, 128, bias=False, device=dev, seed=4)]
+    twins = [PackRLinear.synthetic(256, 512, bias=False, device=dev, seed=3),
+             PackRLinear.synthetic(512, 128, bias=False, device=dev, seed=4)]
+    opt = ShardedAdam8([p for l in lays for p in (l.W_f, l.lut)], lr=1e-3, weight_decay=0.01)
+    ropt = CUDA8BitAdam([p for l in twins for p in (l.W_f, l.lut)], lr=1e-3, weight_decay=0.01)
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn(300, 256, generator=g, device=dev).to(torch.bfloat16)
+    dy = torch.randn(300, 128, generator=g, device=dev)
+    flat = opt.groups[torch.bfloat16].grad
+    opt.zero_grad()
+    ropt.zero_grad()
+    for _ in range(2):  # two micro-batches: the second accumulates into the sink
+        lays[1](lays[0](x).to(torch.bfloat16)).backward(dy)
+        twins[1](twins[0](x).to(torch.bfloat16)).backward(dy)
+    close = lambda a, b: torch.allclose(a, b, rtol=1e-5, atol=1e-6 * b.abs().max().item())
+    for l, t in zip(lays, twins):
+        gptr = l.W_f.grad.data_ptr()
+        assert flat.data_ptr() <= gptr < flat.data_ptr() + flat.numel() * flat.element_size()
+        assert torch.equal(l.W_f.grad, t.W_f.grad)
+        assert close(l.lut.grad, t.lut.grad)
+    opt.step()
+    ropt.step()
+    torch.cuda.synchronize()
+    for l, t in zip(lays, twins):
+        assert torch.equal(l.W_f, t.W_f)
+        assert close(l.lut, t.lut)
