@@ -324,6 +324,15 @@ def cpu_linear_port(budget_s: float, M: int = 1024):
             "host_cores": os.cpu_count()}
 
 
+def layer_launches(M: int, K: int, N: int) -> int:
+    """libpackr_b200 kernels one PackRLinear forward + backward launches for
+    bf16 x (K % 8 == 0), no bias, cached lut counts: forward = [predecode] +
+    GEMM; backward = dY split + [predecode] + DX GEMM + DW GEMM + lut finalize.
+    The predecode route is taken from 1024 rows on when N % 16 == 0."""
+    pre = 1 if (M >= 1024 and N % 16 == 0) else 0
+    return (pre + 1) + (1 + pre + 1 + 1 + 1)
+
+
 def bench_ffn(args, world, rank, peaks, peak_kind):
     from packr_b200 import PackRLinear
     from packr_b200 import kernel as K
@@ -364,13 +373,23 @@ def bench_ffn(args, world, rank, peaks, peak_kind):
     value = world * flops / (ms_step * 1e-3) / 1e12
     fb_total, _ = timed(fwd_bwd, args.steps, 2, world)
     fb_ms = fb_total / args.steps
-    # dominant kernel: the forward GEMM of the gate layer, timed alone
+    # the forward of the gate layer (predecode + GEMM), then its two kernels
+    # timed alone: the GEMM over the decoded W (the dominant kernel) and the
+    # HBM-bound predecode (5 bytes per weight)
     lay, x = layers[0], xs[0].detach()
     fwd = lambda: K.forward(x, lay.W_p, lay.W_f, lay.lut, None)
     _, f_per = timed(fwd, max(args.steps, 10), 3, 1)
     f_ms = statistics.mean(f_per)
+    Wd = K.predecode_bf16(lay.W_p, lay.W_f, lay.lut)
+    _, g_per = timed(lambda: K.forward_decoded(x, Wd, None), max(args.steps, 10), 3, 1)
+    g_ms = statistics.mean(g_per)
+    _, p_per = timed(lambda: K.predecode_bf16(lay.W_p, lay.W_f, lay.lut), max(args.steps, 10), 3, 1)
+    p_ms = statistics.mean(p_per)
+    del Wd
     f_flops = 2.0 * M * FFN_HIDDEN * FFN_INTER
-    achieved = f_flops / (f_ms * 1e-3) / 1e12
+    achieved = f_flops / (g_ms * 1e-3) / 1e12
+    pre_bytes = 5.0 * FFN_HIDDEN * FFN_INTER
+    pre_gbs = pre_bytes / (p_ms * 1e-3) / 1e9
     cnt = lay.lut_counts()
     bwd = lambda: K.backward(dys[0], x, lay.W_p, lay.W_f, lay.lut, cnt, True, True, True, False)
     _, b_per = timed(bwd, max(args.steps, 10), 3, 1)
@@ -381,11 +400,25 @@ def bench_ffn(args, world, rank, peaks, peak_kind):
     dx_in = [torch.empty_like(t) for t in xs]
     ddy_in = [torch.empty_like(t) for t in dys]
 
+    copy_stream = torch.cuda.Stream()
+
     def e2e_step():
+        # all host->device copies of the step go out on a copy stream at the
+        # start of the step (after the previous step's work); layer i waits
+        # only for its own inputs, so later copies overlap earlier layers
         zero()
-        for i, (lay, hxi, hdyi) in enumerate(zip(layers, hx, hdy)):
-            dx_in[i].copy_(hxi, non_blocking=True)
-            ddy_in[i].copy_(hdyi, non_blocking=True)
+        main = torch.cuda.current_stream()
+        copy_stream.wait_stream(main)
+        ready = []
+        with torch.cuda.stream(copy_stream):
+            for i in range(len(layers)):
+                dx_in[i].copy_(hx[i], non_blocking=True)
+                ddy_in[i].copy_(hdy[i], non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(copy_stream)
+                ready.append(ev)
+        for i, lay in enumerate(layers):
+            main.wait_event(ready[i])
             xi = dx_in[i].detach().requires_grad_(True)
             lay(xi).backward(ddy_in[i])
             hres[i].copy_(lay.lut.grad, non_blocking=True)
@@ -407,16 +440,22 @@ def bench_ffn(args, world, rank, peaks, peak_kind):
                    "flops_per_step_per_gpu": flops, "l2": "inputs larger than L2 (~0.9 GB of operands per step)",
                    "parallelism": f"dp{world}, ZeRO-1 sharded 8-bit optimizer state"},
         "fwd_bwd_only": {"tflops": round(world * flops / (fb_ms * 1e-3) / 1e12, 2), "ms_per_step": round(fb_ms, 4)},
-        "phases_ms_gate_layer": {"forward": round(f_ms, 4), "backward": round(statistics.mean(b_per), 4)},
+        "phases_ms_gate_layer": {"forward": round(f_ms, 4), "forward_gemm": round(g_ms, 4),
+                                 "predecode": round(p_ms, 4), "backward": round(statistics.mean(b_per), 4)},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peaks["bf16_tflops"],
                      "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
-                     "traffic": load_traffic("packr_gemm_kernel<FWD>", "ffn_gate_M%d" % M),
+                     "traffic": load_traffic("packr_gemm_kernel<FWD,plain>", "ffn_gate_M%d" % M),
                      "peak_source": f"{peak_kind} bf16_tflops (burst; kernel timed alone)",
-                     "kernel": "packr_gemm_kernel<FWD> (gate 4096->11008)",
+                     "kernel": "packr_gemm_kernel<FWD, B_PLAIN, 512-row tiles> (gate 4096->11008, decoded W)",
                      "algorithmic_flops_per_launch": f_flops},
+        "roofline_predecode": {"bound": "hbm", "achieved": round(pre_gbs, 1), "peak": peaks["hbm_gbs"],
+                               "unit": "GB/s", "frac": round(pre_gbs / peaks["hbm_gbs"], 4),
+                               "traffic": load_traffic("predecode_kernel", "ffn_gate"),
+                               "kernel": "predecode_kernel (gate W 4096x11008)",
+                               "algorithmic_bytes_per_launch": pre_bytes},
         "e2e": {"value": round(e2e_val, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": hres.numel() * 4},
-        "gpu_launches": args.steps * (len(layers) * 5 + len(opt.groups)),
+        "gpu_launches": args.steps * (sum(layer_launches(M, k, n) for _, k, n in FFN_LAYERS) + len(opt.groups)),
         "clocks": clk.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

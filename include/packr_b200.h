@@ -95,6 +95,16 @@ int packr_forward(const void* x, int x_dtype, const uint8_t* W_p, const uint16_t
                   const void* bias, int bias_dtype, float* out, int64_t M, int64_t K, int64_t N, void* workspace,
                   size_t workspace_bytes, void* stream);
 
+/* The forward GEMM over a W already decoded to bf16 [K, N] (for example by
+ * packr_predecode_bf16, cached by a caller that runs many forwards with the
+ * same weights): out = x @ Wd + bias, same x / bias / out conventions as
+ * packr_forward.  N % 8 == 0 and Wd 16-byte aligned.  No counterpart in the
+ * reference (it decodes inside every packr_matmul call). */
+size_t packr_forward_decoded_workspace_bytes(int64_t M, int64_t K, int64_t N, int x_dtype);
+int packr_forward_decoded(const void* x, int x_dtype, const uint16_t* Wd, const void* bias, int bias_dtype,
+                          float* out, int64_t M, int64_t K, int64_t N, void* workspace, size_t workspace_bytes,
+                          void* stream);
+
 /* Backward of the forward above; replaces PackRMatmulFunction.backward of
  * reference packr/autograd.py:56-88 and the bias gradient of layer.py:97:
  *   dX[M,K]   = bf16(bf16(dY) @ W^T)      stored as x's dtype (NULL: skipped)

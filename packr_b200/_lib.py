@@ -47,6 +47,8 @@ SIGNATURES = {
     "packr_adam8_multi": (_I32, [ctypes.POINTER(AdamTensor), _I32, _F32, _F32, _F32, _F32, _F32, _F32, _F32, _VP]),
     "packr_forward_workspace_bytes": (_SZ, [_I64, _I64, _I64, _I32]),
     "packr_forward": (_I32, [_VP, _I32, _VP, _VP, _VP, _VP, _I32, _VP, _I64, _I64, _I64, _VP, _SZ, _VP]),
+    "packr_forward_decoded_workspace_bytes": (_SZ, [_I64, _I64, _I64, _I32]),
+    "packr_forward_decoded": (_I32, [_VP, _I32, _VP, _VP, _I32, _VP, _I64, _I64, _I64, _VP, _SZ, _VP]),
     "packr_backward_workspace_bytes": (_SZ, [_I64, _I64, _I64, _I32, _I32]),
     "packr_backward": (_I32, [_VP, _VP, _I32, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _I64, _I64, _I64, _I32, _VP,
                               _SZ, _VP]),

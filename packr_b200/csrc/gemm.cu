@@ -74,7 +74,11 @@ constexpr int DEC_WARPS_TMA = 8;       // decode warps, TMA-staged path
 constexpr int DEC_THREADS = DEC_WARPS * 32;
 constexpr int CHUNKS = BN_CTA * BK / 8 / DEC_THREADS;  // chunks of 8 weights per thread per stage (ring path)
 constexpr int LUT_BYTES = 256 * 32 * 4;  // one u32 per (entry, lane)
-constexpr int HIST_COPIES = 4;  // lut-gradient histogram copies per epilogue warp (lane & 3)
+// lut-gradient histogram copies per CTA (DW).  Copy c is lane-interleaved:
+// bin b of lane l is word b*32 + l, so the 32 lanes of a red.shared always
+// hit 32 different banks.  Epilogue warps 2-5 share copy 0, warps 6-9 copy 1.
+constexpr int HIST_COPIES = 2;
+constexpr int HIST_COPY_BYTES = 256 * 32 * 4;
 constexpr int ACC_COLS = BN;
 // FWD / DX switch from the fused decode to predecode + plain GEMM at this
 // many output rows (tokens): below it the decode traffic of the fused kernel
@@ -108,7 +112,7 @@ struct Cfg {
   static constexpr bool kWtma = kDecode && BSRC == B_WTMA;
   static constexpr bool kPlainB = MODE != DW && BSRC == B_PLAIN;  // FWD / DX with B by TMA
   static constexpr int kMSub = MSUB;
-  static constexpr int kStages = kWtma ? (MSUB == 2 ? 3 : 4) : (kPlainB && MSUB == 2 ? 4 : 6);
+  static constexpr int kStages = kWtma ? (MSUB == 2 ? 3 : 4) : (kPlainB && MSUB == 2 ? 4 : (MODE == DW ? 5 : 6));
   static constexpr int kABytes = MSUB * A_BYTES;            // A subtiles per stage
   static constexpr int kWpBytes = kWtma ? BN_CTA * BK : 0;  // u8 W_p tile per stage
   static constexpr int kStageBytes = kABytes + B_BYTES + kWpBytes;
@@ -128,7 +132,7 @@ struct Cfg {
   static constexpr int kThreads = kWarps * 32;
   static constexpr bool kAmn = MODE == DW;   // A stored MN-major in smem
   static constexpr bool kBmn = MODE != DX;   // B stored MN-major in smem
-  static constexpr int kHistBytes = kEpiWarps * HIST_COPIES * 256 * 4;
+  static constexpr int kHistBytes = HIST_COPIES * HIST_COPY_BYTES;
   static constexpr int kLutBytes = kDecode ? LUT_BYTES : 0;
   static constexpr int kAuxBytes = MODE == DW ? kHistBytes : kLutBytes + kStgBytes;
   static constexpr int kBarOff = kStages * kStageBytes + kAuxBytes;
@@ -589,7 +593,7 @@ __global__ void __launch_bounds__(Cfg<MODE, BSRC, MSUB>::kThreads, 1)
     const int row = q * 32 + lane;
     const uint32_t tempty0 = mapa(smem_u32(&bars->tempty[0]), 0);
     const uint32_t tempty1 = mapa(smem_u32(&bars->tempty[1]), 0);
-    const uint32_t hist_lane = smem_u32(sAux) + (uint32_t)(((warp - 2) * HIST_COPIES + (lane & 3)) * 1024);
+    const uint32_t hist_lane = smem_u32(sAux) + (uint32_t)(((warp - 2) >> 2) * HIST_COPY_BYTES + lane * 4);
     const uint32_t stg = smem_u32(sAux) + (uint32_t)(C::kLutBytes + (warp - 2) * 4096);
     // DW: the W_p bytes of the next tile's chunks are fetched before its
     // accumulator is ready (they do not depend on it)
@@ -626,8 +630,8 @@ __global__ void __launch_bounds__(Cfg<MODE, BSRC, MSUB>::kThreads, 1)
     for (int sub = 0; sub < MSUB; ++sub) {
       const int acc = MSUB == 1 ? (t_local & 1) : sub;
       const uint32_t aph = MSUB == 1 ? ((uint32_t)(t_local >> 1) & 1u) : ((uint32_t)t_local & 1u);
-      // every lane waits; the warp proceeds only if all lanes saw the phase
-      if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bars->tfull[acc], aph, abort_flag))) { alive = false; break; }
+      // one lane polls; the warp proceeds only if every lane saw the phase
+      if (!mbar_wait_warp(&bars->tfull[acc], aph, abort_flag)) { alive = false; break; }
       if (warp == 2 && lane == 0) PACKR_TRACE_EVENT(4, t_local);
       tc_fence_after();
       const int m0 = (tile % P.m_tiles) * (2 * BM * MSUB) + sub * 2 * BM + (int)rank * BM;
@@ -640,6 +644,7 @@ __global__ void __launch_bounds__(Cfg<MODE, BSRC, MSUB>::kThreads, 1)
         uint32_t v[32];
         tmem_ld_32x32b_x32(tmem_base + (uint32_t)(acc * ACC_COLS + cc * 32) + ((uint32_t)(q * 32) << 16), v);
         tmem_ld_wait();
+        if (warp == 2 && lane == 0) PACKR_TRACE_EVENT(12, (t_local * 2 + sub) * 8 + c);
         const int gn0 = n0 + cc * 32;
         // warp-uniform skip; the staged stores are collective, the others per row
         if (gn0 >= P.Ng || m0 + q * 32 >= P.Mg) continue;
@@ -717,13 +722,14 @@ __global__ void __launch_bounds__(Cfg<MODE, BSRC, MSUB>::kThreads, 1)
               }
             }
           }
+          if (warp == 2 && lane == 0) PACKR_TRACE_EVENT(13, (t_local * 2 + sub) * 8 + c);
           if (MODE == DW && want_hist) {
             const uint32_t w[8] = {wpa[c].x, wpa[c].y, wpa[c].z, wpa[c].w, wpb[c].x, wpb[c].y, wpb[c].z, wpb[c].w};
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
               if (j < nval) {
                 const uint32_t bin = (w[j >> 2] >> (8 * (j & 3))) & 0xFFu;
-                asm volatile("red.shared.add.f32 [%0], %1;" ::"r"(hist_lane + bin * 4), "f"(__uint_as_float(v[j]))
+                asm volatile("red.shared.add.f32 [%0], %1;" ::"r"(hist_lane + bin * 128), "f"(__uint_as_float(v[j]))
                              : "memory");
               }
             }
@@ -738,13 +744,15 @@ __global__ void __launch_bounds__(Cfg<MODE, BSRC, MSUB>::kThreads, 1)
     }
     if (MODE == DW && P.dlut_sum != nullptr) {
       asm volatile("bar.sync 1, %0;" ::"n"(C::kEpiWarps * 32) : "memory");
+      // bin b: every copy's 32 lane words, summed across the warp
       const float* h0 = reinterpret_cast<const float*>(sAux);
-      const int et = threadIdx.x - 64;
-      for (int b = et; b < 256; b += C::kEpiWarps * 32) {
+      for (int b = warp - 2; b < 256; b += C::kEpiWarps) {
         float s = 0.0f;
 #pragma unroll
-        for (int w = 0; w < C::kEpiWarps * HIST_COPIES; ++w) s += h0[w * 256 + b];
-        if (s != 0.0f) atomicAdd(P.dlut_sum + b, s);
+        for (int c = 0; c < HIST_COPIES; ++c) s += h0[c * (HIST_COPY_BYTES / 4) + b * 32 + lane];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
+        if (lane == 0 && s != 0.0f) atomicAdd(P.dlut_sum + b, s);
       }
     }
   } else if (C::kDecode && !C::kWtma && warp == C::kSignalWarp) {
@@ -772,7 +780,7 @@ __global__ void __launch_bounds__(Cfg<MODE, BSRC, MSUB>::kThreads, 1)
     for (int it = 0; it < total; ++it) {
       const int s = it % STAGES;
       const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
-      if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bars->wfull[s], ph, abort_flag))) break;
+      if (!mbar_wait_warp(&bars->wfull[s], ph, abort_flag)) break;
       if (t == 0) PACKR_TRACE_EVENT(6, it);
       const int tile = pair + (it / kb_total) * npairs;
       const int nb0 = (tile / P.m_tiles) * BN + (int)rank * BN_CTA;
@@ -804,7 +812,8 @@ __global__ void __launch_bounds__(Cfg<MODE, BSRC, MSUB>::kThreads, 1)
     auto process = [&](const Chunks& c, int it) {
       const int s = it % STAGES;
       const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
-      if (!*abort_flag && __all_sync(0xFFFFFFFFu, mbar_wait(&bars->empty[s], ph ^ 1u, abort_flag))) {
+      const bool go = __shfl_sync(0xFFFFFFFFu, *abort_flag ? 0 : 1, 0) != 0;  // warp-uniform
+      if (go && mbar_wait_warp(&bars->empty[s], ph ^ 1u, abort_flag)) {
         if (t == 0) PACKR_TRACE_EVENT(6, it);
         decode_store<MODE>(c, sB0 + s * B_BYTES, lut_lane, t);
         fence_proxy_async_smem();

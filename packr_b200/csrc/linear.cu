@@ -146,6 +146,56 @@ extern "C" int packr_forward(const void* x, int x_dtype, const uint8_t* W_p, con
   return gemm::launch<gemm::FWD>(P, maps, s);
 }
 
+extern "C" size_t packr_forward_decoded_workspace_bytes(int64_t M, int64_t K, int64_t N, int x_dtype) {
+  Carve c{nullptr};
+  FwdPlan p;
+  return plan_forward(c, p, M > 0 ? M : 0, K > 0 ? K : 0, N > 0 ? N : 0, x_dtype, false);
+}
+
+extern "C" int packr_forward_decoded(const void* x, int x_dtype, const uint16_t* Wd, const void* bias, int bias_dtype,
+                                     float* out, int64_t M, int64_t K, int64_t N, void* workspace,
+                                     size_t workspace_bytes, void* stream) {
+  if (M < 0 || K <= 0 || N <= 0 || M > 0x7FFFFFFFll || K > 0x7FFFFFFFll || N > 0x7FFFFFFFll) return PACKR_ERR_SHAPE;
+  if ((N & 7) != 0) return PACKR_ERR_SHAPE;  // Wd rows must be 16-byte multiples for TMA
+  if (x_dtype != PACKR_DTYPE_F32 && x_dtype != PACKR_DTYPE_BF16) return PACKR_ERR_INVALID_ARGUMENT;
+  if (Wd == nullptr || (M > 0 && (x == nullptr || out == nullptr))) return PACKR_ERR_INVALID_ARGUMENT;
+  if (bias != nullptr && bias_dtype != PACKR_DTYPE_BF16 && bias_dtype != PACKR_DTYPE_F32)
+    return PACKR_ERR_INVALID_ARGUMENT;
+  if (!aligned(Wd, 16) || (x && !aligned(x, x_dtype == PACKR_DTYPE_F32 ? 4 : 2)) || !aligned(out, 4) ||
+      (bias != nullptr && !aligned(bias, bias_dtype == PACKR_DTYPE_F32 ? 4 : 2)))
+    return PACKR_ERR_ALIGNMENT;
+  int st = check_device();
+  if (st != PACKR_OK) return st;
+  if (M == 0) return PACKR_OK;
+  cudaStream_t s = as_stream(stream);
+  Carve c{static_cast<uint8_t*>(workspace)};
+  FwdPlan p;
+  const size_t need = plan_forward(c, p, M, K, N, x_dtype, false);
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need || !aligned(workspace, kAlign)))
+    return PACKR_ERR_WORKSPACE;
+  const void* a_ptr = x;
+  long long lda = K;
+  if (p.xh != nullptr) {
+    st = prep::split_rows(x, x_dtype == PACKR_DTYPE_F32, K, M, K, p.xh, nullptr, round8(K), nullptr, s);
+    if (st != PACKR_OK) return st;
+    a_ptr = p.xh;
+    lda = round8(K);
+  }
+  gemm::Maps maps;
+  if ((st = gemm::make_map(&maps.a[0], a_ptr, K, M, lda * 2, gemm::BM)) != PACKR_OK) return st;
+  if ((st = gemm::make_map(&maps.b[0], Wd, N, K, N * 2, 64)) != PACKR_OK) return st;
+  gemm::Params P{};
+  P.Mg = (int)M;
+  P.Ng = (int)N;
+  P.Kg = (int)K;
+  P.nseg = 1;
+  P.out = out;
+  P.ld_out = N;
+  P.bias = bias;
+  P.bias_f32 = bias_dtype == PACKR_DTYPE_F32;
+  return gemm::launch_plain<gemm::FWD>(P, maps, s);
+}
+
 extern "C" size_t packr_backward_workspace_bytes(int64_t M, int64_t K, int64_t N, int x_dtype, int flags) {
   Carve c{nullptr};
   BwdPlan p;

@@ -67,8 +67,19 @@ int predecode(const uint8_t* W_p, const uint16_t* W_f, const float* lut, uint16_
   if (!wtma_ok(W_p, W_f, N) || !aligned(out, 16)) return PACKR_ERR_ALIGNMENT;
   const long long chunks = K * N / 8;
   if (chunks == 0) return PACKR_OK;
+  // as many resident blocks as fit (smem, registers), one wave: the loop
+  // strides over the chunks
+  static int per_sm[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (per_sm[dev & 63] == 0) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, predecode_kernel, kPredecodeThreads, 0) != cudaSuccess || n < 1)
+      n = 4;
+    per_sm[dev & 63] = n;
+  }
   const long long want = (chunks + kPredecodeThreads - 1) / kPredecodeThreads;
-  const long long cap = 4ll * sm_count();
+  const long long cap = (long long)per_sm[dev & 63] * sm_count();
   predecode_kernel<<<(int)(want < cap ? want : cap), kPredecodeThreads, 0, st>>>(
       reinterpret_cast<const uint2*>(W_p), reinterpret_cast<const uint4*>(W_f), lut, reinterpret_cast<uint4*>(out),
       chunks);

@@ -76,6 +76,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// Warp-wide bounded wait: lane 0 polls; once it has seen the phase complete,
+// the other lanes take the barrier's acquire themselves (their try_wait
+// succeeds at once).  One polling lane instead of 32 keeps waiting warps off
+// the shared-memory pipe.  The result is the same in every lane.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  const int lane = threadIdx.x & 31;
+  bool ok = true;
+  if (lane == 0) ok = mbar_wait(bar, parity, abort_flag);
+  ok = __shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0) != 0;
+  if (ok && lane != 0) ok = mbar_wait(bar, parity, abort_flag);
+  return __all_sync(0xFFFFFFFFu, ok);
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");

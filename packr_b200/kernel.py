@@ -81,6 +81,32 @@ def forward(x: torch.Tensor, W_p: torch.Tensor, W_f: torch.Tensor, lut: torch.Te
     return out
 
 
+def forward_decoded(x: torch.Tensor, Wd: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """out[M, N] float32 = x @ Wd + bias for an already decoded bf16 Wd [K, N]
+    (predecode_bf16), through the plain tcgen05 GEMM."""
+    lib = _lib.load()
+    x = _as_operand(x)
+    M, K = x.shape
+    N = Wd.shape[1]
+    dev = x.device
+    if Wd.dtype != torch.bfloat16 or tuple(Wd.shape) != (K, N):
+        raise ValueError("Wd must be bf16 [K, N]")
+    Wd = Wd.contiguous()
+    if bias is not None:
+        bias = bias.detach()
+        if bias.dtype not in (torch.bfloat16, torch.float32):
+            bias = bias.float()
+        bias = bias.contiguous()
+    out = torch.empty(M, N, dtype=torch.float32, device=dev)
+    xd = _dtype_code(x)
+    with torch.cuda.device(dev):
+        ws = _workspace(lib.packr_forward_decoded_workspace_bytes(M, K, N, xd), dev)
+        code = lib.packr_forward_decoded(_ptr(x), xd, _ptr(Wd), _ptr(bias), _dtype_code(bias) if bias is not None else 0,
+                                         _ptr(out), M, K, N, _ptr(ws), 0 if ws is None else ws.numel(), _stream(dev))
+    _lib.check("packr_forward_decoded", code)
+    return out
+
+
 def bincount256(W_p: torch.Tensor) -> torch.Tensor:
     """int32[256] counts of the byte values of W_p (on W_p's device)."""
     lib = _lib.load()

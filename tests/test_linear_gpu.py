@@ -110,6 +110,23 @@ def test_predecode_bit_exact_extreme_lut(cuda):
     assert np.array_equal(got, oracle.decode_bf16(bits(c["W_p"]), bits(W_f), bits(lut)))
 
 
+@pytest.mark.parametrize("M,Kd,Nd,dt,bias", [(512, 1024, 512, torch.bfloat16, True), (1100, 200, 264, torch.float32, True),
+                                            (1, 64, 48, torch.bfloat16, False)])
+def test_forward_decoded(cuda, M, Kd, Nd, dt, bias):
+    """The plain GEMM over a predecoded W against the oracle; from 1024 rows on
+    it is exactly what packr_forward runs after its own predecode."""
+    c_cpu = linear_case(M, Kd, Nd, x_dtype=dt, bias=bias, seed=M + 7)
+    c = to_cuda(c_cpu)
+    n = {k: bits(v) for k, v in c_cpu.items() if v is not None}
+    ref = oracle.linear_forward(n["x"], n["W_p"], n["W_f"], n["lut"], n.get("bias"), x_is_bf16=dt == torch.bfloat16)
+    Wd = K.decode_bf16(c["W_p"], c["W_f"], c["lut"])
+    out = K.forward_decoded(c["x"], Wd, c["bias"])
+    torch.cuda.synchronize()
+    assert oracle.max_rel(bits(out), ref) <= TOL
+    if M >= 1024 and Nd % 16 == 0:
+        assert torch.equal(out, K.forward(c["x"], c["W_p"], c["W_f"], c["lut"], c["bias"]))
+
+
 def test_forward_route_follows_workspace(cuda):
     """A workspace sized for the fused route (no room for the decoded W) makes
     the forward fall back to it; both routes give the same bits."""
