@@ -86,6 +86,10 @@ constexpr int ACC_COLS = BN;
 #ifndef PACKR_PREDECODE_MIN_M
 #define PACKR_PREDECODE_MIN_M 1024
 #endif
+// Stream-K work split for the GEMMs without a fused decode (1: on).
+#ifndef PACKR_STREAM_K
+#define PACKR_STREAM_K 1
+#endif
 // Plain GEMMs use 512-row pair tiles from this many rows on.
 #ifndef PACKR_PLAIN_MSUB2_MIN_M
 #define PACKR_PLAIN_MSUB2_MIN_M 1024
@@ -123,6 +127,10 @@ struct Cfg {
   // per-warp shared-memory buffer, so that global stores cover whole rows
   // segments of 128 (f32) or 64 (bf16) bytes instead of 16 bytes per row.
   static constexpr bool kStageOut = kWtma || kPlainB;
+  // stream-K code compiled in (used when Params::sk): the plain FWD / DX
+  // GEMMs only (for DW the split-tile fix-up measured slower than the wave
+  // quantisation it removes)
+  static constexpr bool kStreamK = kPlainB;
   static constexpr int kStgBytes = kStageOut ? kEpiWarps * 4096 : 0;
   static constexpr int kChunksPerEpiWarp = (BN / 32) / (kEpiWarps / 4);
   static constexpr int kDecWarp0 = 2 + kEpiWarps;             // first decode warp
@@ -165,7 +173,74 @@ struct Params {
   float* dlut_sum;           // DW: [256], nullable
   int out_vec;               // out base 16-B aligned
   int idx_vec;               // hist_idx base 16-B aligned
+  // stream-K (sk = 1): the (tile, k-block) iteration space is cut into equal
+  // contiguous ranges, one per CTA pair.  A tile split between pairs p and
+  // p+1: p+1 computes its last k-blocks first ("head") and leaves the f32
+  // partial in sk_partial slot p+1; p computes its first k-blocks last
+  // ("tail"), adds the partial and runs the epilogue.
+  int sk;
+  float* sk_partial;         // [pairs][MSUB][2 ranks][256 cols][128 rows]
+  int* sk_flags;             // [pairs][2 ranks][epilogue warps], zeroed before the launch
+  int sk_slots;              // pairs the two buffers above have room for (0: no stream-K)
+  int sk_dp_tiles;           // with sk: tiles [0, sk_dp_tiles) go round-robin first (whole tiles)
 };
+
+// Workspace for stream-K: partial slots and flags for up to `pairs` CTA pairs.
+inline size_t sk_partial_bytes(int pairs, int msub) { return (size_t)pairs * msub * 2 * BN * BM * sizeof(float); }
+inline size_t sk_flag_bytes(int pairs) { return (size_t)pairs * 2 * 8 * sizeof(int); }
+
+// One unit of a pair's work: k-blocks [k0, k1) of one tile.
+struct Unit {
+  int tile, k0, k1;
+  int kind;  // 0 whole tile, 1 head (partial to the workspace), 2 tail (adds the next pair's head)
+};
+
+// The sequence of units of one CTA pair; every role walks the same sequence:
+// whole tiles round-robin (tile = pair + i * pairs) below dp_tiles, then, with
+// stream-K, this pair's contiguous share of the remaining (tile, k-block)
+// iterations.  Round-robin keeps the tiles in flight at once adjacent (shared
+// operands stay in L2); the stream-K tail balances the last wave.
+struct Sched {
+  long long g, g_end;  // stream-K iteration range (tile * kb_total + k-block)
+  int tile, step, dp_end, kb_total;
+  bool sk;
+};
+
+__device__ __forceinline__ Sched make_sched(const Params& P, int pair, int npairs) {
+  Sched s;
+  s.kb_total = P.nseg * P.k_blocks;
+  const int num_tiles = P.m_tiles * P.n_tiles;
+  s.sk = P.sk != 0;
+  s.dp_end = s.sk ? P.sk_dp_tiles : num_tiles;
+  const long long T = (long long)(num_tiles - s.dp_end) * s.kb_total;
+  const long long base = (long long)s.dp_end * s.kb_total;
+  s.g = base + T * pair / npairs;
+  s.g_end = base + T * (pair + 1) / npairs;
+  s.tile = pair;
+  s.step = npairs;
+  return s;
+}
+
+__device__ __forceinline__ bool next_unit(Sched& s, Unit& u) {
+  if (s.tile < s.dp_end) {
+    u.tile = s.tile;
+    u.k0 = 0;
+    u.k1 = s.kb_total;
+    u.kind = 0;
+    s.tile += s.step;
+    return true;
+  }
+  if (!s.sk || s.g >= s.g_end) return false;
+  const long long tile = s.g / s.kb_total;
+  const long long t0 = tile * s.kb_total, t1 = t0 + s.kb_total;
+  const long long e = s.g_end < t1 ? s.g_end : t1;
+  u.tile = (int)tile;
+  u.k0 = (int)(s.g - t0);
+  u.k1 = (int)(e - t0);
+  u.kind = u.k0 > 0 ? 1 : (u.k1 < s.kb_total ? 2 : 0);
+  s.g = e;
+  return true;
+}
 
 struct Maps {
   CUtensorMap a[3];
@@ -405,6 +480,38 @@ __device__ __forceinline__ void store_rows_staged(uint32_t stg, const float* v, 
   __syncwarp();
 }
 
+// Bounded wait for a stream-K flag written by another CTA pair of the same
+// launch (all pairs are resident at once).  Lane 0 polls with acquire loads
+// and decides; the result is the same in every lane, and the warp barrier
+// orders the other lanes' later loads after lane 0's acquire.  Gives up like
+// mbar_wait.
+__device__ __forceinline__ bool wait_flag(const int* f, volatile int* abort_flag) {
+  int ok = 0;
+  if ((threadIdx.x & 31) == 0) {
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 0;; ++i) {
+      int v;
+      asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+      if (v != 0) {
+        ok = 1;
+        break;
+      }
+      if ((i & 63u) == 63u) {
+        if (*abort_flag) break;
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          *abort_flag = 1;
+          atomicExch(&g_wait_timeout, 1u);
+          break;
+        }
+        __nanosleep(200);
+      }
+    }
+  }
+  ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+  __syncwarp();
+  return ok != 0;
+}
+
 // ------------------------------------------------------------------ kernel
 template <int MODE, int BSRC, int MSUB>
 __global__ void __launch_bounds__(Cfg<MODE, BSRC, MSUB>::kThreads, 1)
@@ -480,10 +587,13 @@ __global__ void __launch_bounds__(Cfg<MODE, BSRC, MSUB>::kThreads, 1)
     if (lane == 0) {
       int it = 0;
       bool ok = true;
-      for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
+      Sched sc = make_sched(P, pair, npairs);
+      Unit u;
+      while (ok && next_unit(sc, u)) {
+        const int tile = u.tile;
         const int m0 = (tile % P.m_tiles) * (2 * BM * MSUB) + (int)rank * BM;
         const int n0 = (tile / P.m_tiles) * BN + (int)rank * BN_CTA;
-        for (int kk = 0; kk < kb_total; ++kk, ++it) {
+        for (int kk = u.k0; kk < u.k1; ++kk, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
           if (!mbar_wait(&bars->empty[s], ph ^ 1u, abort_flag)) { ok = false; break; }
@@ -539,7 +649,9 @@ __global__ void __launch_bounds__(Cfg<MODE, BSRC, MSUB>::kThreads, 1)
       int it = 0, t_local = 0;
       bool ok = true;
       const uint32_t sA0 = smem_u32(sA), sB0 = smem_u32(sB);
-      for (int tile = pair; tile < num_tiles && ok; tile += npairs, ++t_local) {
+      Sched sc = make_sched(P, pair, npairs);
+      Unit u;
+      for (; ok && next_unit(sc, u); ++t_local) {
         // accumulator slots (256 TMEM columns each): MSUB = 1 alternates the
         // two slots between tiles; MSUB = 2 uses slot `sub` for subtile `sub`
         const int acc = MSUB == 1 ? (t_local & 1) : 0;
@@ -547,7 +659,7 @@ __global__ void __launch_bounds__(Cfg<MODE, BSRC, MSUB>::kThreads, 1)
         if (!mbar_wait(&bars->tempty[acc], aph ^ 1u, abort_flag)) { ok = false; break; }
         PACKR_TRACE_EVENT(3, t_local);
         tc_fence_after();
-        for (int kk = 0; kk < kb_total; ++kk, ++it) {
+        for (int kk = u.k0; kk < u.k1; ++kk, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
           if (!mbar_wait(&bars->full[s], ph, abort_flag)) { ok = false; break; }
@@ -558,7 +670,7 @@ __global__ void __launch_bounds__(Cfg<MODE, BSRC, MSUB>::kThreads, 1)
           const uint32_t a_s = sA0 + s * C::kABytes, b_s = sB0 + s * B_BYTES;
 #pragma unroll
           for (int sub = 0; sub < MSUB; ++sub) {
-            if (sub == 1 && kk == 0) {  // subtile 1's accumulator is released after subtile 0's
+            if (sub == 1 && kk == u.k0) {  // subtile 1's accumulator is released after subtile 0's
               if (!mbar_wait(&bars->tempty[1], aph ^ 1u, abort_flag)) { ok = false; break; }
               tc_fence_after();
             }
@@ -568,10 +680,10 @@ __global__ void __launch_bounds__(Cfg<MODE, BSRC, MSUB>::kThreads, 1)
             for (int k = 0; k < BK / UK; ++k) {
               const uint64_t bd = C::kBmn ? sdesc_sw128(b_s + k * 2048, 8192, 1024) : sdesc_sw128(b_s + k * 32, 16, 1024);
               const uint64_t ad = C::kAmn ? sdesc_sw128(a_sub + k * 2048, 8192, 1024) : sdesc_sw128(a_sub + k * 32, 16, 1024);
-              umma_bf16_pair(d_tmem, ad, bd, C::kIdesc, (kk | k) != 0 ? 1u : 0u);
+              umma_bf16_pair(d_tmem, ad, bd, C::kIdesc, (kk != u.k0 || k != 0) ? 1u : 0u);
             }
             // subtile 0 complete: its drain overlaps subtile 1's last MMAs
-            if (MSUB == 2 && sub == 0 && kk == kb_total - 1) umma_commit_pair(&bars->tfull[0], PAIR_MASK);
+            if (MSUB == 2 && sub == 0 && kk == u.k1 - 1) umma_commit_pair(&bars->tfull[0], PAIR_MASK);
           }
           if (!ok) break;
           umma_commit_pair(&bars->empty[s], PAIR_MASK);
@@ -623,10 +735,16 @@ __global__ void __launch_bounds__(Cfg<MODE, BSRC, MSUB>::kThreads, 1)
       }
     };
     const bool want_hist = MODE == DW && P.hist_idx != nullptr;
-    if (want_hist && pair < num_tiles) fetch_idx(pair);
+    const int ew = warp - 2;  // epilogue warp index
+    Sched sc = make_sched(P, pair, npairs);
+    Unit u, un;
+    bool have = next_unit(sc, u);
+    if (want_hist && have) fetch_idx(u.tile);
     int t_local = 0;
     bool alive = true;
-    for (int tile = pair; tile < num_tiles && alive; tile += npairs, ++t_local)
+    for (; have && alive; ++t_local) {
+    const bool have_next = next_unit(sc, un);
+    const int tile = u.tile;
     for (int sub = 0; sub < MSUB; ++sub) {
       const int acc = MSUB == 1 ? (t_local & 1) : sub;
       const uint32_t aph = MSUB == 1 ? ((uint32_t)(t_local >> 1) & 1u) : ((uint32_t)t_local & 1u);
@@ -638,6 +756,15 @@ __global__ void __launch_bounds__(Cfg<MODE, BSRC, MSUB>::kThreads, 1)
       const int n0 = (tile / P.m_tiles) * BN;
       const long long gm = (long long)m0 + row;
       const bool row_ok = gm < P.Mg;
+      // stream-K partial slots ([col][row] f32, this CTA rank's 128 rows)
+      float* const my_slot = P.sk_partial + (((size_t)pair * MSUB + sub) * 2 + rank) * (size_t)(BN * BM);
+      const float* const next_slot = P.sk_partial + (((size_t)(pair + 1) * MSUB + sub) * 2 + rank) * (size_t)(BN * BM);
+      if (C::kStreamK && u.kind == 2 && sub == 0) {  // tail: the next pair's head partial must be published
+        if (!wait_flag(P.sk_flags + ((pair + 1) * 2 + (int)rank) * C::kEpiWarps + ew, abort_flag)) {
+          alive = false;
+          break;
+        }
+      }
 #pragma unroll
       for (int c = 0; c < C::kChunksPerEpiWarp; ++c) {
         const int cc = cc0 + c;
@@ -648,6 +775,16 @@ __global__ void __launch_bounds__(Cfg<MODE, BSRC, MSUB>::kThreads, 1)
         const int gn0 = n0 + cc * 32;
         // warp-uniform skip; the staged stores are collective, the others per row
         if (gn0 >= P.Ng || m0 + q * 32 >= P.Mg) continue;
+        if (C::kStreamK && u.kind == 1) {  // head: raw partial, coalesced along rows
+#pragma unroll
+          for (int j = 0; j < 32; ++j) __stcg(my_slot + (cc * 32 + j) * BM + row, __uint_as_float(v[j]));
+          continue;
+        }
+        if (C::kStreamK && u.kind == 2) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            v[j] = __float_as_uint(__fadd_rn(__uint_as_float(v[j]), __ldcg(next_slot + (cc * 32 + j) * BM + row)));
+        }
         if (!C::kStageOut && !row_ok) continue;
         const int nval = min(32, P.Ng - gn0);
         if (MODE == FWD) {
@@ -740,7 +877,18 @@ __global__ void __launch_bounds__(Cfg<MODE, BSRC, MSUB>::kThreads, 1)
       __syncwarp();
       if (warp == 2 && lane == 0) PACKR_TRACE_EVENT(5, t_local);
       if (lane == 0) mbar_arrive_cluster(acc ? tempty1 : tempty0);
-      if (want_hist && tile + npairs < num_tiles) fetch_idx(tile + npairs);
+    }
+    if (C::kStreamK && alive && u.kind == 1) {  // publish this warp's part of the head partial
+      __threadfence();
+      __syncwarp();
+      if (lane == 0) {
+        int* f = P.sk_flags + (pair * 2 + (int)rank) * C::kEpiWarps + ew;
+        asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(f), "r"(1) : "memory");
+      }
+    }
+    if (want_hist && have_next) fetch_idx(un.tile);
+    u = un;
+    have = have_next;
     }
     if (MODE == DW && P.dlut_sum != nullptr) {
       asm volatile("bar.sync 1, %0;" ::"n"(C::kEpiWarps * 32) : "memory");
@@ -909,21 +1057,10 @@ template <int MODE, int BSRC, int MSUB = 1>
 int launch_impl(Params P, const Maps& maps, cudaStream_t stream) {
   using C = Cfg<MODE, BSRC, MSUB>;
   static std::once_flag attr_once[64];
+  static int resident_pairs[64];
   int dev = 0;
   cudaGetDevice(&dev);
-  int attr_rc = 0;
-  std::call_once(attr_once[dev & 63], [&] {
-    attr_rc = cudaFuncSetAttribute(packr_gemm_kernel<MODE, BSRC, MSUB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   C::kSmemBytes) != cudaSuccess;
-  });
-  if (attr_rc) return PACKR_ERR_CUDA;
-  P.m_tiles = (P.Mg + 2 * BM * MSUB - 1) / (2 * BM * MSUB);
-  const int tiles = P.m_tiles * P.n_tiles;
-  if (tiles == 0) return PACKR_OK;
-  const int max_pairs = sm_count() / 2;
-  const int pairs = tiles < max_pairs ? tiles : max_pairs;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2 * pairs, 1, 1);
   cfg.blockDim = dim3(C::kThreads, 1, 1);
   cfg.dynamicSmemBytes = C::kSmemBytes;
   cfg.stream = stream;
@@ -934,6 +1071,47 @@ int launch_impl(Params P, const Maps& maps, cudaStream_t stream) {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  int attr_rc = 0;
+  std::call_once(attr_once[dev & 63], [&] {
+    attr_rc = cudaFuncSetAttribute(packr_gemm_kernel<MODE, BSRC, MSUB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   C::kSmemBytes) != cudaSuccess;
+    // CTA pairs that can be resident at once (a cluster needs two free SMs
+    // of one GPC): the persistent grid is never larger
+    cudaLaunchConfig_t q = cfg;
+    q.gridDim = dim3(2 * (sm_count() / 2), 1, 1);
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, packr_gemm_kernel<MODE, BSRC, MSUB>, &q) != cudaSuccess || n < 1) {
+      cudaGetLastError();
+      n = sm_count() / 2;
+    }
+    resident_pairs[dev & 63] = n;
+  });
+  if (attr_rc) return PACKR_ERR_CUDA;
+  P.m_tiles = (P.Mg + 2 * BM * MSUB - 1) / (2 * BM * MSUB);
+  const int tiles = P.m_tiles * P.n_tiles;
+  if (tiles == 0) return PACKR_OK;
+  const int max_pairs = resident_pairs[dev & 63];
+  const int pairs = tiles < max_pairs ? tiles : max_pairs;
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  // stream-K when every pair gets at least one tile's worth of k-blocks (so a
+  // tile is split between two pairs at most) and the workspace has the slots
+  P.sk = 0;
+  if (C::kStreamK && PACKR_STREAM_K && P.sk_partial != nullptr && P.sk_flags != nullptr && pairs > 1 &&
+      pairs <= P.sk_slots) {
+    const long long kbt = (long long)P.nseg * P.k_blocks;
+    // Only when the last wave of whole tiles would be less than half full:
+    // a split tile costs an extra accumulator drain and a partial read, more
+    // than a fuller last wave wastes.  Whole waves but the last go
+    // round-robin; the stream-K share of the rest is at least one tile per
+    // pair.
+    const int waves = tiles / pairs, rem = tiles % pairs;
+    P.sk_dp_tiles = waves >= 2 ? (waves - 1) * pairs : 0;
+    if (waves >= 1 && rem != 0 && rem * 2 <= pairs && (long long)(tiles - P.sk_dp_tiles) * kbt / pairs >= kbt) {
+      P.sk = 1;
+      if (cudaMemsetAsync(P.sk_flags, 0, (size_t)pairs * 2 * C::kEpiWarps * sizeof(int), stream) != cudaSuccess)
+        return PACKR_ERR_CUDA;
+    }
+  }
   if (cudaLaunchKernelEx(&cfg, packr_gemm_kernel<MODE, BSRC, MSUB>, P, maps) != cudaSuccess) {
     cudaGetLastError();
     return PACKR_ERR_LAUNCH;

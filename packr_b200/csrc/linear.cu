@@ -30,28 +30,45 @@ bool x_needs_copy(int x_dtype, long long K) { return x_dtype == PACKR_DTYPE_F32 
 // workspace holds the decoded W; otherwise the fused-decode GEMM runs.
 inline bool predecode_eligible(long long M, long long N) { return M >= PACKR_PREDECODE_MIN_M && (N & 15) == 0; }
 
+// Stream-K scratch (partial tiles and flags) for up to this many CTA pairs.
+inline int sk_pairs() { return sm_count() / 2; }
+inline int plain_msub(long long M) { return M >= PACKR_PLAIN_MSUB2_MIN_M ? 2 : 1; }
+
 struct FwdPlan {
   uint16_t* xh;
   uint16_t* wd;  // decoded W [K, N] (predecode route only)
+  float* skp;    // stream-K partials / flags (predecode route only)
+  int* skf;
 };
 
-size_t plan_forward(Carve& c, FwdPlan& p, long long M, long long K, long long N, int x_dtype, bool pre) {
+size_t plan_forward(Carve& c, FwdPlan& p, long long M, long long K, long long N, int x_dtype, bool pre,
+                    bool sk = false) {
   p.xh = x_needs_copy(x_dtype, K) ? c.take<uint16_t>((size_t)M * round8(K)) : nullptr;
   p.wd = pre ? c.take<uint16_t>((size_t)K * N) : nullptr;
+  const bool use_sk = pre && sk;
+  p.skp = use_sk ? c.take<float>(gemm::sk_partial_bytes(sk_pairs(), plain_msub(M)) / sizeof(float)) : nullptr;
+  p.skf = use_sk ? c.take<int>(gemm::sk_flag_bytes(sk_pairs()) / sizeof(int)) : nullptr;
   return c.off;
 }
 
 struct BwdPlan {
   uint16_t *dh, *dl, *xh, *xl;
   uint16_t* wd;  // decoded W [K, N] (predecode route for dX only)
+  float* skp;    // stream-K partials / flags, shared by the dX and dW GEMMs
+  int* skf;
   float *colsum, *dlut_sum;
   int32_t* counts;
 };
 
 size_t plan_backward(Carve& c, BwdPlan& p, long long M, long long K, long long N, int x_dtype, int flags,
-                     bool want_dx, bool want_dw, bool want_dlut, bool want_dbias, bool have_counts, bool pre) {
+                     bool want_dx, bool want_dw, bool want_dlut, bool want_dbias, bool have_counts, bool pre,
+                     bool sk = false) {
   const bool split = (flags & PACKR_BWD_DW_SPLIT) != 0 && (want_dw || want_dlut);
   p.wd = pre && want_dx ? c.take<uint16_t>((size_t)K * N) : nullptr;
+  const bool use_sk = sk && ((pre && want_dx) || want_dw || want_dlut);
+  const int msub = pre && want_dx ? plain_msub(M) : 1;
+  p.skp = use_sk ? c.take<float>(gemm::sk_partial_bytes(sk_pairs(), msub) / sizeof(float)) : nullptr;
+  p.skf = use_sk ? c.take<int>(gemm::sk_flag_bytes(sk_pairs()) / sizeof(int)) : nullptr;
   p.dh = c.take<uint16_t>((size_t)M * round8(N));
   p.dl = split ? c.take<uint16_t>((size_t)M * round8(N)) : nullptr;
   const bool need_x = want_dw || want_dlut;
@@ -86,7 +103,8 @@ extern "C" size_t packr_forward_workspace_bytes(int64_t M, int64_t K, int64_t N,
   M = M > 0 ? M : 0;
   K = K > 0 ? K : 0;
   N = N > 0 ? N : 0;
-  return plan_forward(c, p, M, K, N, x_dtype, predecode_eligible(M, N));
+  const bool pre = predecode_eligible(M, N);
+  return plan_forward(c, p, M, K, N, x_dtype, pre, pre);
 }
 
 extern "C" int packr_forward(const void* x, int x_dtype, const uint8_t* W_p, const uint16_t* W_f, const float* lut,
@@ -101,14 +119,20 @@ extern "C" int packr_forward(const void* x, int x_dtype, const uint8_t* W_p, con
   if ((st = check_device()) != PACKR_OK) return st;
   if (M == 0) return PACKR_OK;
   cudaStream_t s = as_stream(stream);
-  bool pre = predecode_eligible(M, N) && gemm::wtma_ok(W_p, W_f, N);
+  // the richest route the workspace holds: predecode + stream-K, predecode,
+  // fused decode
+  const bool pre_ok = predecode_eligible(M, N) && gemm::wtma_ok(W_p, W_f, N);
   Carve c{static_cast<uint8_t*>(workspace)};
   FwdPlan p;
-  size_t need = plan_forward(c, p, M, K, N, x_dtype, pre);
-  if (pre && workspace_bytes < need) {  // workspace sized for the fused route
-    pre = false;
+  bool pre = false;
+  size_t need = 0;
+  const bool tries[3][2] = {{true, true}, {true, false}, {false, false}};
+  for (const auto& t : tries) {
+    if (t[0] && !pre_ok) continue;
     c = Carve{static_cast<uint8_t*>(workspace)};
-    need = plan_forward(c, p, M, K, N, x_dtype, false);
+    need = plan_forward(c, p, M, K, N, x_dtype, t[0], t[1]);
+    pre = t[0];
+    if (workspace_bytes >= need) break;
   }
   if (need > 0 && (workspace == nullptr || workspace_bytes < need || !aligned(workspace, kAlign)))
     return PACKR_ERR_WORKSPACE;
@@ -138,6 +162,9 @@ extern "C" int packr_forward(const void* x, int x_dtype, const uint8_t* W_p, con
   P.ld_out = N;
   P.bias = bias;
   P.bias_f32 = bias_dtype == PACKR_DTYPE_F32;
+  P.sk_partial = p.skp;
+  P.sk_flags = p.skf;
+  P.sk_slots = p.skp != nullptr ? sk_pairs() : 0;
   if (pre) {
     if ((st = gemm::predecode(W_p, W_f, lut, p.wd, K, N, s)) != PACKR_OK) return st;
     if ((st = gemm::make_map(&maps.b[0], p.wd, N, K, N * 2, 64)) != PACKR_OK) return st;
@@ -202,7 +229,7 @@ extern "C" size_t packr_backward_workspace_bytes(int64_t M, int64_t K, int64_t N
   M = M > 0 ? M : 0;
   K = K > 0 ? K : 0;
   N = N > 0 ? N : 0;
-  return plan_backward(c, p, M, K, N, x_dtype, flags, true, true, true, true, false, predecode_eligible(M, N));
+  return plan_backward(c, p, M, K, N, x_dtype, flags, true, true, true, true, false, predecode_eligible(M, N), true);
 }
 
 extern "C" int packr_backward(const float* dY, const void* x, int x_dtype, const uint8_t* W_p, const uint16_t* W_f,
@@ -227,16 +254,20 @@ extern "C" int packr_backward(const float* dY, const void* x, int x_dtype, const
     if (want_dbias && cudaMemsetAsync(dbias, 0, (size_t)N * 2, s) != cudaSuccess) return PACKR_ERR_CUDA;
     return PACKR_OK;
   }
-  bool pre = want_dx && predecode_eligible(M, N) && gemm::wtma_ok(W_p, W_f, N);
+  // the richest route the workspace holds (predecode for dX, stream-K)
+  const bool pre_ok = want_dx && predecode_eligible(M, N) && gemm::wtma_ok(W_p, W_f, N);
   Carve c{static_cast<uint8_t*>(workspace)};
   BwdPlan p;
-  size_t need = plan_backward(c, p, M, K, N, x_dtype, flags, want_dx, want_dw, want_dlut, want_dbias,
-                              lut_counts != nullptr, pre);
-  if (pre && workspace_bytes < need) {  // workspace sized for the fused route
-    pre = false;
+  bool pre = false;
+  size_t need = 0;
+  const bool tries[4][2] = {{true, true}, {true, false}, {false, true}, {false, false}};
+  for (const auto& t : tries) {
+    if (t[0] && !pre_ok) continue;
     c = Carve{static_cast<uint8_t*>(workspace)};
     need = plan_backward(c, p, M, K, N, x_dtype, flags, want_dx, want_dw, want_dlut, want_dbias,
-                         lut_counts != nullptr, false);
+                         lut_counts != nullptr, t[0], t[1]);
+    pre = t[0];
+    if (workspace_bytes >= need) break;
   }
   if (workspace == nullptr || workspace_bytes < need || !aligned(workspace, kAlign)) return PACKR_ERR_WORKSPACE;
   if (p.colsum && cudaMemsetAsync(p.colsum, 0, (size_t)N * 4, s) != cudaSuccess) return PACKR_ERR_CUDA;
@@ -262,6 +293,9 @@ extern "C" int packr_backward(const float* dY, const void* x, int x_dtype, const
     P.out = dX;
     P.ld_out = K;
     P.out_f32 = x_dtype == PACKR_DTYPE_F32;
+    P.sk_partial = p.skp;
+    P.sk_flags = p.skf;
+    P.sk_slots = p.skp != nullptr ? sk_pairs() : 0;
     if (pre) {
       if ((st = gemm::predecode(W_p, W_f, lut, p.wd, K, N, s)) != PACKR_OK) return st;
       if ((st = gemm::make_map(&maps.b[0], p.wd, N, K, N * 2, gemm::BN_CTA)) != PACKR_OK) return st;
@@ -303,6 +337,9 @@ extern "C" int packr_backward(const float* dY, const void* x, int x_dtype, const
     P.ld_out = N;
     P.hist_idx = want_dlut ? W_p : nullptr;
     P.dlut_sum = p.dlut_sum;
+    P.sk_partial = p.skp;
+    P.sk_flags = p.skf;
+    P.sk_slots = p.skp != nullptr ? sk_pairs() : 0;
     if ((st = gemm::launch<gemm::DW>(P, maps, s)) != PACKR_OK) return st;
   }
   const int32_t* counts = lut_counts;

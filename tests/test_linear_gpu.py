@@ -188,6 +188,9 @@ CASES = [
     (300, 512, 1024, torch.float32, False),    # one 512-row tile, upper subtile partial
     (1500, 320, 528, torch.bfloat16, True),    # predecode + plain GEMM, ragged M / K / N tiles
     (1100, 192, 264, torch.float32, True),     # large M but N % 16 != 0: fused register-ring route
+    (1024, 2048, 9728, torch.bfloat16, True),  # stream-K split of 76 FWD tiles over 74 pairs
+    (512, 1024, 5120, torch.float32, True),    # f32 x: 3 dW reduction segments
+    (4096, 2560, 512, torch.bfloat16, False),  # stream-K split of 80 DX tiles over 74 pairs
     (16, 4096, 11008, torch.bfloat16, True),   # Llama-7B gate/up, decode-bound M
     (16, 11008, 4096, torch.bfloat16, True),   # Llama-7B down
 ]
