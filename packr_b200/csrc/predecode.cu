@@ -17,7 +17,7 @@ namespace packr {
 namespace gemm {
 
 constexpr int kPredecodeThreads = 256;
-constexpr int kPredecodeUnroll = 4;
+constexpr int kPredecodeUnroll = 8;
 
 __device__ __forceinline__ uint4 decode8(const uint4 f, const uint2 w, const uint32_t* lut_lane) {
   const uint32_t ww[2] = {w.x, w.y};

@@ -15,6 +15,33 @@ constexpr int kRowsPerCta = 32;
 //   lo[r, c] = bf16(v - f32(hi))  (optional; v - f32(hi) is exact in f32)
 //   colsum[c] += sum over rows of v, in f32 (optional)
 // Each thread owns 8 consecutive columns of kRowsPerCta rows.
+// Loads one row segment of 8 values (vector path).
+template <bool SRC_F32>
+__device__ __forceinline__ void load8(const void* src, long long off, float* v) {
+  if (SRC_F32) {
+    const float4* s = reinterpret_cast<const float4*>(static_cast<const float*>(src) + off);
+    const float4 a = __ldcs(s);
+    const float4 b = __ldcs(s + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+    const uint4 a = __ldcs(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(src) + off));
+    const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      v[2 * j] = __uint_as_float(w[j] << 16);
+      v[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+    }
+  }
+}
+
+// src [R, C] (f32 or bf16, row stride ld_src elements) ->
+//   hi[r, c] = bf16(v)           (row stride ld_dst)
+//   lo[r, c] = bf16(v - f32(hi))  (optional; v - f32(hi) is exact in f32)
+//   colsum[c] += sum over rows of v, in f32 (optional)
+// Each thread owns 8 consecutive columns of kRowsPerCta rows; rows go in
+// groups of kRowUnroll whose loads are all issued before any is used, so
+// every thread keeps several 16-byte loads in flight.
+constexpr int kRowUnroll = 4;
 template <bool SRC_F32>
 __global__ void __launch_bounds__(kThreads) split_rows_kernel(const void* __restrict__ src, long long ld_src, int R,
                                                              int C, uint16_t* __restrict__ hi,
@@ -27,33 +54,7 @@ __global__ void __launch_bounds__(kThreads) split_rows_kernel(const void* __rest
   const int nc = (int)min(8ll, (long long)C - c0);
   const bool vec = nc == 8 && (ld_src & 7) == 0 && (ld_dst & 7) == 0;
   float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  for (int r = r0; r < r1; ++r) {
-    float v[8];
-    if (SRC_F32) {
-      const float* s = static_cast<const float*>(src) + (long long)r * ld_src + c0;
-      if (vec) {
-        const float4 a = __ldcs(reinterpret_cast<const float4*>(s));
-        const float4 b = __ldcs(reinterpret_cast<const float4*>(s) + 1);
-        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-      } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = j < nc ? s[j] : 0.0f;
-      }
-    } else {
-      const uint16_t* s = static_cast<const uint16_t*>(src) + (long long)r * ld_src + c0;
-      if (vec) {
-        const uint4 a = __ldcs(reinterpret_cast<const uint4*>(s));
-        const uint32_t w[4] = {a.x, a.y, a.z, a.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          v[2 * j] = __uint_as_float(w[j] << 16);
-          v[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = j < nc ? bf16_to_f32(s[j]) : 0.0f;
-      }
-    }
+  auto emit = [&](int r, const float* v) {
     uint32_t h[4], l[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -74,14 +75,44 @@ __global__ void __launch_bounds__(kThreads) split_rows_kernel(const void* __rest
       *reinterpret_cast<uint4*>(dh) = make_uint4(h[0], h[1], h[2], h[3]);
       if (dl) *reinterpret_cast<uint4*>(dl) = make_uint4(l[0], l[1], l[2], l[3]);
     } else {
-      for (int j = 0; j < nc; ++j) {
-        dh[j] = (uint16_t)(h[j >> 1] >> (16 * (j & 1)));
-        if (dl) dl[j] = (uint16_t)(l[j >> 1] >> (16 * (j & 1)));
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (j < nc) {
+          dh[j] = (uint16_t)(h[j >> 1] >> (16 * (j & 1)));
+          if (dl) dl[j] = (uint16_t)(l[j >> 1] >> (16 * (j & 1)));
+        }
       }
     }
+  };
+  int r = r0;
+  if (vec) {
+    for (; r + kRowUnroll <= r1; r += kRowUnroll) {
+      float v[kRowUnroll][8];
+#pragma unroll
+      for (int u = 0; u < kRowUnroll; ++u) load8<SRC_F32>(src, (long long)(r + u) * ld_src + c0, v[u]);
+#pragma unroll
+      for (int u = 0; u < kRowUnroll; ++u) emit(r + u, v[u]);
+    }
+  }
+  for (; r < r1; ++r) {
+    float v[8];
+    if (vec) {
+      load8<SRC_F32>(src, (long long)r * ld_src + c0, v);
+    } else if (SRC_F32) {
+      const float* s = static_cast<const float*>(src) + (long long)r * ld_src + c0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = j < nc ? s[j] : 0.0f;
+    } else {
+      const uint16_t* s = static_cast<const uint16_t*>(src) + (long long)r * ld_src + c0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = j < nc ? bf16_to_f32(s[j]) : 0.0f;
+    }
+    emit(r, v);
   }
   if (colsum != nullptr) {
-    for (int j = 0; j < nc; ++j) atomicAdd(colsum + c0 + j, acc[j]);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (j < nc) atomicAdd(colsum + c0 + j, acc[j]);
   }
 }
 
