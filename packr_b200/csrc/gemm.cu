@@ -1,6 +1,6 @@
 // tcgen05 GEMMs of the PackRLinear forward and backward, with the weight
-// decode fused into the operand pipeline and the lut gradient folded into the
-// dW epilogue.
+// decode fused into the operand pipeline (or read predecoded) and the lut
+// gradient folded into the dW epilogue.
 //
 // One persistent, warp-specialised kernel template serves three GEMMs
 // (K = in_features, N = out_features, T = tokens):
@@ -8,34 +8,35 @@
 //   DX   dX[T,K]   (bf16) = bf16(dY)[T,N] . W[K,N]^T             (autograd.py:70)
 //   DW   dW_f[K,N] (bf16) = x^T[K,T] . dY[T,N], fp32 accumulate   (autograd.py:73-75)
 //        + dlut_sum[W_p[k,n]] += dW[k,n]                          (autograd.py:77-82)
-// with W = bf16(W_f + bf16(lut[W_p])) (autograd.py:66-67) never written to
-// HBM: decode warps read W_p (u8) and W_f (bf16) tiles straight from global
-// memory, look the 256-entry lut up in a lane-replicated shared-memory copy
-// (bank-conflict free), add in bf16 (add.rn.bf16x2; the reference's fp32 add
-// then bf16 rounding gives the same bits because 24 >= 2*8+2), and store the
-// bf16 operand into the 128-byte-swizzled shared-memory tile the tensor core
-// reads.  Activations (x, dY) arrive by TMA.
+// with W = bf16(W_f + bf16(lut[W_p])) (autograd.py:66-67).  The weight
+// operand of FWD / DX comes from one of three sources (BSrc): W_f / W_p tiles
+// staged by TMA and decoded in place in shared memory (B_WTMA), the same
+// decode fed by a register ring of global loads when W's rows are not 16-byte
+// multiples (B_RING), or a bf16 W decoded once by predecode_kernel and read by
+// TMA (B_PLAIN, large T).  The decode looks the 256-entry lut up in a
+// lane-replicated shared-memory copy (bank-conflict free) and adds in bf16
+// (add.rn.bf16x2: the reference's fp32 add then bf16 rounding gives the same
+// bits because 24 >= 2*8+2).  Activations (x, bf16(dY)) arrive by TMA.
 //
-// Tiles and roles.  A cluster of two CTAs (one per SM) computes a 256 x 256
-// output tile with tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 16 per
-// instruction): each CTA holds 128 rows of A and 128 columns of B in its own
-// shared memory, and each CTA's TMEM holds its 128 output rows x 256 columns.
+// Tiles and roles.  A cluster of two CTAs (one per SM) runs
+// tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 16 per instruction): each
+// CTA holds 128 rows of A and 128 columns of B in its own shared memory, and
+// its TMEM holds its 128 output rows x 256 columns per accumulator.  MSUB = 2
+// stacks two such M-subtiles in one 512 x 256 tile that shares every B stage.
 // Per CTA:
-//   warp 0      TMA producer (activation tiles; both operands for DW); its
-//               loads complete on the even CTA's mbarrier (.cta_group::2, no
-//               multicast)
+//   warp 0      TMA producer (activation tiles; both operands for DW and
+//               B_PLAIN; W_f / W_p for B_WTMA); loads of the pair complete on
+//               the even CTA's mbarrier (.cta_group::2, no multicast)
 //   warp 1      TMEM owner; in the even CTA also the single-thread MMA issuer
-//   warps 2-5   epilogue: tcgen05.ld of the f32 accumulator, bias / rounding /
-//               lut-gradient histogram, global stores
-//   warps 6-13  weight decode (FWD, DX only): a 3-deep register ring of W_f/W_p
-//               loads, lut lookup, bf16 add, swizzled store of this CTA's half
-//               of the B tile
-// Shared memory per CTA: 6 stages x (A 16 KB + B 16 KB) + 32 KB lut copy
-// (decode modes) or 4 KB of per-warp lut-gradient histograms (DW).  TMEM: two
-// 128 x 256 f32 accumulators (512 columns) so the epilogue of tile i overlaps
-// the mainloop of tile i+1.  Every mbarrier wait is bounded (2 s); a wait that
-// gives up sets the CTA abort word and the device timeout word, every role
-// drains and the kernel returns.
+//   warps 2..   epilogue (4 or 8 warps): tcgen05.ld of the f32 accumulator,
+//               bias / rounding / lut-gradient histogram / stream-K partials,
+//               row-coalesced stores through a per-warp staging buffer
+//   then        weight decode warps (B_WTMA, B_RING) and, for B_RING, the
+//               decode-completion signal warp
+// TMEM: two 256-column accumulators — double buffered across tiles for
+// MSUB = 1, one per subtile for MSUB = 2.  Every mbarrier and flag wait is
+// bounded (2 s); a wait that gives up sets the CTA abort word and the device
+// timeout word, every role drains and the kernel returns.
 #include <cudaTypedefs.h>
 
 #include <mutex>
