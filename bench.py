@@ -1,6 +1,6 @@
 """Benchmark of PackR's training hot path on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload adam8|ffn] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload ffn|adam8|decode] [--impl ours|reference]
 
 Prints ONE JSON line (rank 0).  For N>1 it is launched by torchrun, one rank
 per GPU (NCCL); every rank runs the same per-GPU workload (weak scaling) and
@@ -11,8 +11,12 @@ Workloads (synthetic, seeded; no dataset exists for this path):
          gate 4096->11008, up 4096->11008, down 11008->4096, M = 4096 tokens
          of bf16 activations per GPU, f32 upstream gradients holding
          bf16-exact values; one step = the three layers' forward and backward
-         through autograd (out, dX, dW_f, dlut); metric TFLOP/s over
-         6*M*K*N per layer.  Per step the operands (~0.9 GB) exceed L2.
+         through autograd (out, dX, dW_f, dlut) plus the data-parallel 8-bit
+         AdamW update; metric TFLOP/s over 6*M*K*N per layer.  Per step the
+         operands (~0.9 GB) exceed L2.
+  decode forward of the same three layers at M = 16 tokens (--tokens to
+         change): the decode-bound regime; metric GB/s of packed weights
+         (3 bytes per weight) streamed per second.
   adam8  CUDA8BitAdam step over one flat 110,000,000-element bf16 parameter
          (lr 2e-5, betas (0.9, 0.999), eps 1e-8, wd 0.01, block 256); metric
          Gparam/s.  Per step the inputs (1.1 GB) exceed L2 (126 MB).
@@ -324,6 +328,87 @@ def cpu_linear_port(budget_s: float, M: int = 1024):
             "host_cores": os.cpu_count()}
 
 
+def cpu_decode_port(budget_s: float, M: int):
+    """Times the reference PackRLinear forward (oracle/reference_port.py,
+    torch CPU, all host threads) over the three FFN layers at M tokens."""
+    from oracle import reference_port as rp
+    from packr_b200.synthetic import linear_case
+    cases = [linear_case(M, k, n, x_dtype=torch.bfloat16, bias=False, seed=i, fanin_scaled=True)
+             for i, (_, k, n) in enumerate(FFN_LAYERS)]
+
+    def run():
+        for c in cases:
+            rp.forward(c["x"], c["W_p"], c["W_f"], c["lut"])
+    run()
+    times = []
+    t0 = time.perf_counter()
+    while len(times) < 2 or time.perf_counter() - t0 < budget_s:
+        a = time.perf_counter()
+        run()
+        times.append(time.perf_counter() - a)
+    sec = statistics.median(times)
+    wbytes = sum(3.0 * k * n for _, k, n in FFN_LAYERS)
+    return {"value": wbytes / sec / 1e9, "unit": "GB/s (weight bytes)", "cores": torch.get_num_threads(),
+            "kind": "port", "sample": f"forward of the three FFN layers at M={M}, {len(times)} timed samples "
+                                      "(median); torch-CPU restatement of the reference path",
+            "host_cores": os.cpu_count()}
+
+
+def bench_decode(args, world, rank, peaks, peak_kind):
+    """Decode-bound forward: the three Llama-7B FFN layers at M (default 16)
+    tokens, no bias; value = packed-weight bytes (3 per weight) / time."""
+    from packr_b200 import kernel as K
+    M = args.tokens if args.tokens_given else 16
+    dev = torch.device("cuda", torch.cuda.current_device())
+    from packr_b200.synthetic import linear_case
+    layers = []
+    for i, (_, k, n) in enumerate(FFN_LAYERS):
+        c = linear_case(M, k, n, x_dtype=torch.bfloat16, bias=False, seed=100 + i, fanin_scaled=True)
+        layers.append({kk: (v.to(dev) if v is not None else None) for kk, v in c.items()})
+    wbytes = sum(3.0 * k * n for _, k, n in FFN_LAYERS)
+    algo = sum(3.0 * k * n + 2.0 * M * k + 4.0 * M * n for _, k, n in FFN_LAYERS)
+
+    def step():
+        for c in layers:
+            K.forward(c["x"], c["W_p"], c["W_f"], c["lut"], None)
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        total_ms, per = timed(step, args.steps, args.warmup, world, warm_seconds=1.5)
+    ms_step = total_ms / args.steps
+    value = world * wbytes / (ms_step * 1e-3) / 1e9
+    achieved = algo / (statistics.mean(per) * 1e-3) / 1e9
+    hx = [c["x"].cpu().pin_memory() for c in layers]
+    dx = [torch.empty_like(c["x"]) for c in layers]
+    hout = [torch.empty(M, n, dtype=torch.float32, pin_memory=True) for _, _, n in FFN_LAYERS]
+
+    def e2e_step():
+        for i, c in enumerate(layers):
+            dx[i].copy_(hx[i], non_blocking=True)
+            hout[i].copy_(K.forward(dx[i], c["W_p"], c["W_f"], c["lut"], None), non_blocking=True)
+    e2e_ms, _ = timed(e2e_step, args.steps, max(args.warmup, 1), world)
+    line = {
+        "metric": f"PackRLinear decode forward GB/s of packed weights (M={M})", "value": round(value, 1),
+        "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16 x, f32 decode and accumulate", "data": "synthetic (seeded)",
+        "config": {"workload": f"decode: forward of the Llama-7B FFN gate/up/down layers at M={M} tokens",
+                   "weight_bytes_per_step": wbytes, "l2": "weights 0.27 GB per step, larger than L2",
+                   "parallelism": f"replicas x{world}"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None,
+                     "peak_source": f"{peak_kind} hbm_gbs",
+                     "kernel": "gemv_partial_kernel + gemv_reduce_kernel (three layers)",
+                     "algorithmic_bytes_per_launch": algo},
+        "e2e": {"value": round(world * wbytes / (e2e_ms / args.steps * 1e-3) / 1e9, 1), "unit": "GB/s",
+                "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in hx),
+                "d2h_bytes_per_step": sum(t.numel() * t.element_size() for t in hout)},
+        "gpu_launches": args.steps * 2 * len(FFN_LAYERS),
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_decode_port(args.cpu_seconds, M)
+    return line
+
+
 def layer_launches(M: int, K: int, N: int) -> int:
     """libpackr_b200 kernels one PackRLinear forward + backward launches for
     bf16 x (K % 8 == 0), no bias, cached lut counts: forward = [predecode] +
@@ -493,6 +578,17 @@ def reference_arm(args, world, rank):
                 "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
                 "e2e": {"value": round(cb["value"], 5), "unit": "Gparam/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
+    if args.workload == "decode":
+        M = args.tokens if args.tokens_given else 16
+        cb = cpu_decode_port(max(5.0, 0.5 * args.steps), M)
+        return {"impl": "reference", "metric": f"PackRLinear decode forward GB/s of packed weights (M={M})",
+                "value": round(cb["value"], 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "f32", "data": "synthetic",
+                "config": {"workload": f"decode: forward of the Llama-7B FFN layers at M={M} (CPU)"},
+                "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                "e2e": {"value": round(cb["value"], 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
     if args.workload == "ffn":
         cb = cpu_linear_port(max(5.0, 0.5 * args.steps))
         return {"impl": "reference", "metric": "PackRLinear fwd+bwd TFLOP/s (Llama FFN shapes)",
@@ -511,14 +607,17 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="ffn", choices=["ffn", "adam8"])
-    ap.add_argument("--tokens", type=int, default=FFN_M, help="ffn: tokens per GPU")
+    ap.add_argument("--workload", default="ffn", choices=["ffn", "adam8", "decode"])
+    ap.add_argument("--tokens", type=int, default=None, help="tokens per GPU (ffn: 4096, decode: 16)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-once", action="store_true",
                     help="ffn: run each kernel of one gate-layer step once (for ncu captures), print nothing")
     args = ap.parse_args()
+    args.tokens_given = args.tokens is not None
+    if args.tokens is None:
+        args.tokens = FFN_M
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -532,7 +631,8 @@ def main():
     if args.profile_once:
         profile_once(args)
         return
-    line = (bench_ffn if args.workload == "ffn" else bench_adam8)(args, world, rank, peaks, peak_kind)
+    fn = {"ffn": bench_ffn, "adam8": bench_adam8, "decode": bench_decode}[args.workload]
+    line = fn(args, world, rank, peaks, peak_kind)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

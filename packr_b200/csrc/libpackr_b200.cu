@@ -6,5 +6,6 @@
 #include "prep.cu"
 #include "gemm.cu"
 #include "predecode.cu"
+#include "gemv.cu"
 #include "linear.cu"
 #include "static_scratch.cu"

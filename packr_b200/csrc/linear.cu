@@ -104,7 +104,13 @@ extern "C" size_t packr_forward_workspace_bytes(int64_t M, int64_t K, int64_t N,
   K = K > 0 ? K : 0;
   N = N > 0 ? N : 0;
   const bool pre = predecode_eligible(M, N);
-  return plan_forward(c, p, M, K, N, x_dtype, pre, pre);
+  size_t need = plan_forward(c, p, M, K, N, x_dtype, pre, pre);
+  // few rows: the decode-bound CUDA-core route (its split partial sums)
+  if (M >= 1 && M <= gemv::kMaxM && K > 0 && N > 0) {
+    const size_t g = align_up(gemv::workspace_bytes(M, K, N));
+    if (g > need) need = g;
+  }
+  return need;
 }
 
 extern "C" int packr_forward(const void* x, int x_dtype, const uint8_t* W_p, const uint16_t* W_f, const float* lut,
@@ -119,6 +125,14 @@ extern "C" int packr_forward(const void* x, int x_dtype, const uint8_t* W_p, con
   if ((st = check_device()) != PACKR_OK) return st;
   if (M == 0) return PACKR_OK;
   cudaStream_t s = as_stream(stream);
+  // few rows: stream W once through the CUDA cores (fp16-lut decode of the
+  // reference's forward, f32 accumulation), when the workspace holds the
+  // split partial sums
+  if (gemv::eligible(M, K, N, W_p, W_f) && workspace != nullptr && aligned(workspace, kAlign) &&
+      workspace_bytes >= gemv::workspace_bytes(M, K, N)) {
+    return gemv::forward(x, x_dtype == PACKR_DTYPE_F32, W_p, W_f, lut, bias, bias_dtype == PACKR_DTYPE_F32, out, M,
+                         K, N, static_cast<float*>(workspace), s);
+  }
   // the richest route the workspace holds: predecode + stream-K, predecode,
   // fused decode
   const bool pre_ok = predecode_eligible(M, N) && gemm::wtma_ok(W_p, W_f, N);

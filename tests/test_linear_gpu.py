@@ -191,6 +191,9 @@ CASES = [
     (1024, 2048, 9728, torch.bfloat16, True),  # stream-K split of 76 FWD tiles over 74 pairs
     (512, 1024, 5120, torch.float32, True),    # f32 x: 3 dW reduction segments
     (4096, 2560, 512, torch.bfloat16, False),  # stream-K split of 80 DX tiles over 74 pairs
+    (3, 200, 264, torch.float32, True),        # few-row CUDA-core forward, row bound 4
+    (9, 512, 1000, torch.bfloat16, False),     # row bound 12, 4 columns per thread
+    (13, 96, 36, torch.float32, True),         # row bound 16, one K split
     (16, 4096, 11008, torch.bfloat16, True),   # Llama-7B gate/up, decode-bound M
     (16, 11008, 4096, torch.bfloat16, True),   # Llama-7B down
 ]
