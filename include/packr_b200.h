@@ -83,10 +83,12 @@ int packr_adam8_multi(const packr_adam_tensor* tensors, int n_tensors, float lr,
  * and never written to HBM; from 1024 rows on (N % 16 == 0, 16-byte aligned
  * W_p / W_f) W is decoded once into the workspace and read back by TMA,
  * provided the workspace holds it (packr_forward_workspace_bytes counts it;
- * a smaller workspace that fits the fused route selects that route).  Up to
- * 16 rows (N % 4 == 0, 8-byte aligned W_p) the forward streams W through the
- * CUDA cores instead, decoding as the reference's forward does
- * (f32(W_f) + f32(fp16(lut[W_p]))) with f32 accumulation.
+ * a smaller workspace that fits the fused route selects that route).  For
+ * 5..128 rows (N % 16 == 0) W is streamed once through a tcgen05 GEMM that
+ * takes 128 weight columns as the MMA's rows and the tokens as its N, split
+ * over K; up to 4 rows (N % 4 == 0, 8-byte aligned W_p) through the CUDA
+ * cores, decoding as the reference's forward does (f32(W_f) +
+ * f32(fp16(lut[W_p]))) with f32 accumulation.
  * x is bf16 or f32 (f32 x is rounded to bf16 in the workspace first).
  * bias: [N] of bias_dtype (bf16 or f32, added in f32 in the epilogue) or
  * NULL.  M = 0 is a no-op; K, N >= 1.

@@ -81,6 +81,10 @@ constexpr int LUT_BYTES = 256 * 32 * 4;  // one u32 per (entry, lane)
 constexpr int HIST_COPIES = 2;
 constexpr int HIST_COPY_BYTES = 256 * 32 * 4;
 constexpr int ACC_COLS = BN;
+// Epilogue warps wait a whole mainloop for their accumulator: they poll
+// with the hardware's suspend hint (ns) so their polls do not take issue
+// slots from the roles on the critical path.
+constexpr uint32_t kEpilogueSleepNs = 1000;
 // FWD / DX switch from the fused decode to predecode + plain GEMM at this
 // many output rows (tokens): below it the decode traffic of the fused kernel
 // costs less than an extra HBM pass over W.
@@ -750,7 +754,7 @@ __global__ void __launch_bounds__(Cfg<MODE, BSRC, MSUB>::kThreads, 1)
       const int acc = MSUB == 1 ? (t_local & 1) : sub;
       const uint32_t aph = MSUB == 1 ? ((uint32_t)(t_local >> 1) & 1u) : ((uint32_t)t_local & 1u);
       // one lane polls; the warp proceeds only if every lane saw the phase
-      if (!mbar_wait_warp(&bars->tfull[acc], aph, abort_flag)) { alive = false; break; }
+      if (!mbar_wait_warp(&bars->tfull[acc], aph, abort_flag, kEpilogueSleepNs)) { alive = false; break; }
       if (warp == 2 && lane == 0) PACKR_TRACE_EVENT(4, t_local);
       tc_fence_after();
       const int m0 = (tile % P.m_tiles) * (2 * BM * MSUB) + sub * 2 * BM + (int)rank * BM;

@@ -1,4 +1,5 @@
-// Forward for few rows (M <= 16 tokens, decode-bound): out = x @ W + bias
+// Forward for very few rows (decode-bound; used up to 4 tokens, built for up
+// to 16): out = x @ W + bias
 // with W decoded exactly as the reference's forward decodes it,
 // W = f32(W_f) + f32(fp16(lut[W_p])) (packr/kernel.py:127-130), and an f32
 // accumulation on the CUDA cores.  At these sizes the work is streaming W
@@ -68,20 +69,33 @@ struct WVec<4> {
   __device__ __forceinline__ uint32_t pword(int) const { return p; }
 };
 
-// Dynamic shared memory: lut copy [256][32] u32 | x [rows][M] f32.
+template <>
+struct WVec<2> {
+  uint32_t f;
+  uint32_t p;
+  __device__ __forceinline__ void load(const uint16_t* wf, const uint8_t* wp) {
+    f = __ldcs(reinterpret_cast<const unsigned int*>(wf));
+    p = __ldcs(reinterpret_cast<const unsigned short*>(wp));
+  }
+  __device__ __forceinline__ uint32_t fword(int) const { return f; }
+  __device__ __forceinline__ uint32_t pword(int) const { return p; }
+};
+
+// Dynamic shared memory: lut copy [256][32] u32 | x [rows][M] as (x, x) f32
+// pairs, ready to be the packed multiplier of fma.rn.f32x2.
 // M is a compile-time bound on the rows; Mr <= M rows are real (x rows past
 // Mr read as zero and their sums are not written).  Warp w of the CTA owns
 // the 32 * CPT columns starting at (blockIdx.x * 8 + w) * 32 * CPT and walks
 // every row of the CTA's K range for them, kRowUnroll rows per load group
 // with the next group in flight; its sums go straight to the partial array.
 template <int M, int CPT, int U>
-__global__ void __launch_bounds__(kThreads, (M <= 2 ? 4 : M <= 4 ? 3 : 2))
+__global__ void __launch_bounds__(kThreads, (M <= 2 ? 4 : 3))
     gemv_partial_kernel(const void* __restrict__ x, int x_f32, int Mr, const uint8_t* __restrict__ W_p,
                         const uint16_t* __restrict__ W_f, const float* __restrict__ lut,
                         float* __restrict__ partial, int K, int N, int rows_per_split) {
   extern __shared__ __align__(16) uint32_t gsm[];
   uint32_t* lut_s = gsm;                                 // 256 * 32
-  float* xs = reinterpret_cast<float*>(gsm + 256 * 32);  // rows_per_split * M
+  f32x2* xs = reinterpret_cast<f32x2*>(gsm + 256 * 32);  // rows_per_split * M
   constexpr int kStrip = 32 * CPT;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int k0 = blockIdx.y * rows_per_split;
@@ -92,9 +106,10 @@ __global__ void __launch_bounds__(kThreads, (M <= 2 ? 4 : M <= 4 ? 3 : 2))
   for (int i = threadIdx.x; i < nrows * M; i += kThreads) {
     const int r = i / M, m = i - r * M;
     const long long src = (long long)m * K + k0 + r;
-    xs[i] = m >= Mr ? 0.0f
-                    : x_f32 ? __ldg(static_cast<const float*>(x) + src)
-                            : bf16_to_f32(__ldg(static_cast<const uint16_t*>(x) + src));
+    const float v = m >= Mr ? 0.0f
+                            : x_f32 ? __ldg(static_cast<const float*>(x) + src)
+                                    : bf16_to_f32(__ldg(static_cast<const uint16_t*>(x) + src));
+    xs[i] = pk2(v, v);
   }
   __syncthreads();
 
@@ -119,11 +134,10 @@ __global__ void __launch_bounds__(kThreads, (M <= 2 ? 4 : M <= 4 ? 3 : 2))
       const float f1 = __fadd_rn(__uint_as_float(fw & 0xFFFF0000u), __uint_as_float(lut_lane[((pw >> 8) & 0xFFu) * 32]));
       wv[j] = pk2(f0, f1);
     }
-    const float* xr = xs + r * M;
+    const f32x2* xr = xs + r * M;
 #pragma unroll
     for (int m = 0; m < M; ++m) {
-      const float xv = xr[m];
-      const f32x2 x2 = pk2(xv, xv);
+      const f32x2 x2 = xr[m];
 #pragma unroll
       for (int j = 0; j < CPT / 2; ++j) acc[m][j] = fma2(x2, wv[j], acc[m][j]);
     }
@@ -205,27 +219,28 @@ struct Plan {
 
 inline int row_bound(long long M) { return M <= 2 ? (int)M : M <= 4 ? 4 : M <= 8 ? 8 : M <= 12 ? 12 : 16; }
 
-// Columns per thread: 8 (one 16-byte W_f load) when N allows it and the
-// accumulators fit, else 4.  K is split so that the grid is about one wave of
+// Columns per thread: 8 for one row (one 16-byte W_f load), 4 up to 8 rows,
+// 2 beyond (the accumulators of 12-16 rows would cost occupancy).  K is split so that the grid is about one wave of
 // `resident` CTAs per SM, with the partial sums (splits x M x N f32) at most
-// about a tenth of W's bytes and the x slice of a split at most 32 KB.
+// about a tenth of W's bytes and the x slice of a split (8 bytes per value)
+// at most 32 KB.
 inline Plan plan(long long M, long long K, long long N, int resident = 8) {
   Plan p{};
   p.mb = row_bound(M);
-  p.cpt = (N % 8 == 0 && p.mb <= 1) ? 8 : 4;
+  p.cpt = (N % 8 == 0 && p.mb <= 1) ? 8 : p.mb >= 12 ? 2 : 4;
   const long long col_blocks = (N + (long long)kWarps * 32 * p.cpt - 1) / ((long long)kWarps * 32 * p.cpt);
   long long splits = ((long long)resident * sm_count() + col_blocks - 1) / col_blocks;
   long long cap = (3 * K) / (40 * M);  // partial bytes <= ~W bytes / 10
   if (cap < 1) cap = 1;
   if (splits > cap) splits = cap;
-  const long long min_splits = (K * p.mb * 4 + 32767) / 32768;  // x slice <= 32 KB
+  const long long min_splits = (K * p.mb * 8 + 32767) / 32768;  // x slice <= 32 KB
   if (splits < min_splits) splits = min_splits;
   if (splits > K) splits = K;
   if (splits < 1) splits = 1;
   const long long rows = (K + splits - 1) / splits;
   p.rows_per_split = (int)rows;
   p.splits = (int)((K + rows - 1) / rows);
-  p.smem = 256 * 32 * 4 + (size_t)rows * p.mb * 4;
+  p.smem = 256 * 32 * 4 + (size_t)rows * p.mb * 8;
   return p;
 }
 
@@ -233,7 +248,7 @@ inline Plan plan(long long M, long long K, long long N, int resident = 8) {
 inline bool eligible(long long M, long long K, long long N, const uint8_t* W_p, const uint16_t* W_f) {
   if (M < 1 || M > kMaxM || (N % 4) != 0 || K < 1) return false;
   const Plan p = plan(M, K, N);
-  const uintptr_t va = p.cpt == 8 ? 16 : 8;
+  const uintptr_t va = 2 * p.cpt;  // bytes of one W_f chunk
   return aligned(W_f, va) && aligned(W_p, va / 2);
 }
 
@@ -280,13 +295,17 @@ int launch_cpt(const Plan& p, const void* x, int x_f32, int Mr, const uint8_t* W
                const float* lut, float* partial, long long K, long long N, cudaStream_t st) {
   int splits = 0;
   int rc;
-  if constexpr (M <= 8) {
+  if constexpr (M == 1) {
     if (p.cpt == 8) {
       rc = launch_m<M, 8>(p, x, x_f32, Mr, W_p, W_f, lut, partial, K, N, st, &splits);
       return rc == PACKR_OK ? splits : -rc;
     }
   }
-  rc = launch_m<M, 4>(p, x, x_f32, Mr, W_p, W_f, lut, partial, K, N, st, &splits);
+  if constexpr (M >= 12) {
+    rc = launch_m<M, 2>(p, x, x_f32, Mr, W_p, W_f, lut, partial, K, N, st, &splits);
+  } else {
+    rc = launch_m<M, 4>(p, x, x_f32, Mr, W_p, W_f, lut, partial, K, N, st, &splits);
+  }
   return rc == PACKR_OK ? splits : -rc;
 }
 

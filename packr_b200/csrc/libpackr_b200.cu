@@ -7,5 +7,6 @@
 #include "gemm.cu"
 #include "predecode.cu"
 #include "gemv.cu"
+#include "skinny.cu"
 #include "linear.cu"
 #include "static_scratch.cu"

@@ -25,6 +25,20 @@ struct Carve {
 
 bool x_needs_copy(int x_dtype, long long K) { return x_dtype == PACKR_DTYPE_F32 || (K & 7) != 0; }
 
+// Forward token counts served by the skinny tcgen05 GEMM (W as the 128-row
+// MMA operand, tokens as N): measured on the Llama-7B FFN shapes, the
+// CUDA-core GEMV streams W fastest up to 4 tokens, the skinny GEMM from 5 to
+// 128 (at 128 tokens: 86 vs 81 us for 4096 -> 11008 and 67 vs 186 us for
+// 11008 -> 4096, whose 16 column tiles leave most SMs idle in the 256-row
+// tile GEMM), the 256-row tile GEMMs beyond.
+#ifndef PACKR_SKINNY_MIN_M
+#define PACKR_SKINNY_MIN_M 5
+#endif
+constexpr long long kSkinnyMaxM = 128;
+inline bool skinny_eligible(long long M, long long N) {
+  return M >= PACKR_SKINNY_MIN_M && M <= kSkinnyMaxM && (N & 15) == 0;
+}
+
 // FWD / DX take the predecode + plain GEMM route for M >= PACKR_PREDECODE_MIN_M
 // when W's layout allows TMA (N % 16 == 0, 16-byte aligned W_p / W_f) and the
 // workspace holds the decoded W; otherwise the fused-decode GEMM runs.
@@ -105,10 +119,19 @@ extern "C" size_t packr_forward_workspace_bytes(int64_t M, int64_t K, int64_t N,
   N = N > 0 ? N : 0;
   const bool pre = predecode_eligible(M, N);
   size_t need = plan_forward(c, p, M, K, N, x_dtype, pre, pre);
-  // few rows: the decode-bound CUDA-core route (its split partial sums)
-  if (M >= 1 && M <= gemv::kMaxM && K > 0 && N > 0) {
-    const size_t g = align_up(gemv::workspace_bytes(M, K, N));
-    if (g > need) need = g;
+  if (M >= 1 && K > 0 && N > 0) {
+    // few rows: the split partial sums of the skinny GEMM (plus its bf16 x)
+    // or of the CUDA-core route
+    if (skinny_eligible(M, N)) {
+      Carve c2{nullptr};
+      FwdPlan p2;
+      const size_t g = plan_forward(c2, p2, M, K, N, x_dtype, false) +
+                       align_up(gemm::skinny_partial_bytes(M, K, N));
+      if (g > need) need = g;
+    } else if (M <= gemv::kMaxM) {
+      const size_t g = align_up(gemv::workspace_bytes(M, K, N));
+      if (g > need) need = g;
+    }
   }
   return need;
 }
@@ -125,6 +148,26 @@ extern "C" int packr_forward(const void* x, int x_dtype, const uint8_t* W_p, con
   if ((st = check_device()) != PACKR_OK) return st;
   if (M == 0) return PACKR_OK;
   cudaStream_t s = as_stream(stream);
+  // few tokens: the skinny tcgen05 GEMM (W streamed once as the MMA's
+  // 128-row operand, split over K), when the workspace holds its partials
+  if (skinny_eligible(M, N) && gemm::wtma_ok(W_p, W_f, N) && workspace != nullptr && aligned(workspace, kAlign)) {
+    Carve c2{static_cast<uint8_t*>(workspace)};
+    FwdPlan p2;
+    plan_forward(c2, p2, M, K, N, x_dtype, false);
+    float* partial = c2.take<float>(gemm::skinny_partial_bytes(M, K, N) / sizeof(float));
+    if (workspace_bytes >= c2.off) {
+      const uint16_t* xb = static_cast<const uint16_t*>(x);
+      long long ldx = K;
+      if (p2.xh != nullptr) {
+        st = prep::split_rows(x, x_dtype == PACKR_DTYPE_F32, K, M, K, p2.xh, nullptr, round8(K), nullptr, s);
+        if (st != PACKR_OK) return st;
+        xb = p2.xh;
+        ldx = round8(K);
+      }
+      return gemm::skinny_forward(xb, ldx, W_p, W_f, lut, bias, bias_dtype == PACKR_DTYPE_F32, out, M, K, N,
+                                  partial, s);
+    }
+  }
   // few rows: stream W once through the CUDA cores (fp16-lut decode of the
   // reference's forward, f32 accumulation), when the workspace holds the
   // split partial sums

@@ -46,6 +46,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// As mbar_try_wait, but a thread whose phase is not complete may be
+// suspended (off the issue slots) until it completes or about `ns` elapse.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -59,13 +73,19 @@ constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 // Waits for phase `parity` of `bar`.  Returns false (after setting the CTA's
 // abort word and the device-wide timeout word) if the wait exceeds the bound
 // or another role of the CTA already aborted.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+// sleep_ns = 0: every poll spins (waits on the critical path: producer, MMA
+// issuer, decode).  sleep_ns > 0: after the first polls the hardware may
+// suspend the thread for up to sleep_ns per poll, so that long waits (an
+// epilogue waiting for a whole tile) leave the issue slots to working warps;
+// a suspended thread can notice the completed phase late by up to that long.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          uint32_t sleep_ns = 0) {
   const uint32_t b = smem_u32(bar);
   if (mbar_try_wait(b, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(b, parity)) return true;
-    if ((i & 255u) == 0) {
+    if ((sleep_ns == 0 || i < 64) ? mbar_try_wait(b, parity) : mbar_try_wait_sleep(b, parity, sleep_ns)) return true;
+    if ((i & 15u) == 0) {
       if (*abort_flag) return false;
       if (globaltimer_ns() - t0 > kWaitLimitNs) {
         *abort_flag = 1;
@@ -80,10 +100,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 // the other lanes take the barrier's acquire themselves (their try_wait
 // succeeds at once).  One polling lane instead of 32 keeps waiting warps off
 // the shared-memory pipe.  The result is the same in every lane.
-__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                               uint32_t sleep_ns = 0) {
   const int lane = threadIdx.x & 31;
   bool ok = true;
-  if (lane == 0) ok = mbar_wait(bar, parity, abort_flag);
+  if (lane == 0) ok = mbar_wait(bar, parity, abort_flag, sleep_ns);
   ok = __shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0) != 0;
   if (ok && lane != 0) ok = mbar_wait(bar, parity, abort_flag);
   return __all_sync(0xFFFFFFFFu, ok);
@@ -102,6 +123,13 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* m, uin
           smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
       : "memory");
+}
+
+// Brings a tile into L2 ahead of its load (no shared memory, no barrier).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* m, int c0, int c1) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(m)),
+               "r"(c0), "r"(c1)
+               : "memory");
 }
 
 __device__ __forceinline__ void fence_proxy_async_smem() {

@@ -194,6 +194,10 @@ CASES = [
     (3, 200, 264, torch.float32, True),        # few-row CUDA-core forward, row bound 4
     (9, 512, 1000, torch.bfloat16, False),     # row bound 12, 4 columns per thread
     (13, 96, 36, torch.float32, True),         # row bound 16, one K split
+    (60, 1024, 2048, torch.float32, True),     # skinny tcgen05 forward, 64-token MMA width, f32 x
+    (100, 640, 512, torch.bfloat16, True),     # skinny tcgen05 forward, 128-token MMA width
+    (7, 640, 512, torch.bfloat16, False),      # skinny tcgen05 forward, 32-token MMA width
+    (4, 512, 1024, torch.bfloat16, True),      # CUDA-core forward, 4 rows
     (16, 4096, 11008, torch.bfloat16, True),   # Llama-7B gate/up, decode-bound M
     (16, 11008, 4096, torch.bfloat16, True),   # Llama-7B down
 ]
