@@ -122,6 +122,11 @@ def dist_setup():
     if world > 1:
         import datetime
         import torch.distributed as dist
+        # NCCL's own messages (its version banner included) go to stderr, so
+        # that stdout carries the one JSON line
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+        if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
+            os.environ["NCCL_DEBUG"] = "WARN"
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
