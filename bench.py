@@ -439,7 +439,8 @@ def bench_ffn(args, world, rank, peaks, peak_kind):
         dys.append(torch.randn(M, n, generator=g, device=dev).to(torch.bfloat16).float())
         layers.append(lay)
     params = [p for lay in layers for p in (lay.W_f, lay.lut)]
-    opt = ShardedAdam8(params, lr=2e-5, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01)
+    opt = ShardedAdam8(params, lr=2e-5, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01,
+                       overlap_grad_reduce=True)
 
     def zero():
         for lay, x in zip(layers, xs):
@@ -524,7 +525,8 @@ def bench_ffn(args, world, rank, peaks, peak_kind):
         "config": {"workload": f"ffn: Llama-7B FFN gate/up/down (4096<->11008) PackRLinear training step, "
                                f"M={M} tokens per GPU",
                    "step": "forward + backward of the three layers, then the data-parallel 8-bit AdamW update "
-                           "(gradient reduce-scatter, AdamW on this rank's 1/N state shard, W_f/lut all-gather; "
+                           "(gradient reduce-scatter started per bucket from the gradient hooks during the "
+                           "backward, AdamW on this rank's 1/N state shard, W_f/lut all-gather; "
                            "no collectives at N=1); value counts the 6*M*K*N GEMM FLOPs",
                    "hidden": FFN_HIDDEN, "intermediate": FFN_INTER, "tokens_per_gpu": M,
                    "flops_per_step_per_gpu": flops, "l2": "inputs larger than L2 (~0.9 GB of operands per step)",
@@ -545,7 +547,7 @@ def bench_ffn(args, world, rank, peaks, peak_kind):
                                "algorithmic_bytes_per_launch": pre_bytes},
         "e2e": {"value": round(e2e_val, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": hres.numel() * 4},
-        "gpu_launches": args.steps * (sum(layer_launches(M, k, n) for _, k, n in FFN_LAYERS) + len(opt.groups)),
+        "gpu_launches": args.steps * (sum(layer_launches(M, k, n) for _, k, n in FFN_LAYERS) + len(opt.buckets)),
         "clocks": clk.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

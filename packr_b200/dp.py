@@ -5,28 +5,36 @@ The reference has no distributed code; this is the one parallel strategy the
 B200 build adds (one process per GPU, NCCL over NVLink/NVSwitch).
 
 Layout.  The trainable parameters (W_f, lut, bias_f, and any other tensors
-passed in) are re-homed into one flat buffer per dtype; each parameter
-starts at a multiple of 256 elements, so the 256-element quantisation blocks
-of the 8-bit state never straddle two parameters, and the buffer is padded to
-a multiple of 256 * world_size so every rank's shard is a whole number of
-blocks.  A parameter's `.data` becomes a view of its flat buffer, so the
-all-gather writes the updated values in place.
+passed in) are re-homed into flat buffers ("buckets"), one dtype per bucket,
+filled in parameter order up to `bucket_bytes` (a larger parameter gets a
+bucket of its own).  Each parameter starts at a multiple of 256 elements, so
+the 256-element quantisation blocks of the 8-bit state never straddle two
+parameters, and every bucket is padded to a multiple of 256 * world_size so
+each rank's shard of it is a whole number of blocks.  A parameter's `.data`
+becomes a view of its bucket, so the all-gather writes the updated values in
+place.
 
-Step (identical collective sequence on every rank):
-  1. copy each .grad into the flat gradient buffer (zeros where None).  Each
-     parameter carries `_packr_grad_sink = (flat_grad, offset)`: PackRLinear's
-     backward writes dW_f straight into that slice while .grad is None, and
-     the copy is skipped for a .grad that already is the slice
+Step (identical collective sequence on every rank), per bucket:
+  1. the gradients land in the bucket's flat gradient buffer: each parameter
+     carries `_packr_grad_sink = (flat_grad, offset)`, PackRLinear's backward
+     writes dW_f straight into that slice while .grad is None, other
+     gradients are copied (zeros where None)
   2. reduce_scatter_tensor(op=AVG)   -> this rank's averaged gradient shard
   3. packr_adam8_multi over the parameter sub-ranges of the shard (the same
      per-block arithmetic as CUDA8BitAdam, so the result equals the
      single-process step on the averaged gradient)
   4. all_gather_into_tensor           -> every rank holds the new parameters
-With world_size 1 the collectives are skipped and the optimizer reads the
-flat gradient buffer itself.
+With overlap_grad_reduce=True (world_size > 1) step 2 of a bucket is issued
+asynchronously from a post-accumulate-grad hook as soon as the last gradient
+of the bucket is produced, so it runs on NCCL's stream while the backward of
+earlier layers continues; step() then waits for it.  That assumes one
+backward per step: wrap the earlier micro-batches of gradient accumulation in
+`with opt.no_sync():`.  With world_size 1 the collectives are skipped and the
+optimizer reads the flat gradient buffer itself.
 """
 from __future__ import annotations
 
+import contextlib
 from dataclasses import dataclass, field
 
 import torch
@@ -38,12 +46,12 @@ BLOCK = 256
 @dataclass
 class _Slot:
     param: torch.Tensor
-    offset: int   # element offset in the flat buffer (multiple of BLOCK)
+    offset: int   # element offset in the bucket (multiple of BLOCK)
     numel: int
 
 
 @dataclass
-class _Group:
+class _Bucket:
     dtype: torch.dtype
     slots: list = field(default_factory=list)
     total: int = 0
@@ -55,6 +63,8 @@ class _Group:
     ms: torch.Tensor | None = None
     vs: torch.Tensor | None = None
     entries: list = field(default_factory=list)  # (p_view, g_view, m, v, ms, vs)
+    ready: int = 0                                # gradients produced since the last step (overlap mode)
+    work: object = None                           # pending reduce-scatter
 
 
 def _round_up(x: int, m: int) -> int:
@@ -70,7 +80,7 @@ class ShardedAdam8:
     """
 
     def __init__(self, params, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0, process_group=None,
-                 adam_fn=None):
+                 adam_fn=None, bucket_bytes: int = 32 << 20, overlap_grad_reduce: bool = False):
         self.params = [p for p in params if p.requires_grad]
         if not self.params:
             raise ValueError("ShardedAdam8: no trainable parameters")
@@ -87,46 +97,97 @@ class ShardedAdam8:
         self.adam_fn = adam_fn
         self.step_count = 0
         self.device = self.params[0].device
-        self.groups: dict[torch.dtype, _Group] = {}
+        self.buckets: list[_Bucket] = []
+        open_bucket: dict[torch.dtype, _Bucket] = {}
         for p in self.params:
             if p.device != self.device:
                 raise ValueError("ShardedAdam8: all parameters must be on one device")
-            g = self.groups.setdefault(p.dtype, _Group(p.dtype))
-            g.slots.append(_Slot(p, g.total, p.numel()))
-            g.total = _round_up(g.total + p.numel(), BLOCK)
-        for g in self.groups.values():
-            self._build(g)
+            b = open_bucket.get(p.dtype)
+            if b is None or (b.slots and (b.total + p.numel()) * p.element_size() > bucket_bytes):
+                b = _Bucket(p.dtype)
+                self.buckets.append(b)
+                open_bucket[p.dtype] = b
+            b.slots.append(_Slot(p, b.total, p.numel()))
+            b.total = _round_up(b.total + p.numel(), BLOCK)
+        self._bucket_of = {}
+        for b in self.buckets:
+            self._build(b)
+            for s in b.slots:
+                self._bucket_of[id(s.param)] = b
+        self.overlap = bool(overlap_grad_reduce) and self.world > 1
+        self._sync = True
+        if self.overlap:
+            for p in self.params:
+                p.register_post_accumulate_grad_hook(self._on_grad)
 
     # -------------------------------------------------------------- layout
-    def _build(self, g: _Group) -> None:
-        total = _round_up(max(g.total, 1), BLOCK * self.world)
-        g.total = total
-        g.flat = torch.zeros(total, dtype=g.dtype, device=self.device)
-        g.grad = torch.zeros(total, dtype=g.dtype, device=self.device)
-        for s in g.slots:
-            g.flat[s.offset:s.offset + s.numel].copy_(s.param.detach().reshape(-1))
-            s.param.data = g.flat[s.offset:s.offset + s.numel].view_as(s.param)
-            s.param._packr_grad_sink = (g.grad, s.offset)
+    def _build(self, b: _Bucket) -> None:
+        total = _round_up(max(b.total, 1), BLOCK * self.world)
+        b.total = total
+        b.flat = torch.zeros(total, dtype=b.dtype, device=self.device)
+        b.grad = torch.zeros(total, dtype=b.dtype, device=self.device)
+        for s in b.slots:
+            b.flat[s.offset:s.offset + s.numel].copy_(s.param.detach().reshape(-1))
+            s.param.data = b.flat[s.offset:s.offset + s.numel].view_as(s.param)
+            s.param._packr_grad_sink = (b.grad, s.offset)
         shard = total // self.world
         s0 = self.rank * shard
-        g.shard_grad = g.grad if self.world == 1 else torch.zeros(shard, dtype=g.dtype, device=self.device)
-        g.m = torch.zeros(shard, dtype=torch.int8, device=self.device)
-        g.v = torch.zeros(shard, dtype=torch.int8, device=self.device)
-        g.ms = torch.ones(shard // BLOCK, dtype=torch.float32, device=self.device)
-        g.vs = torch.ones(shard // BLOCK, dtype=torch.float32, device=self.device)
+        b.shard_grad = b.grad if self.world == 1 else torch.zeros(shard, dtype=b.dtype, device=self.device)
+        b.m = torch.zeros(shard, dtype=torch.int8, device=self.device)
+        b.v = torch.zeros(shard, dtype=torch.int8, device=self.device)
+        b.ms = torch.ones(shard // BLOCK, dtype=torch.float32, device=self.device)
+        b.vs = torch.ones(shard // BLOCK, dtype=torch.float32, device=self.device)
         # parameter sub-ranges inside this rank's shard; both ends of each
         # range are 256-aligned except a parameter's own last element
-        for s in g.slots:
-            a, b = max(s.offset, s0), min(s.offset + s.numel, s0 + shard)
-            if a >= b:
+        for s in b.slots:
+            a, e = max(s.offset, s0), min(s.offset + s.numel, s0 + shard)
+            if a >= e:
                 continue
-            la, lb = a - s0, b - s0
-            ba, bb = la // BLOCK, (lb + BLOCK - 1) // BLOCK
-            g.entries.append((g.flat[a:b], g.shard_grad[la:lb], g.m[la:lb], g.v[la:lb], g.ms[ba:bb], g.vs[ba:bb]))
+            la, le = a - s0, e - s0
+            ba, be = la // BLOCK, (le + BLOCK - 1) // BLOCK
+            b.entries.append((b.flat[a:e], b.shard_grad[la:le], b.m[la:le], b.v[la:le], b.ms[ba:be], b.vs[ba:be]))
 
     @property
     def shard_numel(self) -> int:
-        return sum(g.total // self.world for g in self.groups.values())
+        return sum(b.total // self.world for b in self.buckets)
+
+    def bucket_of(self, param: torch.Tensor) -> _Bucket:
+        return self._bucket_of[id(param)]
+
+    # -------------------------------------------------------------- gradients
+    def _gather_grads(self, b: _Bucket) -> None:
+        for s in b.slots:
+            dst = b.grad[s.offset:s.offset + s.numel]
+            if s.param.grad is None:
+                dst.zero_()
+            elif s.param.grad.data_ptr() != dst.data_ptr():  # not already the slice
+                dst.copy_(s.param.grad.reshape(-1))
+
+    def _launch_reduce(self, b: _Bucket) -> None:
+        self._gather_grads(b)
+        if self.world > 1:
+            b.work = dist.reduce_scatter_tensor(b.shard_grad, b.grad, op=dist.ReduceOp.AVG, group=self.pg,
+                                                async_op=True)
+        else:
+            b.work = True
+
+    def _on_grad(self, param: torch.Tensor) -> None:
+        if not self._sync:
+            return
+        b = self._bucket_of[id(param)]
+        b.ready += 1
+        if b.ready == len(b.slots) and b.work is None:
+            self._launch_reduce(b)
+
+    @contextlib.contextmanager
+    def no_sync(self):
+        """Backward passes inside do not start the gradient reduce-scatter
+        (the earlier micro-batches of gradient accumulation)."""
+        prev, self._sync = self._sync, False
+        try:
+            yield
+        finally:
+            self._sync = prev
 
     # -------------------------------------------------------------- step
     @torch.no_grad()
@@ -135,23 +196,24 @@ class ShardedAdam8:
         b1, b2 = self.betas
         bc1 = 1.0 - b1 ** self.step_count
         bc2 = 1.0 - b2 ** self.step_count
-        for dt in sorted(self.groups, key=str):
-            g = self.groups[dt]
-            for s in g.slots:
-                dst = g.grad[s.offset:s.offset + s.numel]
-                if s.param.grad is None:
-                    dst.zero_()
-                elif s.param.grad.data_ptr() != dst.data_ptr():  # not already the slice
-                    dst.copy_(s.param.grad.reshape(-1))
+        for b in self.buckets:  # the same collective order on every rank
+            if b.work is None:
+                self._launch_reduce(b)
+        gathers = []
+        for b in self.buckets:
             if self.world > 1:
-                dist.reduce_scatter_tensor(g.shard_grad, g.grad, op=dist.ReduceOp.AVG, group=self.pg)
-            if g.entries:
-                self.adam_fn(g.entries, self.lr, b1, b2, self.eps, bc1, bc2, self.weight_decay)
+                b.work.wait()
+            b.work = None
+            b.ready = 0
+            if b.entries:
+                self.adam_fn(b.entries, self.lr, b1, b2, self.eps, bc1, bc2, self.weight_decay)
             if self.world > 1:
-                shard = g.total // self.world
-                mine = g.flat[self.rank * shard:(self.rank + 1) * shard]
+                shard = b.total // self.world
+                mine = b.flat[self.rank * shard:(self.rank + 1) * shard]
                 src = mine if self.device.type == "cuda" else mine.clone()
-                dist.all_gather_into_tensor(g.flat, src, group=self.pg)
+                gathers.append(dist.all_gather_into_tensor(b.flat, src, group=self.pg, async_op=True))
+        for w in gathers:
+            w.wait()
 
     def zero_grad(self, set_to_none: bool = True) -> None:
         for p in self.params:
@@ -161,15 +223,18 @@ class ShardedAdam8:
                 p.grad.zero_()
 
     def state_dict(self) -> dict:
-        """This rank's shard of the 8-bit state (int8 m/v, f32 block scales)."""
+        """This rank's shard of the 8-bit state (int8 m/v, f32 block scales), per bucket."""
         return {"step": self.step_count, "world": self.world, "rank": self.rank,
-                "groups": {str(dt): {"m": g.m, "v": g.v, "m_scale": g.ms, "v_scale": g.vs}
-                           for dt, g in self.groups.items()}}
+                "buckets": [{"dtype": str(b.dtype), "m": b.m, "v": b.v, "m_scale": b.ms, "v_scale": b.vs}
+                            for b in self.buckets]}
 
     def load_state_dict(self, sd: dict) -> None:
         if sd["world"] != self.world or sd["rank"] != self.rank:
             raise ValueError("ShardedAdam8.load_state_dict: saved for a different world size / rank")
+        if len(sd["buckets"]) != len(self.buckets):
+            raise ValueError("ShardedAdam8.load_state_dict: saved with a different bucket layout")
         self.step_count = int(sd["step"])
-        for dt, g in self.groups.items():
-            s = sd["groups"][str(dt)]
-            g.m.copy_(s["m"]); g.v.copy_(s["v"]); g.ms.copy_(s["m_scale"]); g.vs.copy_(s["v_scale"])
+        for b, s in zip(self.buckets, sd["buckets"]):
+            if s["dtype"] != str(b.dtype) or s["m"].numel() != b.m.numel():
+                raise ValueError("ShardedAdam8.load_state_dict: saved with a different bucket layout")
+            b.m.copy_(s["m"]); b.v.copy_(s["v"]); b.ms.copy_(s["m_scale"]); b.vs.copy_(s["v_scale"])

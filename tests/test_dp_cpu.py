@@ -48,16 +48,34 @@ def make_grads(rank, step):
     return out
 
 
-def _worker(rank, world, port, steps, q):
+def _worker(rank, world, port, steps, q, mode="assign"):
+    """mode "assign": gradients set on .grad; "overlap": produced by a backward
+    (sum(p * g)) with the reduce-scatter started from the gradient hooks, the
+    buckets small enough to hold one or two parameters, and a first backward
+    of each step under no_sync() whose gradient is then replaced."""
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         params = make_params()
-        opt = ShardedAdam8(params, lr=1e-3, weight_decay=0.01, adam_fn=oracle_adam_fn)
+        if mode == "overlap":
+            opt = ShardedAdam8(params, lr=1e-3, weight_decay=0.01, adam_fn=oracle_adam_fn, bucket_bytes=1024,
+                               overlap_grad_reduce=True)
+            assert len(opt.buckets) > 2
+        else:
+            opt = ShardedAdam8(params, lr=1e-3, weight_decay=0.01, adam_fn=oracle_adam_fn)
         for s in range(1, steps + 1):
-            for p, gr in zip(params, make_grads(rank, s)):
-                p.grad = gr
+            grads = make_grads(rank, s)
+            if mode == "overlap":
+                opt.zero_grad()
+                with opt.no_sync():  # an accumulation micro-batch: no reduce-scatter
+                    sum((p * g).sum() for p, g in zip(params, grads)).backward()
+                opt.zero_grad()
+                sum((p * g).sum() for p, g in zip(params, grads)).backward()
+                assert all(b.work is not None for b in opt.buckets)  # every bucket already in flight
+            else:
+                for p, gr in zip(params, grads):
+                    p.grad = gr
             opt.step()
         q.put((rank, [_np(p.detach()).copy() for p in params], opt.shard_numel))
     finally:
@@ -88,13 +106,13 @@ def expected(world, steps):
     return [_np(p).copy() for p in params]
 
 
-@pytest.mark.parametrize("world", [2, 3])
-def test_sharded_step_equals_single_process(world):
+@pytest.mark.parametrize("world,mode", [(2, "assign"), (3, "assign"), (2, "overlap")])
+def test_sharded_step_equals_single_process(world, mode):
     steps = 3
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, steps, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, steps, q, mode)) for r in range(world)]
     for p in procs:
         p.start()
     results = {}
@@ -125,10 +143,11 @@ def test_single_process_layout_and_views():
     # parameters now live in the flat buffers, values unchanged, 256-aligned starts
     for p, b in zip(params, before):
         assert torch.equal(p.detach(), b)
-    for g in opt.groups.values():
-        for s in g.slots:
+    for b in opt.buckets:
+        assert len({s.param.dtype for s in b.slots}) == 1
+        for s in b.slots:
             assert s.offset % 256 == 0
-            assert s.param.data_ptr() == g.flat[s.offset:].data_ptr()
+            assert s.param.data_ptr() == b.flat[s.offset:].data_ptr()
     for p, gr in zip(params, make_grads(0, 1)):
         p.grad = gr
     opt.step()

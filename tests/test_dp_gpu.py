@@ -70,7 +70,8 @@ def _worker(rank, world, port, q):
         torch.manual_seed(7)
         layers = [PackRLinear.synthetic(64, 128, device=dev, seed=11), PackRLinear.synthetic(128, 32, device=dev, seed=12)]
         mp_ = [p for l in layers for p in (l.W_f, l.lut, l.bias_f)]
-        dopt = ShardedAdam8(mp_, lr=1e-2)
+        # several buckets, each reduce-scatter started from the gradient hooks
+        dopt = ShardedAdam8(mp_, lr=1e-2, bucket_bytes=1 << 14, overlap_grad_reduce=True)
         gx = torch.Generator().manual_seed(99)
         X = torch.randn(8, 64, generator=gx).to(dev)
         Y = torch.randn(8, 32, generator=gx).to(dev)
@@ -164,7 +165,6 @@ def test_grad_sink_single_gpu(cuda):
     g = torch.Generator(device=dev).manual_seed(0)
     x = torch.randn(300, 256, generator=g, device=dev).to(torch.bfloat16)
     dy = torch.randn(300, 128, generator=g, device=dev)
-    flat = opt.groups[torch.bfloat16].grad
     opt.zero_grad()
     ropt.zero_grad()
     for _ in range(2):  # two micro-batches: the second accumulates into the sink
@@ -173,6 +173,7 @@ def test_grad_sink_single_gpu(cuda):
     close = lambda a, b: torch.allclose(a, b, rtol=1e-5, atol=1e-6 * b.abs().max().item())
     for l, t in zip(lays, twins):
         gptr = l.W_f.grad.data_ptr()
+        flat = opt.bucket_of(l.W_f).grad
         assert flat.data_ptr() <= gptr < flat.data_ptr() + flat.numel() * flat.element_size()
         assert torch.equal(l.W_f.grad, t.W_f.grad)
         assert close(l.lut.grad, t.lut.grad)
