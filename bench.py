@@ -17,6 +17,11 @@ Workloads (synthetic, seeded; no dataset exists for this path):
   decode forward of the same three layers at M = 16 tokens (--tokens to
          change): the decode-bound regime; metric GB/s of packed weights
          (3 bytes per weight) streamed per second.
+  bert   BERT-base fine-tune step (FFN layers compressed, batch 32 x seq 128,
+         CUDA8BitAdam); metric sequences/s, with the PackRLinear and Adam
+         shares of the step.
+  llama8b Llama-3-8B-shaped decoder, every Linear a PackRLinear, seq 2048,
+         micro-batch 1 per GPU, data parallel; metric tokens/s.
   adam8  CUDA8BitAdam step over one flat 110,000,000-element bf16 parameter
          (lr 2e-5, betas (0.9, 0.999), eps 1e-8, wd 0.01, block 256); metric
          Gparam/s.  Per step the inputs (1.1 GB) exceed L2 (126 MB).
@@ -414,6 +419,121 @@ def bench_decode(args, world, rank, peaks, peak_kind):
     return line
 
 
+def bench_bert(args, world, rank, peaks, peak_kind):
+    """BERT-base fine-tune step (12 layers, hidden 768, FFN 3072, 12 heads,
+    vocab 30522), random init, FFN Linear layers compressed to PackRLinear,
+    batch 32 x seq 128 of random ids, 2-class labels, CUDA8BitAdam over all
+    ~110M params (fp32 model, bf16 W_f)."""
+    from packr_b200 import kernel as K
+    from packr_b200 import workloads as wl
+    from packr_b200.cuda_adam import CUDA8BitAdam
+    from packr_b200.dp import ShardedAdam8
+    dev = torch.device("cuda", torch.cuda.current_device())
+    model = wl.bert_classifier(dev, seed=0)
+    model.train()
+    params = [p for p in model.parameters() if p.requires_grad]
+    n_params = sum(p.numel() for p in params)
+    if world > 1:
+        opt = ShardedAdam8(params, lr=2e-5, weight_decay=0.01, overlap_grad_reduce=True)
+    else:
+        opt = CUDA8BitAdam(params, lr=2e-5, weight_decay=0.01)
+    ids, labels = wl.bert_batch(dev, seed=rank)
+
+    def step():
+        opt.zero_grad(set_to_none=True)
+        model(input_ids=ids, labels=labels).loss.backward()
+        opt.step()
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        total_ms, per = timed(step, args.steps, args.warmup, world, warm_seconds=1.5)
+    ms_step = total_ms / args.steps
+    value = world * 32 / (ms_step * 1e-3)
+    # shares: the optimizer step alone, and the 24 compressed layers' fwd+bwd alone
+    _, a_per = timed(opt.step, max(args.steps, 10), 3, 1)
+    adam_ms = statistics.mean(a_per)
+    layers = [m for m in model.modules() if m.__class__.__name__ == "PackRLinear"]
+    xs = {l: torch.randn(32 * 128, l.in_features, device=dev) for l in layers[:2]}
+    dys = {l: torch.randn(32 * 128, l.out_features, device=dev) for l in layers[:2]}
+
+    def packr_layers():
+        for l in layers[:2]:
+            cnt = l.lut_counts()
+            K.forward(xs[l], l.W_p, l.W_f, l.lut, l.bias_f)
+            K.backward(dys[l], xs[l], l.W_p, l.W_f, l.lut, cnt, True, True, True, l.bias_f is not None)
+    _, l_per = timed(packr_layers, max(args.steps, 10), 3, 1)
+    packr_ms = statistics.mean(l_per) * len(layers) / 2
+    flops_packr = sum(6.0 * 32 * 128 * l.in_features * l.out_features for l in layers)
+    line = {
+        "metric": "BERT-base fine-tune sequences/s (FFN compressed to PackRLinear)", "value": round(value, 1),
+        "unit": "sequences/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp32 model, bf16 W_f operands", "data": "synthetic (random ids, 2-class labels)",
+        "config": {"workload": "bert: BERT-base (12 x 768, FFN 3072, 12 heads, vocab 30522), FFN layers as "
+                               "PackRLinear (compress_model, layer_scope='ffn'), batch 32 x seq 128 per GPU",
+                   "params": n_params, "packr_layers": len(layers),
+                   "optimizer": "CUDA8BitAdam" if world == 1 else "ShardedAdam8 (ZeRO-1, overlapped reduce-scatter)",
+                   "parallelism": f"dp{world}"},
+        "shares_ms": {"step": round(ms_step, 4), "packr_linear_fwd_bwd": round(packr_ms, 4),
+                      "adam": round(adam_ms, 4)},
+        "roofline": {"bound": "tensor", "achieved": round(flops_packr / (packr_ms * 1e-3) / 1e12, 1),
+                     "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": round(flops_packr / (packr_ms * 1e-3) / 1e12 / peaks["bf16_tflops"], 4),
+                     "traffic": None, "peak_source": f"{peak_kind} bf16_tflops",
+                     "kernel": "PackRLinear forward + backward of the 24 compressed layers (f32 x: fp32-faithful dW)",
+                     "algorithmic_flops_per_launch": flops_packr},
+        "gpu_launches": None,
+        "clocks": clk.summary(),
+    }
+    return line
+
+
+def bench_llama(args, world, rank, peaks, peak_kind):
+    """Llama-3-8B-shaped decoder (32 x 4096, FFN 14336, 32 q / 8 kv heads,
+    vocab 128256), random init, every Linear a synthetic PackRLinear, bf16,
+    seq 2048, micro-batch 1 per GPU, data parallel with ShardedAdam8."""
+    from packr_b200 import workloads as wl
+    from packr_b200.dp import ShardedAdam8
+    dev = torch.device("cuda", torch.cuda.current_device())
+    layers = int(os.environ.get("PACKR_BENCH_LLAMA_LAYERS", "32"))
+    model = wl.llama_decoder(dev, layers=layers, seed=0)
+    model.train()
+    params = [p for p in model.parameters() if p.requires_grad]
+    n_params = sum(p.numel() for p in params)
+    opt = ShardedAdam8(params, lr=2e-5, weight_decay=0.01, overlap_grad_reduce=True)
+    seq = args.tokens if args.tokens_given else 2048
+    ids = wl.llama_batch(dev, seq=seq, seed=rank)
+    linear_weights = sum(m.inner.in_features * m.inner.out_features for m in model.modules()
+                         if m.__class__.__name__ == "_Cast")
+
+    def step():
+        opt.zero_grad(set_to_none=True)
+        model(input_ids=ids, labels=ids).loss.backward()
+        opt.step()
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        total_ms, per = timed(step, args.steps, args.warmup, world, warm_seconds=1.5)
+    ms_step = total_ms / args.steps
+    value = world * seq / (ms_step * 1e-3)
+    flops = 6.0 * seq * linear_weights
+    line = {
+        "metric": "Llama-3-8B-shaped training tokens/s (every Linear a PackRLinear)", "value": round(value, 1),
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16 activations, bf16 W_f operands, f32 accumulate", "data": "synthetic (random ids)",
+        "config": {"workload": f"llama8b: {layers} x 4096, FFN 14336, 32/8 heads, vocab 128256, every Linear "
+                               f"PackRLinear (synthetic init), seq {seq}, micro-batch 1 per GPU",
+                   "params": n_params, "linear_weights": linear_weights,
+                   "optimizer": "ShardedAdam8 (ZeRO-1, overlapped reduce-scatter)", "parallelism": f"dp{world}"},
+        "roofline": {"bound": "tensor", "achieved": round(flops / (ms_step * 1e-3) / 1e12, 1),
+                     "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": round(flops / (ms_step * 1e-3) / 1e12 / peaks["bf16_tflops"], 4), "traffic": None,
+                     "peak_source": f"{peak_kind} bf16_tflops",
+                     "kernel": "whole step; FLOPs = 6 x tokens x Linear weights (attention not counted)",
+                     "algorithmic_flops_per_launch": flops},
+        "gpu_launches": None,
+        "clocks": clk.summary(),
+    }
+    return line
+
+
 def layer_launches(M: int, K: int, N: int) -> int:
     """libpackr_b200 kernels one PackRLinear forward + backward launches for
     bf16 x (K % 8 == 0), no bias, cached lut counts: forward = [predecode] +
@@ -614,7 +734,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="ffn", choices=["ffn", "adam8", "decode"])
+    ap.add_argument("--workload", default="ffn", choices=["ffn", "adam8", "decode", "bert", "llama8b"])
     ap.add_argument("--tokens", type=int, default=None, help="tokens per GPU (ffn: 4096, decode: 16)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -638,7 +758,8 @@ def main():
     if args.profile_once:
         profile_once(args)
         return
-    fn = {"ffn": bench_ffn, "adam8": bench_adam8, "decode": bench_decode}[args.workload]
+    fn = {"ffn": bench_ffn, "adam8": bench_adam8, "decode": bench_decode, "bert": bench_bert,
+          "llama8b": bench_llama}[args.workload]
     line = fn(args, world, rank, peaks, peak_kind)
     if rank == 0:
         print(json.dumps(line), flush=True)
