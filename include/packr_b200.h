@@ -150,6 +150,22 @@ int packr_decode_bf16(const uint8_t* W_p, const uint16_t* W_f, const float* lut,
 int packr_predecode_bf16(const uint8_t* W_p, const uint16_t* W_f, const float* lut, uint16_t* out, int64_t K,
                          int64_t N, void* stream);
 
+/* ---- VelvetController support ---------------------------------------------
+ * sums[i] (double, device) = sum of parameter i's int8 second-moment codes,
+ * each times its block's v_scale when block_size > 0, unweighted when
+ * block_size == 0 (reference packr/velvet.py:296-320
+ * takes the mean of the [blocks, block_size] view, or of the raw codes when
+ * that view would need padding; the caller divides by numel).  One launch for
+ * all parameters (the reference reads one `.item()` per parameter). */
+typedef struct packr_vsum_desc {
+  const int8_t* v;
+  const float* v_scale;  /* used when block_size > 0 */
+  int64_t numel;
+  int64_t block_size;    /* 0: sum of the raw codes */
+  int64_t block_origin;  /* element i is scaled by v_scale[(block_origin + i) / block_size] */
+} packr_vsum_desc;
+int packr_state_v_sums(const packr_vsum_desc* descs, int n, double* sums, void* stream);
+
 /* packr_backward without a caller-provided workspace, for callers that cannot
  * allocate device memory (a host runtime with a fixed device-memory budget
  * and no allocator of its own, a binding that can pass tensors it was given

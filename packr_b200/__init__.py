@@ -4,7 +4,7 @@ Drop-in for the reference package's public surface on this path
 (reference packr/__init__.py:13-45, packr/cuda_adam.py:142):
 
     import packr_b200 as packr
-    from packr_b200 import compress_model, PackRConfig, PackRLinear
+    from packr_b200 import compress_model, PackRConfig, PackRLinear, VelvetController
     from packr_b200.cuda_adam import CUDA8BitAdam
 
 Every op runs hand-written sm_100a kernels from libpackr_b200.so through its
@@ -17,6 +17,7 @@ from .layer_patcher import compress_model
 from .config import PackRConfig, SchemeType
 from .optim import FusedQuantizedAdam
 from .cuda_adam import CUDA8BitAdam
+from .velvet import VelvetController
 
 # Legacy aliases (reference packr/__init__.py:29-34)
 PHRConfig = PackRConfig
@@ -26,6 +27,6 @@ phr_matmul = packr_matmul
 
 __all__ = [
     "PackRConfig", "PackRLinear", "PackRMatmulFunction", "PackRLinearFunction", "packr_matmul", "compress_model",
-    "SchemeType", "FusedQuantizedAdam", "CUDA8BitAdam",
+    "SchemeType", "FusedQuantizedAdam", "CUDA8BitAdam", "VelvetController",
     "PHRConfig", "PHRLinear", "PHRMatmulFunction", "phr_matmul",
 ]

@@ -56,10 +56,15 @@ SIGNATURES = {
     "packr_lut_finalize": (_I32, [_VP, _VP, _VP, _VP]),
     "packr_decode_bf16": (_I32, [_VP, _VP, _VP, _VP, _I64, _I64, _VP]),
     "packr_predecode_bf16": (_I32, [_VP, _VP, _VP, _VP, _I64, _I64, _VP]),
+    "packr_state_v_sums": (_I32, [_VP, _I32, _VP, _VP]),
     "packr_backward_static_scratch": (_I32, [_VP, _VP, _I32, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _I64, _I64,
                                              _I64, _I32, _VP]),
 }
 PACKR_BWD_DW_SPLIT = 1
+
+
+class VSumDesc(ctypes.Structure):
+    _fields_ = [("v", _VP), ("v_scale", _VP), ("numel", _I64), ("block_size", _I64), ("block_origin", _I64)]
 
 
 def lib_path() -> Path:

@@ -10,3 +10,4 @@
 #include "skinny.cu"
 #include "linear.cu"
 #include "static_scratch.cu"
+#include "velvet.cu"

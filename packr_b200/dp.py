@@ -84,7 +84,11 @@ class ShardedAdam8:
         self.params = [p for p in params if p.requires_grad]
         if not self.params:
             raise ValueError("ShardedAdam8: no trainable parameters")
-        self.lr, self.betas, self.eps, self.weight_decay = lr, betas, eps, weight_decay
+        self.betas, self.eps, self.weight_decay = betas, eps, weight_decay
+        # one group, so that LR controllers (VelvetController, schedulers) can
+        # set group["lr"] as they do on a torch optimizer
+        self.param_groups = [{"params": self.params, "lr": lr}]
+        self.state: dict = {}  # the 8-bit state lives in the buckets (state_dict, v_means)
         self.pg = process_group
         if dist.is_available() and dist.is_initialized():
             self.world = dist.get_world_size(self.pg)
@@ -146,6 +150,14 @@ class ShardedAdam8:
             la, le = a - s0, e - s0
             ba, be = la // BLOCK, (le + BLOCK - 1) // BLOCK
             b.entries.append((b.flat[a:e], b.shard_grad[la:le], b.m[la:le], b.v[la:le], b.ms[ba:be], b.vs[ba:be]))
+
+    @property
+    def lr(self) -> float:
+        return self.param_groups[0]["lr"]
+
+    @lr.setter
+    def lr(self, value: float) -> None:
+        self.param_groups[0]["lr"] = value
 
     @property
     def shard_numel(self) -> int:
@@ -214,6 +226,32 @@ class ShardedAdam8:
                 gathers.append(dist.all_gather_into_tensor(b.flat, src, group=self.pg, async_op=True))
         for w in gathers:
             w.wait()
+
+    @torch.no_grad()
+    def v_means(self) -> dict:
+        """{id(param): mean of the dequantised second moment} over the whole
+        parameter, for VelvetController.  Each rank sums the codes x block
+        scale of the parameter slices in its shard (one packr_state_v_sums
+        launch), one all-reduce of the per-parameter sums (the same call on
+        every rank) combines the shards, one copy brings them to the host."""
+        from .velvet import state_v_sums
+        slices, where = [], []
+        for i, p in enumerate(self.params):
+            b = self._bucket_of[id(p)]
+            shard = b.total // self.world
+            s0 = self.rank * shard
+            slot = next(s for s in b.slots if s.param is p)
+            a, e = max(slot.offset, s0), min(slot.offset + slot.numel, s0 + shard)
+            if a < e:
+                slices.append((b.v, b.vs, a - s0, e - a, BLOCK))
+                where.append(i)
+        sums = torch.zeros(len(self.params), dtype=torch.float64, device=self.device)
+        if slices:
+            sums.index_copy_(0, torch.tensor(where, device=self.device), state_v_sums(slices, self.device))
+        if self.world > 1:
+            dist.all_reduce(sums, group=self.pg)
+        n = torch.tensor([max(p.numel(), 1) for p in self.params], dtype=torch.float64, device=self.device)
+        return dict(zip((id(p) for p in self.params), (sums / n).cpu().tolist()))
 
     def zero_grad(self, set_to_none: bool = True) -> None:
         for p in self.params:
