@@ -56,6 +56,7 @@ SIGNATURES = {
     "packr_lut_finalize": (_I32, [_VP, _VP, _VP, _VP]),
     "packr_decode_bf16": (_I32, [_VP, _VP, _VP, _VP, _I64, _I64, _VP]),
     "packr_predecode_bf16": (_I32, [_VP, _VP, _VP, _VP, _I64, _I64, _VP]),
+    "packr_selfcheck_rounding": (_I32, [_VP, _VP]),
     "packr_state_v_sums": (_I32, [_VP, _I32, _VP, _VP]),
     "packr_backward_static_scratch": (_I32, [_VP, _VP, _I32, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _I64, _I64,
                                              _I64, _I32, _VP]),

@@ -171,6 +171,32 @@ __device__ __forceinline__ f32x2 div_recip2(f32x2 a, f32x2 neg_b, f32x2 y) {
   return fma2(r, y, q);
 }
 
+// -RN(v/bc2) by Markstein with the negated reciprocal -RN(1/bc2): RN is
+// symmetric, so every step is the exact negation of the one for RN(v/bc2).
+__device__ __forceinline__ f32x2 neg_div_bc2(f32x2 v, const Pairs& C) {
+  const f32x2 nq = mul2(v, C.nyb2);
+  return fma2(fma2(nq, C.pb2, v), C.nyb2, nq);
+}
+
+// RN(RN(lr*T1) / RN(RN(sqrt(T2)) + eps)) on a pair, given T1 = RN(m/bc1) and
+// nT2 = -RN(v/bc2): the square root by the residual correction carried
+// negated (ng = -g, e = g*g - x, ns = -(g + (x - g*g)*h)), d = s + eps carried
+// as nd = -d, its reciprocal by one Newton step, the quotient by Markstein.
+// Each step is the exact negation of the sequence in the header.
+__device__ __forceinline__ f32x2 fast_update2(f32x2 T1, f32x2 nT2, const Pairs& C) {
+  float x0, x1;
+  upk2(nT2, x0, x1);
+  const f32x2 r0 = pk2(rsqrt_approx(-x0), rsqrt_approx(-x1));
+  const f32x2 ng = mul2(nT2, r0);
+  const f32x2 ns = fma2(fma2(ng, ng, nT2), mul2(C.half, r0), ng);
+  const f32x2 nd = sub2(ns, C.eps);
+  float d0, d1;
+  upk2(nd, d0, d1);
+  const f32x2 y0 = pk2(rcp_approx(-d0), rcp_approx(-d1));
+  const f32x2 y = fma2(y0, fma2(nd, y0, C.one), y0);
+  return div_recip2(mul2(C.lr, T1), nd, y);
+}
+
 // int8 -> float without the conversion unit: (x ^ 0x80) is x + 128 in
 // [0, 255]; placed in the low byte of 2^23 (0x4B000000) it forms the float
 // 2^23 + 128 + x exactly, and subtracting 2^23 + 128 leaves x exactly.
@@ -491,11 +517,7 @@ __global__ void __launch_bounds__(kThreads, 2) adam8_kernel(const __grid_constan
         const f32x2 QM = div_recip2(MN[j], nms2, yms);
         const f32x2 QV = div_recip2(VN[j], nvs2, yvs);
         const f32x2 T1 = div_recip2(MN[j], C.nb1, C.yb1);
-        // -T2 = -RN(v_new/bc2) by Markstein with the negated reciprocal:
-        // RN is symmetric, so every step is the exact negation of the one
-        // for T2.
-        const f32x2 nq2 = mul2(VN[j], C.nyb2);
-        const f32x2 nT2 = fma2(fma2(nq2, C.pb2, VN[j]), C.nyb2, nq2);
+        const f32x2 nT2 = neg_div_bc2(VN[j], C);
         {
           float q0, q1, u0, u1;
           upk2(add2(QM, f32x2((MN[j] & 0x8000000080000000ull) | 0x3F0000003F000000ull)), q0, q1);
@@ -509,21 +531,7 @@ __global__ void __launch_bounds__(kThreads, 2) adam8_kernel(const __grid_constan
           mw[j >> 1] = pack4(cm[0], cm[1], cm[2], cm[3]);
           vw[j >> 1] = pack4(cv[0], cv[1], cv[2], cv[3]);
         }
-        // s = RN(sqrt(T2)) by the residual correction, carried negated:
-        // ng = -g, e = g*g - x = -(x - g*g), ns = -(g + (x - g*g) * h)
-        float x0, x1;
-        upk2(nT2, x0, x1);
-        const f32x2 r0 = pk2(rsqrt_approx(-x0), rsqrt_approx(-x1));
-        const f32x2 ng = mul2(nT2, r0);
-        const f32x2 ns = fma2(fma2(ng, ng, nT2), mul2(C.half, r0), ng);
-        // d = s + eps (carried as nd = -d), its correctly rounded reciprocal,
-        // (lr * T1) / d
-        const f32x2 nd = sub2(ns, C.eps);
-        float d0, d1;
-        upk2(nd, d0, d1);
-        const f32x2 y0 = pk2(rcp_approx(-d0), rcp_approx(-d1));
-        const f32x2 y = fma2(y0, fma2(nd, y0, C.one), y0);
-        const f32x2 upd = div_recip2(mul2(C.lr, T1), nd, y);
+        const f32x2 upd = fast_update2(T1, nT2, C);
         f32x2 P = raw_pair<BF16>(praw, j);
         if (h.wd > 0.0f) P = fma2(C.nlrwd, P, P);
         float p0, p1;
@@ -561,7 +569,8 @@ __global__ void __launch_bounds__(kThreads, 2) adam8_kernel(const __grid_constan
           vw[j >> 1] = pack4(cv[0], cv[1], cv[2], cv[3]);
         }
         if constexpr (BF16) {
-          po[j] = pack_bf16x2_rne(pn[0], pn[1]);
+          // the reference's integer rounding (also for a NaN it produces)
+          po[j] = f32_to_bf16_rne(pn[0]) | (f32_to_bf16_rne(pn[1]) << 16);
         } else {
           po[2 * j] = __float_as_uint(pn[0]);
           po[2 * j + 1] = __float_as_uint(pn[1]);
@@ -596,6 +605,90 @@ __global__ void __launch_bounds__(kThreads, 2) adam8_kernel(const __grid_constan
     stage = stage == kStages - 1 ? 0 : stage + 1;
   }
   cp_async_wait<0>();
+}
+
+Hyper make_hyper(float lr, float beta1, float beta2, float eps, float bc1, float bc2, float weight_decay) {
+  Hyper h{};
+  h.lr = lr; h.b1 = beta1; h.b2 = beta2; h.eps = eps; h.bc1 = bc1; h.bc2 = bc2; h.wd = weight_decay;
+  // host float arithmetic is IEEE round-to-nearest (SSE), as on the device
+  auto two = [](float x) {
+    uint32_t u;
+    std::memcpy(&u, &x, 4);
+    return ((unsigned long long)u << 32) | u;
+  };
+  const volatile float one = 1.0f;
+  const float one_m_b1 = one - beta1, one_m_b2 = one - beta2, lr_wd = lr * weight_decay;
+  const float y_bc1 = (float)(1.0 / (double)bc1), y_bc2 = (float)(1.0 / (double)bc2);
+  h.pr = Pairs{two(beta1), two(one_m_b1), two(beta2), two(one_m_b2), two(-lr_wd), two(y_bc1), two(-bc1),
+               two(-y_bc2), two(bc2), two(lr), two(eps), two(1.0f), two(0.5f), two(8388736.0f)};
+  // Fast-path ranges: bias corrections in [2^-20, 1] (so the moments'
+  // quotients stay below 2^120), eps and lr finite and below 2^40.
+  const bool in_range = bc1 >= 0x1p-20f && bc1 <= 1.0f && bc2 >= 0x1p-20f && bc2 <= 1.0f && eps >= 0.0f &&
+                        eps < 0x1p+40f && lr >= 0.0f && lr < 0x1p+40f && weight_decay >= 0.0f &&
+                        weight_decay < 0x1p+40f;
+  if (in_range) {
+    h.lr_bc1 = (float)((double)lr / (double)bc1);
+    h.inv_bc2 = (float)(1.0 / (double)bc2);
+    h.fast_ok = 1;
+  }
+  return h;
+}
+
+// Self-check of the short correctly rounded sequences against CUDA's IEEE
+// operations: [0] RN(1/b) for every positive normal b with a normal
+// reciprocal, [1] RN(sqrt(x)) for every x in [2^-100, 2^128), [2] Markstein
+// quotients a/b on pseudo-random pairs (exponents of a in [-96, 100), of b in
+// [-20, 20)), [3] the whole parameter update RN(RN(lr*RN(m/bc1)) /
+// RN(RN(sqrt(RN(v/bc2))) + eps)) on pseudo-random m in +-[2^-40, 2^20] and v
+// in [2^-80, 2^40].
+__device__ __forceinline__ uint32_t mix32(unsigned long long x) {
+  x ^= x >> 33;
+  x *= 0xff51afd7ed558ccdull;
+  x ^= x >> 33;
+  x *= 0xc4ceb9fe1a85ec53ull;
+  x ^= x >> 33;
+  return (uint32_t)x;
+}
+__device__ __forceinline__ float rand_float(uint32_t h, int emin, int espan, bool sign) {
+  const uint32_t e = (uint32_t)(127 + emin + (int)((h >> 23) % (uint32_t)espan));
+  return __uint_as_float((sign && (h & 1u) ? 0x80000000u : 0u) | (e << 23) | ((h * 2654435761u) & 0x7FFFFFu));
+}
+
+__global__ void selfcheck_kernel(unsigned long long* bad, const Hyper h, unsigned long long nrand) {
+  const unsigned long long tid = (unsigned long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const unsigned long long nth = (unsigned long long)gridDim.x * blockDim.x;
+  unsigned long long c0 = 0, c1 = 0, c2 = 0, c3 = 0;
+  for (unsigned long long i = 0x00800000ull + tid; i < 0x7E800000ull; i += nth) {
+    const float b = __uint_as_float((uint32_t)i);
+    c0 += __float_as_uint(rcp_rn_newton(b)) != __float_as_uint(__frcp_rn(b));
+  }
+  for (unsigned long long i = 0x0D800000ull + tid; i < 0x7F800000ull; i += nth) {
+    const float x = __uint_as_float((uint32_t)i);
+    c1 += __float_as_uint(sqrt_rn_residual(x)) != __float_as_uint(__fsqrt_rn(x));
+  }
+  const Pairs& C = h.pr;
+  for (unsigned long long i = tid; i < nrand; i += nth) {
+    const uint32_t ha = mix32(4 * i), hb = mix32(4 * i + 1), hm = mix32(4 * i + 2), hv = mix32(4 * i + 3);
+    const float a = rand_float(ha, -96, 196, true), b = rand_float(hb, -20, 40, false);
+    const float y = rcp_rn_newton(b);
+    float q0, q1;
+    upk2(div_recip2(pk2(a, -a), pk2(-b, -b), pk2(y, y)), q0, q1);
+    c2 += (__float_as_uint(q0) != __float_as_uint(__fdiv_rn(a, b))) + (__float_as_uint(q1) != __float_as_uint(__fdiv_rn(-a, b)));
+    const float m = rand_float(hm, -40, 61, true), v = rand_float(hv, -80, 121, false);
+    const float m2 = -m * 0.75f, v2 = v * 1.25f;
+    const f32x2 MN = pk2(m, m2), VN = pk2(v, v2);
+    float u0, u1;
+    upk2(fast_update2(div_recip2(MN, C.nb1, C.yb1), neg_div_bc2(VN, C), C), u0, u1);
+    auto ieee = [&](float mm, float vv) {
+      const float t1 = __fdiv_rn(mm, h.bc1), t2 = __fdiv_rn(vv, h.bc2);
+      return __fdiv_rn(__fmul_rn(h.lr, t1), __fadd_rn(__fsqrt_rn(t2), h.eps));
+    };
+    c3 += (__float_as_uint(u0) != __float_as_uint(ieee(m, v))) + (__float_as_uint(u1) != __float_as_uint(ieee(m2, v2)));
+  }
+  if (c0) atomicAdd(bad + 0, c0);
+  if (c1) atomicAdd(bad + 1, c1);
+  if (c2) atomicAdd(bad + 2, c2);
+  if (c3) atomicAdd(bad + 3, c3);
 }
 
 template <bool BF16>
@@ -672,33 +765,23 @@ extern "C" int packr_adam8_multi(const packr_adam_tensor* tensors, int n_tensors
       return PACKR_ERR_ALIGNMENT;
     (t.dtype == PACKR_DTYPE_BF16 ? any_bf16 : any_f32) = true;
   }
-  adam::Hyper h{};
-  h.lr = lr; h.b1 = beta1; h.b2 = beta2; h.eps = eps; h.bc1 = bc1; h.bc2 = bc2; h.wd = weight_decay;
-  {
-    // host float arithmetic is IEEE round-to-nearest (SSE), as on the device
-    auto two = [](float x) {
-      uint32_t u;
-      std::memcpy(&u, &x, 4);
-      return ((unsigned long long)u << 32) | u;
-    };
-    const volatile float one = 1.0f;
-    const float one_m_b1 = one - beta1, one_m_b2 = one - beta2, lr_wd = lr * weight_decay;
-    const float y_bc1 = (float)(1.0 / (double)bc1), y_bc2 = (float)(1.0 / (double)bc2);
-    h.pr = adam::Pairs{two(beta1), two(one_m_b1), two(beta2), two(one_m_b2), two(-lr_wd), two(y_bc1), two(-bc1),
-                       two(-y_bc2), two(bc2), two(lr), two(eps), two(1.0f), two(0.5f), two(8388736.0f)};
-  }
-  // Fast-path ranges: bias corrections in [2^-20, 1] (so the moments'
-  // quotients stay below 2^120), eps and lr finite and below 2^40.
-  const bool in_range = bc1 >= 0x1p-20f && bc1 <= 1.0f && bc2 >= 0x1p-20f && bc2 <= 1.0f && eps >= 0.0f &&
-                        eps < 0x1p+40f && lr >= 0.0f && lr < 0x1p+40f && weight_decay >= 0.0f &&
-                        weight_decay < 0x1p+40f;
-  if (in_range) {
-    h.lr_bc1 = (float)((double)lr / (double)bc1);
-    h.inv_bc2 = (float)(1.0 / (double)bc2);
-    h.fast_ok = 1;
-  }
+  const adam::Hyper h = adam::make_hyper(lr, beta1, beta2, eps, bc1, bc2, weight_decay);
   cudaStream_t s = as_stream(stream);
   if (any_bf16 && (st = adam::launch_dtype<true>(tensors, n_tensors, h, s)) != PACKR_OK) return st;
   if (any_f32 && (st = adam::launch_dtype<false>(tensors, n_tensors, h, s)) != PACKR_OK) return st;
   return PACKR_OK;
+}
+
+extern "C" int packr_selfcheck_rounding(unsigned long long* mismatches, void* stream) {
+  using namespace packr;
+  if (mismatches == nullptr) return PACKR_ERR_INVALID_ARGUMENT;
+  if (!aligned(mismatches, 8)) return PACKR_ERR_ALIGNMENT;
+  int st = check_device();
+  if (st != PACKR_OK) return st;
+  cudaStream_t s = as_stream(stream);
+  if (cudaMemsetAsync(mismatches, 0, 4 * sizeof(unsigned long long), s) != cudaSuccess) return PACKR_ERR_CUDA;
+  // lr 2e-5, bc1 = 1 - 0.9, bc2 = 1 - 0.999 (first step), eps 1e-8
+  const adam::Hyper h = adam::make_hyper(2e-5f, 0.9f, 0.999f, 1e-8f, 0.1f, 0.001f, 0.0f);
+  adam::selfcheck_kernel<<<sm_count() * 8, 256, 0, s>>>(mismatches, h, 1ull << 30);
+  return launch_status();
 }

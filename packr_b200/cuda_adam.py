@@ -35,6 +35,21 @@ def _init_state(state, p):
     state["v_scale"] = torch.ones(nb, dtype=torch.float32, device=p.device)
 
 
+def selfcheck_rounding(device="cuda") -> list[int]:
+    """Mismatch counts of the kernel's short correctly rounded sequences
+    against CUDA's IEEE operations on `device` (packr_selfcheck_rounding):
+    [reciprocals, square roots, quotients, whole updates]; all 0 when the
+    device computes them exactly."""
+    lib = _lib.load()
+    dev = torch.device(device)
+    out = torch.empty(4, dtype=torch.int64, device=dev)
+    with torch.cuda.device(dev):
+        code = lib.packr_selfcheck_rounding(ctypes.c_void_p(out.data_ptr()),
+                                            ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream))
+    _lib.check("packr_selfcheck_rounding", code)
+    return [int(v) for v in out.cpu().tolist()]
+
+
 def adam8_launch(entries, lr, b1, b2, eps, bc1, bc2, wd, stream=None) -> None:
     """Runs packr_adam8_multi over `entries` = [(p, g, m, v, ms, vs), ...] of
     CUDA tensors on one device.  p/g are bf16 or f32 (same dtype), contiguous."""

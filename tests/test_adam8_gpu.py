@@ -29,6 +29,61 @@ def new_state(n, dev="cuda"):
             torch.ones(nb, device=dev), torch.ones(nb, device=dev))
 
 
+def test_rounding_selfcheck(cuda):
+    """The kernel's short correctly rounded reciprocal / square root /
+    quotient / update sequences equal CUDA's IEEE operations: exhaustively
+    over their argument ranges for the reciprocal and the square root, on
+    2^30 pseudo-random cases for the quotient and the whole update."""
+    from packr_b200.cuda_adam import selfcheck_rounding
+    assert selfcheck_rounding(cuda) == [0, 0, 0, 0]
+
+
+def _special_grads(n, step, dtype, nonfinite):
+    """Gradients with exact zeros, tiny and huge values (and, with
+    `nonfinite`, Inf and NaN) in some blocks: those blocks take the kernel's
+    IEEE path."""
+    g = adam_grad(n, step, dtype=dtype, device="cuda", std=1e-2).clone()
+    if step == 1:
+        g[0:300] = 0                 # zero moments
+    g[700] = 1e-30                   # moments below the fast path's range
+    g[1300] = 3e18                   # v above it
+    if nonfinite and step == 3:
+        g[2000] = float("inf")
+        g[2600] = float("nan")
+    return g
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("nonfinite", [False, True])
+def test_special_values_vs_oracle(cuda, dtype, nonfinite):
+    """Blocks outside the fast path's ranges equal the oracle bit for bit.
+    With Inf/NaN gradients the codes and scales still do; the parameters are
+    compared where the oracle's are finite (a NaN's bits are the CPU's or the
+    GPU's own)."""
+    n = 4096 + 77
+    p = adam_params(n, dtype=dtype, seed=5, device="cuda")
+    st = new_state(n)
+    hp, hm, hv, hms, hvs = np_bits(p), *[np_bits(t) for t in st]
+    lr, b1, b2, eps, wd = 1e-3, 0.9, 0.999, 1e-8, 0.01
+    for s in range(1, 5):
+        bc1, bc2 = oracle.adam8_bias_corrections(b1, b2, s)
+        g = _special_grads(n, s, dtype, nonfinite)
+        adam8_launch([(p, g, *st)], lr, b1, b2, eps, bc1, bc2, wd)
+        torch.cuda.synchronize()
+        oracle.adam8_step(hp, np_bits(g), hm, hv, hms, hvs, lr, b1, b2, eps, bc1, bc2, wd)
+        assert np.array_equal(np_bits(st[2]).view(np.uint32), hms.view(np.uint32)), s
+        assert np.array_equal(np_bits(st[3]).view(np.uint32), hvs.view(np.uint32)), s
+        assert np.array_equal(np_bits(st[0]), hm), s
+        assert np.array_equal(np_bits(st[1]), hv), s
+        got = np_bits(p)
+        if not nonfinite:
+            assert np.array_equal(got, hp), s
+        else:
+            fin = np.isfinite(torch.from_numpy(hp.view(np.int16)).view(torch.bfloat16).float().numpy()
+                              if dtype == torch.bfloat16 else hp)
+            assert np.array_equal(got[fin], hp[fin]), s
+
+
 @pytest.mark.parametrize("wd", [0.0, 0.01])
 def test_multi_tensor_bit_exact_vs_oracle(cuda, wd):
     sizes = [1, 7, 255, 256, 257, 4096 + 13, 3 * 256, 100_003]
