@@ -1,6 +1,7 @@
 """Benchmark of PackR's training hot path on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload ffn|adam8|decode] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload ffn|adam8|decode|bert|llama8b|from_linear]
+                    [--impl ours|reference]
 
 Prints ONE JSON line (rank 0).  For N>1 it is launched by torchrun, one rank
 per GPU (NCCL); every rank runs the same per-GPU workload (weak scaling) and
@@ -22,6 +23,10 @@ Workloads (synthetic, seeded; no dataset exists for this path):
          shares of the step.
   llama8b Llama-3-8B-shaped decoder, every Linear a PackRLinear, seq 2048,
          micro-batch 1 per GPU, data parallel; metric tokens/s.
+  from_linear  PackRLinear.from_linear of one Llama-3-8B decoder layer's
+         seven bf16 Linear weights (q, k, v, o 4096-wide; gate, up 4096->14336;
+         down 14336->4096: 218 M weights, three of them above torch.quantile's
+         2^24 limit); metric Gweights/s.
   adam8  CUDA8BitAdam step over one flat 110,000,000-element bf16 parameter
          (lr 2e-5, betas (0.9, 0.999), eps 1e-8, wd 0.01, block 256); metric
          Gparam/s.  Per step the inputs (1.1 GB) exceed L2 (126 MB).
@@ -693,6 +698,101 @@ def profile_once(args):
     torch.cuda.synchronize()
 
 
+LLAMA_LINEARS = [("q_proj", 4096, 4096), ("k_proj", 4096, 1024), ("v_proj", 4096, 1024), ("o_proj", 4096, 4096),
+                 ("gate_proj", 4096, 14336), ("up_proj", 4096, 14336), ("down_proj", 14336, 4096)]
+
+
+def cpu_from_linear_port(budget_s: float):
+    """The reference's from_linear operation sequence (packr/layer.py:106-159,
+    restated op for op in PackRLinear._from_linear_torch) on the host cores,
+    on a 1024 -> 4096 bf16 layer (the reference's torch.quantile refuses the
+    full Llama layers)."""
+    from packr_b200 import PackRLinear
+    torch.manual_seed(0)
+    lin = torch.nn.Linear(1024, 4096, bias=False).to(torch.bfloat16)
+    times = []
+    t0 = time.perf_counter()
+    while len(times) < 2 or time.perf_counter() - t0 < budget_s:
+        a = time.perf_counter()
+        PackRLinear._from_linear_torch(lin)
+        times.append(time.perf_counter() - a)
+    sec = statistics.median(times)
+    return {"value": 1024 * 4096 / sec / 1e9, "unit": "Gweights/s", "cores": torch.get_num_threads(),
+            "kind": "port", "sample": f"from_linear of a 1024->4096 bf16 Linear, {len(times)} timed samples (median); "
+                                      "the reference's torch operation sequence on the CPU",
+            "host_cores": os.cpu_count()}
+
+
+def bench_from_linear(args, world, rank, peaks, peak_kind):
+    """PackRLinear.from_linear (GPU path) of one Llama-3-8B decoder layer's
+    seven bf16 weights; algorithmic bytes 5 per weight (read W 2, write W_p 1
+    and W_f 2)."""
+    from packr_b200 import PackRLinear, kernel as K
+    from packr_b200.layer import _build_codebook
+    dev = torch.device("cuda", torch.cuda.current_device())
+    g = torch.Generator(device=dev).manual_seed(0)
+    lins = []
+    for name, k, n in LLAMA_LINEARS:
+        lin = torch.nn.Linear(k, n, bias=False, device="meta")
+        lin.weight = torch.nn.Parameter((torch.randn(n, k, generator=g, device=dev) * 0.02).to(torch.bfloat16))
+        lins.append(lin)
+    nw = sum(k * n for _, k, n in LLAMA_LINEARS)
+
+    def step():
+        for lin in lins:
+            PackRLinear.from_linear(lin)
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        total_ms, per = timed(step, args.steps, args.warmup, world, warm_seconds=1.0)
+    ms_step = total_ms / args.steps
+    value = world * nw / (ms_step * 1e-3) / 1e9
+    # the encode pass alone (the dominant kernel), on the largest weight
+    big = lins[4].weight.detach()
+    cb = _build_codebook().to(dev)
+    scale = torch.full((), 40.0, device=dev)
+    _, enc = timed(lambda: K.from_linear_encode(big, cb, scale), args.steps, args.warmup, world)
+    enc_bytes = 5.0 * big.numel()
+    achieved = enc_bytes / (statistics.mean(enc) * 1e-3) / 1e9
+    host = [lin.weight.detach().cpu().pin_memory() for lin in lins]
+    dlin = []
+    for (name, k, n), h in zip(LLAMA_LINEARS, host):
+        lin = torch.nn.Linear(k, n, bias=False, device="meta")
+        lin.weight = torch.nn.Parameter(torch.empty_like(h, device=dev))
+        dlin.append(lin)
+    hwp = [torch.empty(k, n, dtype=torch.uint8, pin_memory=True) for _, k, n in LLAMA_LINEARS]
+    hwf = [torch.empty(k, n, dtype=torch.bfloat16, pin_memory=True) for _, k, n in LLAMA_LINEARS]
+
+    def e2e_step():
+        for i, lin in enumerate(dlin):
+            lin.weight.data.copy_(host[i], non_blocking=True)
+            pk = PackRLinear.from_linear(lin)
+            hwp[i].copy_(pk.W_p, non_blocking=True)
+            hwf[i].copy_(pk.W_f, non_blocking=True)
+    e2e_ms, _ = timed(e2e_step, max(1, args.steps // 2), max(args.warmup, 1), world)
+    e2e_steps = max(1, args.steps // 2)
+    line = {
+        "metric": "PackRLinear.from_linear Gweights/s (Llama-3-8B decoder layer, bf16)", "value": round(value, 3),
+        "unit": "Gweights/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16 weights, f32 select and encode", "data": "synthetic (seeded N(0, 0.02) weights)",
+        "config": {"workload": "from_linear: q/k/v/o/gate/up/down weights of one Llama-3-8B layer "
+                               f"({nw / 1e6:.1f} M weights) per GPU",
+                   "l2": "weights 0.44 GB per step, larger than L2", "parallelism": f"replicas x{world}"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None,
+                     "peak_source": f"{peak_kind} hbm_gbs",
+                     "kernel": "encode_kernel<bf16> on the 14336 x 4096 gate weight",
+                     "algorithmic_bytes_per_launch": enc_bytes},
+        "e2e": {"value": round(world * nw / (e2e_ms / e2e_steps * 1e-3) / 1e9, 3), "unit": "Gweights/s",
+                "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in host),
+                "d2h_bytes_per_step": sum(t.numel() * t.element_size() for t in hwp + hwf)},
+        "gpu_launches": args.steps * len(LLAMA_LINEARS) * 9,
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_from_linear_port(args.cpu_seconds)
+    return line
+
+
 def reference_arm(args, world, rank):
     if rank != 0:
         return None
@@ -716,6 +816,17 @@ def reference_arm(args, world, rank):
                 "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
                 "e2e": {"value": round(cb["value"], 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
+    if args.workload == "from_linear":
+        cb = cpu_from_linear_port(max(5.0, 0.5 * args.steps))
+        return {"impl": "reference", "metric": "PackRLinear.from_linear Gweights/s (Llama-3-8B decoder layer, bf16)",
+                "value": round(cb["value"], 5), "unit": "Gweights/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "bf16 weights", "data": "synthetic",
+                "config": {"workload": "from_linear: 1024->4096 bf16 Linear (CPU; the reference refuses the "
+                                       "Llama gate/up/down weights above 2^24 elements)"},
+                "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                "e2e": {"value": round(cb["value"], 5), "unit": "Gweights/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
     if args.workload == "ffn":
         cb = cpu_linear_port(max(5.0, 0.5 * args.steps))
         return {"impl": "reference", "metric": "PackRLinear fwd+bwd TFLOP/s (Llama FFN shapes)",
@@ -734,7 +845,8 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="ffn", choices=["ffn", "adam8", "decode", "bert", "llama8b"])
+    ap.add_argument("--workload", default="ffn",
+                    choices=["ffn", "adam8", "decode", "bert", "llama8b", "from_linear"])
     ap.add_argument("--tokens", type=int, default=None, help="tokens per GPU (ffn: 4096, decode: 16)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -759,7 +871,7 @@ def main():
         profile_once(args)
         return
     fn = {"ffn": bench_ffn, "adam8": bench_adam8, "decode": bench_decode, "bert": bench_bert,
-          "llama8b": bench_llama}[args.workload]
+          "llama8b": bench_llama, "from_linear": bench_from_linear}[args.workload]
     line = fn(args, world, rank, peaks, peak_kind)
     if rank == 0:
         print(json.dumps(line), flush=True)

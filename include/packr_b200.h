@@ -159,6 +159,27 @@ int packr_decode_bf16(const uint8_t* W_p, const uint16_t* W_f, const float* lut,
 int packr_predecode_bf16(const uint8_t* W_p, const uint16_t* W_f, const float* lut, uint16_t* out, int64_t K,
                          int64_t N, void* stream);
 
+/* ---- PackRLinear.from_linear (reference packr/layer.py:106-159) ----------
+ * Step 1: the rank_lo-th and rank_hi-th smallest |w| (0-based; rank_hi is
+ * rank_lo or rank_lo + 1) of n weights (f32 or bf16), as f32, written to
+ * out2[0..1] on the device: the two order statistics torch.quantile
+ * interpolates (layer.py:127), found by an exact radix select without
+ * sorting and without torch.quantile's 2^24-element limit.  Workspace of
+ * packr_abs_order_stats_workspace_bytes(), 16-byte aligned. */
+size_t packr_abs_order_stats_workspace_bytes(void);
+int packr_abs_order_stats(const void* w, int dtype, int64_t n, int64_t rank_lo, int64_t rank_hi,
+                          float* out2, void* workspace, size_t workspace_bytes, void* stream);
+/* Step 2: weight [out_features, in_features] (nn.Linear layout, f32 or bf16)
+ * -> W_p u8 and W_f bf16 [in_features, out_features], lut f32 [256]:
+ * t = clamp(w * target_scale, -1.6, 1.6) (bf16-rounded for a bf16 weight),
+ * W_p = the nearest codebook entry (lowest index on ties; layer.py:137-141),
+ * lut = codebook / scale (layer.py:144), W_f = bf16(w - lut[W_p])
+ * (layer.py:148).  codebook (256 f32), scale and target_scale (1 f32 each;
+ * target_scale may be NULL = scale) on the device. */
+int packr_from_linear_encode(const void* weight, int dtype, int64_t out_features, int64_t in_features,
+                             const float* codebook, const float* scale, const float* target_scale,
+                             uint8_t* W_p, uint16_t* W_f, float* lut, void* stream);
+
 /* ---- VelvetController support ---------------------------------------------
  * sums[i] (double, device) = sum of parameter i's int8 second-moment codes,
  * each times its block's v_scale when block_size > 0, unweighted when

@@ -11,3 +11,4 @@
 #include "linear.cu"
 #include "static_scratch.cu"
 #include "velvet.cu"
+#include "compress.cu"

@@ -187,6 +187,81 @@ def backward(dY: torch.Tensor, x: torch.Tensor, W_p: torch.Tensor, W_f: torch.Te
     return dX, dW, dlut, dbias
 
 
+def abs_order_stats(w: torch.Tensor, rank_lo: int, rank_hi: int) -> torch.Tensor:
+    """[2] f32 device tensor: the rank_lo-th and rank_hi-th smallest |w|
+    (0-based) of a CUDA f32/bf16 tensor (packr_abs_order_stats)."""
+    lib = _lib.load()
+    w = w.contiguous()
+    dev = w.device
+    out = torch.empty(2, dtype=torch.float32, device=dev)
+    ws = torch.empty(lib.packr_abs_order_stats_workspace_bytes(), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        code = lib.packr_abs_order_stats(_ptr(w), _dtype_code(w), w.numel(), rank_lo, rank_hi, _ptr(out), _ptr(ws),
+                                         ws.numel(), _stream(dev))
+    _lib.check("packr_abs_order_stats", code)
+    return out
+
+
+def quantile_abs(w: torch.Tensor, q: float) -> torch.Tensor:
+    """torch.quantile(w.abs().float(), q) (linear interpolation) on the
+    device, for any size: the same rank arithmetic (f32 q * (n - 1), floor,
+    ceil, fractional weight) and the same torch.lerp, over order statistics
+    found by the library's radix select instead of a full sort."""
+    n = w.numel()
+    pos = torch.tensor(q, dtype=torch.float32) * (n - 1)
+    lo, hi = int(torch.floor(pos)), int(torch.ceil(pos))
+    v = abs_order_stats(w, lo, hi)
+    return torch.lerp(v[0], v[1], (pos - lo).to(w.device))
+
+
+def bf16_product_multiplier(scale: torch.Tensor) -> torch.Tensor:
+    """The f32 multiplier torch uses in `bf16_tensor * scale` for a 0-dim f32
+    device tensor `scale` (the product is computed in f32 and rounded to
+    bf16): probed once per device with torch itself."""
+    dev = scale.device
+    key = str(dev)
+    mode = _BF16_SCALAR_MODE.get(key)
+    if mode is None:
+        g = torch.Generator(device="cpu").manual_seed(0)
+        probe_w = torch.randn(4096, generator=g).to(torch.bfloat16).to(dev)
+        probe_s = torch.tensor(1.0 + 2 ** -8 + 2 ** -12 + 2 ** -19, dtype=torch.float32, device=dev)
+        got = probe_w * probe_s
+        as_f32 = (probe_w.float() * probe_s).to(torch.bfloat16)
+        as_bf16 = (probe_w.float() * probe_s.to(torch.bfloat16).float()).to(torch.bfloat16)
+        if torch.equal(got, as_f32):
+            mode = "f32"
+        elif torch.equal(got, as_bf16):
+            mode = "bf16"
+        else:
+            raise RuntimeError("bf16 * f32 scalar: torch's product matches neither rounding")
+        _BF16_SCALAR_MODE[key] = mode
+    return scale if mode == "f32" else scale.to(torch.bfloat16).float()
+
+
+_BF16_SCALAR_MODE: dict = {}
+
+
+def from_linear_encode(weight: torch.Tensor, codebook: torch.Tensor, scale: torch.Tensor,
+                       target_scale: torch.Tensor | None = None):
+    """(W_p u8 [in, out], W_f bf16 [in, out], lut f32 [256]) from an
+    nn.Linear weight [out, in] (packr_from_linear_encode)."""
+    lib = _lib.load()
+    w = weight.contiguous()
+    dev = w.device
+    out_f, in_f = w.shape
+    W_p = torch.empty(in_f, out_f, dtype=torch.uint8, device=dev)
+    W_f = torch.empty(in_f, out_f, dtype=torch.bfloat16, device=dev)
+    lut = torch.empty(256, dtype=torch.float32, device=dev)
+    cb = codebook.to(device=dev, dtype=torch.float32).contiguous()
+    sc = scale.to(device=dev, dtype=torch.float32).reshape(1).contiguous()
+    ts = target_scale.to(device=dev, dtype=torch.float32).reshape(1).contiguous() if target_scale is not None else sc
+    with torch.cuda.device(dev):
+        code = lib.packr_from_linear_encode(_ptr(w), _dtype_code(w), out_f, in_f, _ptr(cb), _ptr(sc), _ptr(ts),
+                                            _ptr(W_p), _ptr(W_f), _ptr(lut), _stream(dev))
+    _lib.check("packr_from_linear_encode", code)
+    return W_p, W_f, lut
+
+
 def packr_matmul(x, W_p, W_f, lut, bias=None):
     """PackR matmul: out = x @ (W_f + lut[W_p]) + bias  (float32 [M, N]).
 

@@ -95,9 +95,20 @@ class PackRLinear(nn.Module):
     def from_linear(cls, module: nn.Linear):
         """Convert an nn.Linear (reference layer.py:106-159): scale |W| so its
         99th percentile maps to 1.6, take the nearest codebook entry per weight
-        (lowest index on ties), lut = codebook / scale, W_f = W - lut[W_p]."""
+        (lowest index on ties), lut = codebook / scale, W_f = W - lut[W_p].
+
+        A CUDA f32/bf16 weight is compressed by the library's kernels (exact
+        order statistics for the quantile, one encode pass; no size limit);
+        other weights by the same torch operations as the reference."""
         if not isinstance(module, nn.Linear):
             raise TypeError(f"Expected nn.Linear, got {type(module)}")
+        if module.weight.is_cuda and module.weight.dtype in (torch.float32, torch.bfloat16):
+            return cls._from_linear_cuda(module)
+        return cls._from_linear_torch(module)
+
+    @classmethod
+    def _from_linear_torch(cls, module: nn.Linear):
+        """The reference's torch operation sequence (any device)."""
         packr = cls(module.in_features, module.out_features, bias=module.bias is not None)
         device = module.weight.device
         codebook = _build_codebook().to(device)
@@ -122,6 +133,31 @@ class PackRLinear(nn.Module):
         if module.bias is not None:
             packr.bias_f.data = module.bias.detach().to(device=device, dtype=torch.bfloat16)
         return packr
+
+    @classmethod
+    def _from_linear_cuda(cls, module: nn.Linear):
+        from . import kernel
+        w = module.weight.detach()
+        device = w.device
+        in_f, out_f = module.in_features, module.out_features
+        q99 = kernel.quantile_abs(w, 0.99) + 1e-6
+        scale = 1.6 / q99
+        # W_orig * scale for a bf16 weight: the multiplier as torch applies it
+        target_scale = kernel.bf16_product_multiplier(scale) if w.dtype == torch.bfloat16 else scale
+        W_p, W_f, lut = kernel.from_linear_encode(w, _build_codebook().to(device), scale, target_scale)
+        m = cls.__new__(cls)
+        nn.Module.__init__(m)
+        m.in_features, m.out_features = in_f, out_f
+        m.W_p = nn.Parameter(W_p, requires_grad=False)
+        m.W_f = nn.Parameter(W_f)
+        m.lut = nn.Parameter(lut)
+        m.bias_f = (nn.Parameter(module.bias.detach().to(device=device, dtype=torch.bfloat16).clone())
+                    if module.bias is not None else None)
+        m._counts = None
+        m._counts_key = None
+        m._offload_mgr = None
+        m._layer_name = None
+        return m
 
     @classmethod
     def synthetic(cls, in_features, out_features, bias=True, *, device="cuda", seed=0, lut_std=0.02,
