@@ -6,10 +6,12 @@ the library is missing or the device is not sm_100, every op raises.
 from __future__ import annotations
 
 import ctypes
+import os
 import threading
 from pathlib import Path
 
-_LIB_PATH = Path(__file__).resolve().parent / "libpackr_b200.so"
+# PACKR_B200_LIB selects another build of the library (the same ABI)
+_LIB_PATH = Path(os.environ.get("PACKR_B200_LIB") or Path(__file__).resolve().parent / "libpackr_b200.so")
 _lock = threading.Lock()
 _lib = None
 

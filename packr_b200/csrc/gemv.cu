@@ -3,20 +3,26 @@
 // with W decoded exactly as the reference's forward decodes it,
 // W = f32(W_f) + f32(fp16(lut[W_p])) (packr/kernel.py:127-130), and an f32
 // accumulation on the CUDA cores.  At these sizes the work is streaming W
-// once from HBM (3 bytes per weight); a 256-row tensor-core tile would waste
-// almost all of its rows, and the fused decode GEMM can only spread N/256
-// tiles over the SMs.
+// once from HBM (3 bytes per weight); a 128-row tensor-core tile would waste
+// almost all of its rows.
 //
-// Pass 1 (gemv_partial_kernel): CTA (column block, K split); each of its 8
-// warps owns 32 * CPT columns and walks every row of the split for them.  Per
-// row a lane loads CPT W_f values and CPT W_p bytes with one vector load each
-// (the next group of rows in flight while one is used), looks the bytes up in
-// a lane-replicated shared copy of the fp16-rounded lut (bank-conflict free),
-// and accumulates x[m, k] * W[k, n] for every m in packed f32 pairs, x[:,
-// split] staged in shared memory as f32.  The sums of each split go to
-// partial[split][m][n].  Pass 2 (gemv_reduce_kernel) adds the splits in a
-// fixed order and the bias: the result does not depend on timing.
+// One launch (gemv_cluster_kernel): a CTA owns 32 * CPT columns (each lane
+// CPT adjacent columns, loaded with one vector load of W_f and one of W_p per
+// row) and a K range; its 8 warps split that range, each streaming its rows
+// with the next group of rows in flight, looking the bytes up in a
+// lane-replicated shared copy of the fp16-rounded lut (bank-conflict free)
+// and accumulating x[m, k] * W[k, n] for every m in packed f32 pairs (x of
+// the CTA's range staged in shared memory).  The C CTAs of a thread-block
+// cluster (C = 8 or 16) split K for the same columns.  The sums are combined
+// in a fixed order (the 8 warps in order inside a CTA, then the C CTAs in
+// rank order through distributed shared memory, each CTA finishing a 1/C
+// slice of the columns and adding the bias), so the result does not depend
+// on timing and no partial sums go through global memory.
+//
+// gemv_reduce_kernel (a fixed-order sum of split partials plus the bias) is
+// the final pass of the skinny tensor-core forward.
 #include "common.cuh"
+#include "sm100.cuh"
 
 #include <cuda_fp16.h>
 
@@ -40,7 +46,6 @@ __device__ __forceinline__ f32x2 fma2(f32x2 a, f32x2 b, f32x2 c) {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kRowUnroll = 4;
 constexpr int kMaxM = 16;
 
 // Vector loads of CPT consecutive W_f (bf16) and W_p (u8) values.
@@ -81,30 +86,54 @@ struct WVec<2> {
   __device__ __forceinline__ uint32_t pword(int) const { return p; }
 };
 
-// Dynamic shared memory: lut copy [256][32] u32 | x [rows][M] as (x, x) f32
-// pairs, ready to be the packed multiplier of fma.rn.f32x2.
-// M is a compile-time bound on the rows; Mr <= M rows are real (x rows past
-// Mr read as zero and their sums are not written).  Warp w of the CTA owns
-// the 32 * CPT columns starting at (blockIdx.x * 8 + w) * 32 * CPT and walks
-// every row of the CTA's K range for them, kRowUnroll rows per load group
-// with the next group in flight; its sums go straight to the partial array.
-template <int M, int CPT, int U>
-__global__ void __launch_bounds__(kThreads, (M <= 2 ? 4 : 3))
-    gemv_partial_kernel(const void* __restrict__ x, int x_f32, int Mr, const uint8_t* __restrict__ W_p,
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+// Dynamic shared memory: lut copy [256][32] u32 (reused for the 8 warps'
+// sums [8][MB][32 * CPT] f32 after the stream) | x [rows][MB] as (x, x) f32
+// pairs | this CTA's sums [MB][32 * CPT] f32.  MB is a compile-time bound
+// on the rows; Mr <= MB rows are real (rows past Mr read x as zero and are
+// not written).
+template <int MB, int CPT>
+__host__ __device__ constexpr size_t cluster_smem(int rows_per_cta) {
+  return 256 * 32 * 4 + (size_t)rows_per_cta * MB * 8 + (size_t)MB * 32 * CPT * 4;
+}
+
+#ifndef PACKR_GEMV_ROWS_IN_FLIGHT
+#define PACKR_GEMV_ROWS_IN_FLIGHT 4
+#endif
+#ifndef PACKR_GEMV_MIN_CTAS
+#define PACKR_GEMV_MIN_CTAS 3
+#endif
+template <int MB, int CPT, int U>
+__global__ void __launch_bounds__(kThreads, (MB <= 2 ? PACKR_GEMV_MIN_CTAS : 2))
+    gemv_cluster_kernel(const void* __restrict__ x, int x_f32, int Mr, const uint8_t* __restrict__ W_p,
                         const uint16_t* __restrict__ W_f, const float* __restrict__ lut,
-                        float* __restrict__ partial, int K, int N, int rows_per_split) {
+                        const void* __restrict__ bias, int bias_f32, float* __restrict__ out, int K, int N,
+                        int rows_per_cta, int rows_per_warp) {
+  static_assert(8 * MB * 32 * CPT <= 256 * 32, "warp sums must fit in the lut region");
+  constexpr int kCols = 32 * CPT;
   extern __shared__ __align__(16) uint32_t gsm[];
-  uint32_t* lut_s = gsm;                                 // 256 * 32
-  f32x2* xs = reinterpret_cast<f32x2*>(gsm + 256 * 32);  // rows_per_split * M
-  constexpr int kStrip = 32 * CPT;
+  uint32_t* lut_s = gsm;                                   // 256 * 32
+  float* red = reinterpret_cast<float*>(gsm);              // [8][MB][kCols], after the stream
+  f32x2* xs = reinterpret_cast<f32x2*>(gsm + 256 * 32);    // rows_per_cta * MB
+  float* part = reinterpret_cast<float*>(gsm + 256 * 32 + 2 * rows_per_cta * MB);  // [MB][kCols]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int k0 = blockIdx.y * rows_per_split;
-  const int k1 = min(K, k0 + rows_per_split);
-  const int nrows = k1 - k0;
+  const int C = (int)gridDim.y;  // one cluster spans the K splits of a column block
+  const int rank = (int)sm100::cluster_ctarank();
+  const int k0 = rank * rows_per_cta;
+  const int k1 = min(K, k0 + rows_per_cta);
+  const int nrows_cta = max(0, k1 - k0);
   for (int e = warp; e < 256; e += kWarps)
     lut_s[e * 32 + lane] = __float_as_uint(__half2float(__float2half_rn(__ldg(lut + e))));
-  for (int i = threadIdx.x; i < nrows * M; i += kThreads) {
-    const int r = i / M, m = i - r * M;
+  for (int i = threadIdx.x; i < nrows_cta * MB; i += kThreads) {
+    const int r = i / MB, m = i - r * MB;
     const long long src = (long long)m * K + k0 + r;
     const float v = m >= Mr ? 0.0f
                             : x_f32 ? __ldg(static_cast<const float*>(x) + src)
@@ -113,14 +142,14 @@ __global__ void __launch_bounds__(kThreads, (M <= 2 ? 4 : 3))
   }
   __syncthreads();
 
-  const long long n0 = ((long long)blockIdx.x * kWarps + warp) * kStrip + lane * CPT;
-  if (n0 >= N) return;  // N % CPT == 0: a chunk is whole or absent
+  const long long n0 = (long long)blockIdx.x * kCols + lane * CPT;
+  const bool live = n0 < N;  // N % CPT == 0: a lane's columns are whole or absent
+  const int r0 = warp * rows_per_warp;  // rows of this warp, relative to k0
+  const int r1 = min(nrows_cta, r0 + rows_per_warp);
   const uint32_t* lut_lane = lut_s + lane;
-  // accumulators as packed pairs of adjacent columns (fma.rn.f32x2 rounds
-  // each half exactly as the scalar fma would)
-  f32x2 acc[M][CPT / 2];
+  f32x2 acc[MB][CPT / 2];
 #pragma unroll
-  for (int m = 0; m < M; ++m)
+  for (int m = 0; m < MB; ++m)
 #pragma unroll
     for (int j = 0; j < CPT / 2; ++j) acc[m][j] = 0ull;
 
@@ -134,45 +163,98 @@ __global__ void __launch_bounds__(kThreads, (M <= 2 ? 4 : 3))
       const float f1 = __fadd_rn(__uint_as_float(fw & 0xFFFF0000u), __uint_as_float(lut_lane[((pw >> 8) & 0xFFu) * 32]));
       wv[j] = pk2(f0, f1);
     }
-    const f32x2* xr = xs + r * M;
+    const f32x2* xr = xs + r * MB;
 #pragma unroll
-    for (int m = 0; m < M; ++m) {
+    for (int m = 0; m < MB; ++m) {
       const f32x2 x2 = xr[m];
 #pragma unroll
       for (int j = 0; j < CPT / 2; ++j) acc[m][j] = fma2(x2, wv[j], acc[m][j]);
     }
   };
-  auto load_group = [&](WVec<CPT>* w, int r) {
+  // Rows of this warp in groups of U, loads of the next group in flight
+  // while one is consumed (ping-pong buffers, row pointers advanced by N).
+  if (live && r1 > r0) {
+    const long long base = (long long)(k0 + r0) * N + n0;
+    const uint16_t* pf = W_f + base;
+    const uint8_t* pp = W_p + base;
+    const int full = (r1 - r0) / U;  // whole groups
+    WVec<CPT> a[U], b[U];
+    auto load = [&](WVec<CPT>* w) {
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      if (r + u < nrows) {
-        const long long off = (long long)(k0 + r + u) * N + n0;
-        w[u].load(W_f + off, W_p + off);
+      for (int u = 0; u < U; ++u) {
+        w[u].load(pf, pp);
+        pf += N;
+        pp += N;
+      }
+    };
+    auto eat = [&](const WVec<CPT>* w, int r) {
+#pragma unroll
+      for (int u = 0; u < U; ++u) consume(w[u], r + u);
+    };
+    int r = r0;
+    if (full > 0) {
+      load(a);
+      int g = 1;
+      for (; g + 1 < full; g += 2) {
+        load(b);
+        eat(a, r);
+        r += U;
+        load(a);
+        eat(b, r);
+        r += U;
+      }
+      if (g < full) {
+        load(b);
+        eat(a, r);
+        r += U;
+        eat(b, r);
+        r += U;
+      } else {
+        eat(a, r);
+        r += U;
       }
     }
-  };
-  WVec<CPT> cur[U], nxt[U];
-  load_group(cur, 0);
-  for (int r = 0; r < nrows; r += U) {
-    load_group(nxt, r + U);
-#pragma unroll
-    for (int u = 0; u < U; ++u)
-      if (r + u < nrows) consume(cur[u], r + u);
-#pragma unroll
-    for (int u = 0; u < U; ++u) cur[u] = nxt[u];
-  }
-  float* dst = partial + (long long)blockIdx.y * Mr * N + n0;
-#pragma unroll
-  for (int m = 0; m < M; ++m) {
-    if (m < Mr) {
-#pragma unroll
-      for (int j = 0; j < CPT / 2; ++j) {
-        float a0, a1;
-        upk2(acc[m][j], a0, a1);
-        *reinterpret_cast<float2*>(dst + (long long)m * N + 2 * j) = make_float2(a0, a1);
-      }
+    for (; r < r1; ++r) {  // the last rows, one at a time
+      WVec<CPT> t;
+      t.load(pf, pp);
+      pf += N;
+      pp += N;
+      consume(t, r);
     }
   }
+  __syncthreads();  // every warp is done with the lut and x copies
+#pragma unroll
+  for (int m = 0; m < MB; ++m)
+#pragma unroll
+    for (int j = 0; j < CPT / 2; ++j) {
+      float a0, a1;
+      upk2(acc[m][j], a0, a1);
+      *reinterpret_cast<float2*>(&red[(warp * MB + m) * kCols + lane * CPT + 2 * j]) = make_float2(a0, a1);
+    }
+  __syncthreads();
+  for (int i = threadIdx.x; i < MB * kCols; i += kThreads) {
+    float t = red[i];
+#pragma unroll
+    for (int w = 1; w < kWarps; ++w) t = __fadd_rn(t, red[w * MB * kCols + i]);
+    part[i] = t;
+  }
+  cluster_sync_all();  // every CTA's sums are visible to the cluster
+  // CTA `rank` finishes columns [rank * kCols / C, (rank + 1) * kCols / C)
+  const int per = kCols / C;
+  const uint32_t part_s = sm100::smem_u32(part);
+  for (int i = threadIdx.x; i < MB * per; i += kThreads) {
+    const int m = i / per, c = rank * per + (i - m * per);
+    const long long n = (long long)blockIdx.x * kCols + c;
+    float t = 0.0f;
+    for (int q = 0; q < C; ++q) t = __fadd_rn(t, ld_cluster_f32(sm100::mapa(part_s + 4u * (uint32_t)(m * kCols + c), q)));
+    if (m < Mr && n < N) {
+      if (bias != nullptr)
+        t = __fadd_rn(t, bias_f32 ? __ldg(static_cast<const float*>(bias) + n)
+                                  : bf16_to_f32(__ldg(static_cast<const uint16_t*>(bias) + n)));
+      out[(long long)m * N + n] = t;
+    }
+  }
+  cluster_sync_all();  // no CTA leaves while a peer may still read its sums
 }
 
 // out[m, n] = sum over splits of partial[s][m][n] + bias[n], in a fixed
@@ -211,121 +293,119 @@ __global__ void __launch_bounds__(256) gemv_reduce_kernel(const float* __restric
   }
 }
 
+inline int row_bound(long long M) { return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : M <= 8 ? 8 : 16; }
+
+// Columns per lane: 8 up to 4 rows (16-byte W_f loads), 4 for 8 rows, 2 for
+// 16 (the accumulators of more rows would cost occupancy).
+inline int cols_per_lane(int mb, long long N) {
+  const int c = mb <= 4 ? 8 : mb <= 8 ? 4 : 2;
+  return (N % c == 0) ? c : (N % 4 == 0 && c > 4 ? 4 : (N % 2 == 0 ? 2 : 0));
+}
+
 struct Plan {
-  int mb;  // compile-time row bound used for M
-  int cpt, splits, rows_per_split;
+  int mb, cpt, cluster, rows_per_cta, rows_per_warp;
+  long long col_blocks;
   size_t smem;
 };
 
-inline int row_bound(long long M) { return M <= 2 ? (int)M : M <= 4 ? 4 : M <= 8 ? 8 : M <= 12 ? 12 : 16; }
-
-// Columns per thread: 8 for one row (one 16-byte W_f load), 4 up to 8 rows,
-// 2 beyond (the accumulators of 12-16 rows would cost occupancy).  K is split so that the grid is about one wave of
-// `resident` CTAs per SM, with the partial sums (splits x M x N f32) at most
-// about a tenth of W's bytes and the x slice of a split (8 bytes per value)
-// at most 32 KB.
-inline Plan plan(long long M, long long K, long long N, int resident = 8) {
+// Cluster size: 8, or 16 when 8 would leave the grid under two CTAs per SM;
+// never more than K / 64 (so a warp gets rows).
+inline Plan plan(long long M, long long K, long long N) {
   Plan p{};
   p.mb = row_bound(M);
-  p.cpt = (N % 8 == 0 && p.mb <= 1) ? 8 : p.mb >= 12 ? 2 : 4;
-  const long long col_blocks = (N + (long long)kWarps * 32 * p.cpt - 1) / ((long long)kWarps * 32 * p.cpt);
-  long long splits = ((long long)resident * sm_count() + col_blocks - 1) / col_blocks;
-  long long cap = (3 * K) / (40 * M);  // partial bytes <= ~W bytes / 10
-  if (cap < 1) cap = 1;
-  if (splits > cap) splits = cap;
-  const long long min_splits = (K * p.mb * 8 + 32767) / 32768;  // x slice <= 32 KB
-  if (splits < min_splits) splits = min_splits;
-  if (splits > K) splits = K;
-  if (splits < 1) splits = 1;
-  const long long rows = (K + splits - 1) / splits;
-  p.rows_per_split = (int)rows;
-  p.splits = (int)((K + rows - 1) / rows);
-  p.smem = 256 * 32 * 4 + (size_t)rows * p.mb * 8;
+  p.cpt = cols_per_lane(p.mb, N);
+  if (p.cpt == 0) return p;
+  p.col_blocks = (N + 32LL * p.cpt - 1) / (32LL * p.cpt);
+  int c = p.col_blocks * 8 >= 2LL * sm_count() ? 8 : 16;
+  while (c > 1 && K < 64LL * c) c >>= 1;
+  p.cluster = c;
+  p.rows_per_cta = (int)((K + c - 1) / c);
+  p.rows_per_warp = (p.rows_per_cta + kWarps - 1) / kWarps;
   return p;
 }
 
-// Usable for this problem: few rows, W rows whole vector chunks, aligned bases.
+// Usable for this problem: few rows, whole vector chunks, aligned bases, and
+// the x slice of a CTA in shared memory.
 inline bool eligible(long long M, long long K, long long N, const uint8_t* W_p, const uint16_t* W_f) {
-  if (M < 1 || M > kMaxM || (N % 4) != 0 || K < 1) return false;
+  if (M < 1 || M > kMaxM || K < 1 || N < 2 || K > 0x7FFFFFFFLL || N > 0x7FFFFFFFLL) return false;
   const Plan p = plan(M, K, N);
+  if (p.cpt == 0 || (long long)p.rows_per_cta * p.mb * 8 > 96 * 1024) return false;
   const uintptr_t va = 2 * p.cpt;  // bytes of one W_f chunk
   return aligned(W_f, va) && aligned(W_p, va / 2);
 }
 
-// Upper bound over the resident count (at most 8 CTAs of 256 threads per SM).
-inline size_t workspace_bytes(long long M, long long K, long long N) {
-  const Plan p = plan(M, K, N, 8);
-  return (size_t)p.splits * M * N * sizeof(float);
-}
+inline size_t workspace_bytes(long long, long long, long long) { return 0; }
 
-template <int M, int CPT, int U = 4>
-int launch_m(Plan p, const void* x, int x_f32, int Mr, const uint8_t* W_p, const uint16_t* W_f,
-             const float* lut, float* partial, long long K, long long N, cudaStream_t st, int* splits_out) {
+template <int MB, int CPT, int U = PACKR_GEMV_ROWS_IN_FLIGHT>
+int launch(const Plan& p, const void* x, int x_f32, int Mr, const uint8_t* W_p, const uint16_t* W_f, const float* lut,
+           const void* bias, int bias_f32, float* out, long long K, long long N, cudaStream_t st) {
+  auto kern = gemv_cluster_kernel<MB, CPT, U>;
   static int attr_done[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr_done[dev & 63]) {
-    if (cudaFuncSetAttribute(gemv_partial_kernel<M, CPT, U>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) !=
-        cudaSuccess)
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024) != cudaSuccess ||
+        cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
       return PACKR_ERR_CUDA;
     attr_done[dev & 63] = 1;
   }
-  // one wave: the most CTAs per SM whose own plan (its x slice in shared
-  // memory) still lets that many be resident
-  for (int c = 8; c >= 1; --c) {
-    const Plan q = plan((long long)Mr, K, N, c);
-    int fit = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&fit, gemv_partial_kernel<M, CPT, U>, kThreads, q.smem) !=
-        cudaSuccess) {
+  Plan q = p;
+  for (;;) {
+    q.rows_per_cta = (int)((K + q.cluster - 1) / q.cluster);
+    q.rows_per_warp = (q.rows_per_cta + kWarps - 1) / kWarps;
+    q.smem = cluster_smem<MB, CPT>(q.rows_per_cta);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)q.col_blocks, (unsigned)q.cluster, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = q.smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = (unsigned)q.cluster;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess) {
       cudaGetLastError();
-      fit = 0;
+      clusters = 0;
     }
-    p = q;
-    if (fit >= c) break;
+    if (clusters < 1 && q.cluster > 1) {  // a cluster this large does not fit: halve it
+      q.cluster >>= 1;
+      continue;
+    }
+    if (cudaLaunchKernelEx(&cfg, kern, x, x_f32, Mr, W_p, W_f, lut, bias, bias_f32, out, (int)K, (int)N,
+                           q.rows_per_cta, q.rows_per_warp) != cudaSuccess)
+      return launch_status();
+    return launch_status();
   }
-  *splits_out = p.splits;
-  dim3 grid((unsigned)((N + kWarps * 32 * CPT - 1) / (kWarps * 32 * CPT)), (unsigned)p.splits);
-  gemv_partial_kernel<M, CPT, U><<<grid, kThreads, p.smem, st>>>(x, x_f32, Mr, W_p, W_f, lut, partial, (int)K,
-                                                                 (int)N, p.rows_per_split);
-  return launch_status();
 }
 
-template <int M>
+template <int MB>
 int launch_cpt(const Plan& p, const void* x, int x_f32, int Mr, const uint8_t* W_p, const uint16_t* W_f,
-               const float* lut, float* partial, long long K, long long N, cudaStream_t st) {
-  int splits = 0;
-  int rc;
-  if constexpr (M == 1) {
-    if (p.cpt == 8) {
-      rc = launch_m<M, 8>(p, x, x_f32, Mr, W_p, W_f, lut, partial, K, N, st, &splits);
-      return rc == PACKR_OK ? splits : -rc;
-    }
+               const float* lut, const void* bias, int bias_f32, float* out, long long K, long long N,
+               cudaStream_t st) {
+  if constexpr (MB <= 4) {
+    if (p.cpt == 8) return launch<MB, 8>(p, x, x_f32, Mr, W_p, W_f, lut, bias, bias_f32, out, K, N, st);
   }
-  if constexpr (M >= 12) {
-    rc = launch_m<M, 2>(p, x, x_f32, Mr, W_p, W_f, lut, partial, K, N, st, &splits);
-  } else {
-    rc = launch_m<M, 4>(p, x, x_f32, Mr, W_p, W_f, lut, partial, K, N, st, &splits);
+  if constexpr (MB <= 8) {
+    if (p.cpt == 4) return launch<MB, 4>(p, x, x_f32, Mr, W_p, W_f, lut, bias, bias_f32, out, K, N, st);
   }
-  return rc == PACKR_OK ? splits : -rc;
+  return launch<MB, 2>(p, x, x_f32, Mr, W_p, W_f, lut, bias, bias_f32, out, K, N, st);
 }
 
 int forward(const void* x, int x_f32, const uint8_t* W_p, const uint16_t* W_f, const float* lut, const void* bias,
-            int bias_f32, float* out, long long M, long long K, long long N, float* partial, cudaStream_t st) {
+            int bias_f32, float* out, long long M, long long K, long long N, float* /*unused*/, cudaStream_t st) {
   const Plan p = plan(M, K, N);
   const int Mr = (int)M;
-  int rc;
   switch (p.mb) {
-    case 1: rc = launch_cpt<1>(p, x, x_f32, Mr, W_p, W_f, lut, partial, K, N, st); break;
-    case 2: rc = launch_cpt<2>(p, x, x_f32, Mr, W_p, W_f, lut, partial, K, N, st); break;
-    case 4: rc = launch_cpt<4>(p, x, x_f32, Mr, W_p, W_f, lut, partial, K, N, st); break;
-    case 8: rc = launch_cpt<8>(p, x, x_f32, Mr, W_p, W_f, lut, partial, K, N, st); break;
-    case 12: rc = launch_cpt<12>(p, x, x_f32, Mr, W_p, W_f, lut, partial, K, N, st); break;
-    default: rc = launch_cpt<16>(p, x, x_f32, Mr, W_p, W_f, lut, partial, K, N, st); break;
+    case 1: return launch_cpt<1>(p, x, x_f32, Mr, W_p, W_f, lut, bias, bias_f32, out, K, N, st);
+    case 2: return launch_cpt<2>(p, x, x_f32, Mr, W_p, W_f, lut, bias, bias_f32, out, K, N, st);
+    case 4: return launch_cpt<4>(p, x, x_f32, Mr, W_p, W_f, lut, bias, bias_f32, out, K, N, st);
+    case 8: return launch_cpt<8>(p, x, x_f32, Mr, W_p, W_f, lut, bias, bias_f32, out, K, N, st);
+    default: return launch_cpt<16>(p, x, x_f32, Mr, W_p, W_f, lut, bias, bias_f32, out, K, N, st);
   }
-  if (rc <= 0) return -rc;  // launch_cpt returns the split count, or -status
-  gemv_reduce_kernel<<<dim3((unsigned)((N + 31) / 32), (unsigned)M), 256, 0, st>>>(partial, rc, (int)M, (int)N, bias,
-                                                                                   bias_f32, out, N);
-  return launch_status();
 }
 
 }  // namespace gemv

@@ -120,16 +120,13 @@ extern "C" size_t packr_forward_workspace_bytes(int64_t M, int64_t K, int64_t N,
   const bool pre = predecode_eligible(M, N);
   size_t need = plan_forward(c, p, M, K, N, x_dtype, pre, pre);
   if (M >= 1 && K > 0 && N > 0) {
-    // few rows: the split partial sums of the skinny GEMM (plus its bf16 x)
-    // or of the CUDA-core route
+    // few rows: the split partial sums of the skinny GEMM (plus its bf16 x);
+    // the CUDA-core route needs none
     if (skinny_eligible(M, N)) {
       Carve c2{nullptr};
       FwdPlan p2;
       const size_t g = plan_forward(c2, p2, M, K, N, x_dtype, false) +
                        align_up(gemm::skinny_partial_bytes(M, K, N));
-      if (g > need) need = g;
-    } else if (M <= gemv::kMaxM) {
-      const size_t g = align_up(gemv::workspace_bytes(M, K, N));
       if (g > need) need = g;
     }
   }
@@ -169,10 +166,8 @@ extern "C" int packr_forward(const void* x, int x_dtype, const uint8_t* W_p, con
     }
   }
   // few rows: stream W once through the CUDA cores (fp16-lut decode of the
-  // reference's forward, f32 accumulation), when the workspace holds the
-  // split partial sums
-  if (gemv::eligible(M, K, N, W_p, W_f) && workspace != nullptr && aligned(workspace, kAlign) &&
-      workspace_bytes >= gemv::workspace_bytes(M, K, N)) {
+  // reference's forward, f32 accumulation, one launch, no workspace)
+  if (gemv::eligible(M, K, N, W_p, W_f)) {
     return gemv::forward(x, x_dtype == PACKR_DTYPE_F32, W_p, W_f, lut, bias, bias_dtype == PACKR_DTYPE_F32, out, M,
                          K, N, static_cast<float*>(workspace), s);
   }

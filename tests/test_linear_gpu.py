@@ -198,6 +198,9 @@ CASES = [
     (100, 640, 512, torch.bfloat16, True),     # skinny tcgen05 forward, 128-token MMA width
     (7, 640, 512, torch.bfloat16, False),      # skinny tcgen05 forward, 32-token MMA width
     (4, 512, 1024, torch.bfloat16, True),      # CUDA-core forward, 4 rows
+    (1, 4096, 11008, torch.bfloat16, True),    # CUDA-core forward, clusters of 8 CTAs along K
+    (2, 11008, 4096, torch.float32, True),     # clusters of 16 along K, f32 x
+    (8, 300, 1000, torch.bfloat16, True),      # row bound 8, 4 columns per lane (N % 16 != 0)
     (16, 4096, 11008, torch.bfloat16, True),   # Llama-7B gate/up, decode-bound M
     (16, 11008, 4096, torch.bfloat16, True),   # Llama-7B down
 ]
