@@ -369,6 +369,22 @@ def cpu_decode_port(budget_s: float, M: int):
             "host_cores": os.cpu_count()}
 
 
+def graph_of(fn, warm: int = 2):
+    """fn captured once in a CUDA graph; returns a callable that replays it
+    (the tensors fn writes are the graph's own, reused every replay)."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(warm):
+            fn()
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    torch.cuda.synchronize()
+    return g.replay
+
+
 def bench_decode(args, world, rank, peaks, peak_kind):
     """Decode-bound forward: the three Llama-7B FFN layers at M (default 16)
     tokens, no bias; value = packed-weight bytes (3 per weight) / time."""
@@ -383,23 +399,28 @@ def bench_decode(args, world, rank, peaks, peak_kind):
     wbytes = sum(3.0 * k * n for _, k, n in FFN_LAYERS)
     algo = sum(3.0 * k * n + 2.0 * M * k + 4.0 * M * n for _, k, n in FFN_LAYERS)
 
-    def step():
+    def eager():
         for c in layers:
             K.forward(c["x"], c["W_p"], c["W_f"], c["lut"], None)
+    # A decode loop replays its per-token launches from a CUDA graph (as a
+    # serving loop does): the host's per-call overhead (~20 us of Python and
+    # ctypes) is comparable to a layer's kernel time at these sizes.
+    step = graph_of(eager)
     with ClockSampler(torch.cuda.current_device()) as clk:
         total_ms, per = timed(step, args.steps, args.warmup, world, warm_seconds=1.5)
     ms_step = total_ms / args.steps
     value = world * wbytes / (ms_step * 1e-3) / 1e9
     achieved = algo / (statistics.mean(per) * 1e-3) / 1e9
+    eager_ms, _ = timed(eager, args.steps, args.warmup, world)
     hx = [c["x"].cpu().pin_memory() for c in layers]
     dx = [torch.empty_like(c["x"]) for c in layers]
     hout = [torch.empty(M, n, dtype=torch.float32, pin_memory=True) for _, _, n in FFN_LAYERS]
 
-    def e2e_step():
+    def e2e_eager():
         for i, c in enumerate(layers):
             dx[i].copy_(hx[i], non_blocking=True)
             hout[i].copy_(K.forward(dx[i], c["W_p"], c["W_f"], c["lut"], None), non_blocking=True)
-    e2e_ms, _ = timed(e2e_step, args.steps, max(args.warmup, 1), world)
+    e2e_ms, _ = timed(graph_of(e2e_eager), args.steps, max(args.warmup, 1), world)
     line = {
         "metric": f"PackRLinear decode forward GB/s of packed weights (M={M})", "value": round(value, 1),
         "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -407,16 +428,17 @@ def bench_decode(args, world, rank, peaks, peak_kind):
         "dtype": "bf16 x, f32 decode and accumulate", "data": "synthetic (seeded)",
         "config": {"workload": f"decode: forward of the Llama-7B FFN gate/up/down layers at M={M} tokens",
                    "weight_bytes_per_step": wbytes, "l2": "weights 0.27 GB per step, larger than L2",
-                   "parallelism": f"replicas x{world}"},
+                   "parallelism": f"replicas x{world}", "launch": "CUDA graph of the three packr_forward calls",
+                   "eager_ms_per_step": round(eager_ms / args.steps, 5)},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None,
                      "peak_source": f"{peak_kind} hbm_gbs",
-                     "kernel": "gemv_partial_kernel + gemv_reduce_kernel (three layers)",
+                     "kernel": "gemv_cluster_kernel (M <= 4) or skinny tcgen05 + reduce (three layers)",
                      "algorithmic_bytes_per_launch": algo},
         "e2e": {"value": round(world * wbytes / (e2e_ms / args.steps * 1e-3) / 1e9, 1), "unit": "GB/s",
                 "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in hx),
                 "d2h_bytes_per_step": sum(t.numel() * t.element_size() for t in hout)},
-        "gpu_launches": args.steps * 2 * len(FFN_LAYERS),
+        "gpu_launches": args.steps * (1 if M <= 4 else 2) * len(FFN_LAYERS),
         "clocks": clk.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -118,6 +118,7 @@ __global__ void __launch_bounds__(kThreads, (MB <= 2 ? PACKR_GEMV_MIN_CTAS : 2))
                         const void* __restrict__ bias, int bias_f32, float* __restrict__ out, int K, int N,
                         int rows_per_cta, int rows_per_warp) {
   static_assert(8 * MB * 32 * CPT <= 256 * 32, "warp sums must fit in the lut region");
+  static_assert(kThreads == 256, "one lut entry per thread");
   constexpr int kCols = 32 * CPT;
   extern __shared__ __align__(16) uint32_t gsm[];
   uint32_t* lut_s = gsm;                                   // 256 * 32
@@ -130,8 +131,13 @@ __global__ void __launch_bounds__(kThreads, (MB <= 2 ? PACKR_GEMV_MIN_CTAS : 2))
   const int k0 = rank * rows_per_cta;
   const int k1 = min(K, k0 + rows_per_cta);
   const int nrows_cta = max(0, k1 - k0);
-  for (int e = warp; e < 256; e += kWarps)
-    lut_s[e * 32 + lane] = __float_as_uint(__half2float(__float2half_rn(__ldg(lut + e))));
+  {
+    // thread t loads lut[t] once and writes its 32 lane copies, rotated so
+    // that the warp's stores fall in 32 different banks
+    const uint32_t v = __float_as_uint(__half2float(__float2half_rn(__ldg(lut + threadIdx.x))));
+#pragma unroll 8
+    for (int l = 0; l < 32; ++l) lut_s[threadIdx.x * 32 + ((l + lane) & 31)] = v;
+  }
   for (int i = threadIdx.x; i < nrows_cta * MB; i += kThreads) {
     const int r = i / MB, m = i - r * MB;
     const long long src = (long long)m * K + k0 + r;
@@ -240,10 +246,11 @@ __global__ void __launch_bounds__(kThreads, (MB <= 2 ? PACKR_GEMV_MIN_CTAS : 2))
   }
   cluster_sync_all();  // every CTA's sums are visible to the cluster
   // CTA `rank` finishes columns [rank * kCols / C, (rank + 1) * kCols / C)
-  const int per = kCols / C;
+  const int c_lo = rank * kCols / C;
+  const int per = (rank + 1) * kCols / C - c_lo;
   const uint32_t part_s = sm100::smem_u32(part);
   for (int i = threadIdx.x; i < MB * per; i += kThreads) {
-    const int m = i / per, c = rank * per + (i - m * per);
+    const int m = i / per, c = c_lo + (i - m * per);
     const long long n = (long long)blockIdx.x * kCols + c;
     float t = 0.0f;
     for (int q = 0; q < C; ++q) t = __fadd_rn(t, ld_cluster_f32(sm100::mapa(part_s + 4u * (uint32_t)(m * kCols + c), q)));
@@ -295,31 +302,35 @@ __global__ void __launch_bounds__(256) gemv_reduce_kernel(const float* __restric
 
 inline int row_bound(long long M) { return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : M <= 8 ? 8 : 16; }
 
-// Columns per lane: 8 up to 4 rows (16-byte W_f loads), 4 for 8 rows, 2 for
-// 16 (the accumulators of more rows would cost occupancy).
-inline int cols_per_lane(int mb, long long N) {
-  const int c = mb <= 4 ? 8 : mb <= 8 ? 4 : 2;
-  return (N % c == 0) ? c : (N % 4 == 0 && c > 4 ? 4 : (N % 2 == 0 ? 2 : 0));
-}
-
 struct Plan {
   int mb, cpt, cluster, rows_per_cta, rows_per_warp;
   long long col_blocks;
   size_t smem;
 };
 
-// Cluster size: 8, or 16 when 8 would leave the grid under two CTAs per SM;
-// never more than K / 64 (so a warp gets rows).
+// Columns per lane: 8 up to 4 rows (16-byte W_f loads), 4 for 8 rows, 2 for
+// 16 (more accumulators would cost occupancy); 4 or 2 when N needs it.
+// Cluster size C (CTAs along K, at most 16, at least 64 rows each): measured
+// on B200 over the Llama FFN shapes, the stream runs fastest with about 2.35
+// CTAs per SM for one or two rows (e.g. 43 column blocks x 8 for 4096 ->
+// 11008, 16 x 16 for 11008 -> 4096) and about 1.75 for four (at most 12
+// along K): more CTAs per SM lengthen the start and the reduction more than
+// they add to the stream.
 inline Plan plan(long long M, long long K, long long N) {
   Plan p{};
   p.mb = row_bound(M);
-  p.cpt = cols_per_lane(p.mb, N);
+  const int pref = p.mb <= 4 ? 8 : p.mb <= 8 ? 4 : 2;
+  p.cpt = N % pref == 0 ? pref : (N % 4 == 0 && pref > 4 ? 4 : (N % 2 == 0 ? 2 : 0));
   if (p.cpt == 0) return p;
   p.col_blocks = (N + 32LL * p.cpt - 1) / (32LL * p.cpt);
-  int c = p.col_blocks * 8 >= 2LL * sm_count() ? 8 : 16;
-  while (c > 1 && K < 64LL * c) c >>= 1;
-  p.cluster = c;
-  p.rows_per_cta = (int)((K + c - 1) / c);
+  const double per_sm = p.mb <= 2 ? 2.35 : 1.75;
+  const int cmax = p.mb <= 2 ? 16 : 12;
+  long long c = (long long)(per_sm * sm_count() / (double)p.col_blocks);
+  c = c < 1 ? 1 : (c > cmax ? cmax : c);
+  while (c > 1 && K < 64LL * c) --c;
+  p.cluster = (int)c;
+  if (p.cpt == 0) return p;
+  p.rows_per_cta = (int)((K + p.cluster - 1) / p.cluster);
   p.rows_per_warp = (p.rows_per_cta + kWarps - 1) / kWarps;
   return p;
 }
@@ -371,8 +382,8 @@ int launch(const Plan& p, const void* x, int x_f32, int Mr, const uint8_t* W_p, 
       cudaGetLastError();
       clusters = 0;
     }
-    if (clusters < 1 && q.cluster > 1) {  // a cluster this large does not fit: halve it
-      q.cluster >>= 1;
+    if (clusters < 1 && q.cluster > 1) {  // a cluster this large does not fit: shrink it
+      q.cluster -= 1;
       continue;
     }
     if (cudaLaunchKernelEx(&cfg, kern, x, x_f32, Mr, W_p, W_f, lut, bias, bias_f32, out, (int)K, (int)N,
