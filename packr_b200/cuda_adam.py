@@ -11,7 +11,9 @@ the group with 128-bit vector accesses.
 
 Additions over the reference: `_step_count` is saved in state_dict() (the
 reference keeps it only as an attribute, so bias correction restarted on
-resume), and step() raises if a parameter is not on a CUDA device.
+resume), load_state_dict() keeps the int8 codes and f32 scales of bf16
+parameters in their dtypes (torch's loader casts them to bf16), and step()
+raises if a parameter is not on a CUDA device.
 """
 from __future__ import annotations
 
@@ -139,6 +141,19 @@ class CUDA8BitAdam(torch.optim.Optimizer):
         return sd
 
     def load_state_dict(self, state_dict):
+        """torch's Optimizer.load_state_dict casts every state tensor of a
+        floating-point parameter to the parameter's dtype, which would turn
+        the int8 codes and the f32 block scales of a bf16 parameter into
+        bf16; the 8-bit state is put back with its own dtypes."""
         state_dict = dict(state_dict)
         self._step_count = int(state_dict.pop("packr_step_count", self._step_count))
         super().load_state_dict(state_dict)
+        saved = [i for g in state_dict["param_groups"] for i in g["params"]]
+        params = [p for g in self.param_groups for p in g["params"]]
+        for idx, p in zip(saved, params):
+            st = state_dict["state"].get(idx)
+            if not st:
+                continue
+            for k in ("m", "v", "m_scale", "v_scale"):
+                if k in st:
+                    self.state[p][k] = st[k].detach().to(device=p.device).clone()

@@ -113,6 +113,7 @@ class ShardedAdam8:
                 open_bucket[p.dtype] = b
             b.slots.append(_Slot(p, b.total, p.numel()))
             b.total = _round_up(b.total + p.numel(), BLOCK)
+        self._index = {id(p): i for i, p in enumerate(self.params)}
         self._bucket_of = {}
         for b in self.buckets:
             self._build(b)
@@ -265,6 +266,70 @@ class ShardedAdam8:
         return {"step": self.step_count, "world": self.world, "rank": self.rank,
                 "buckets": [{"dtype": str(b.dtype), "m": b.m, "v": b.v, "m_scale": b.ms, "v_scale": b.vs}
                             for b in self.buckets]}
+
+    # ----------------------------------------------------- consolidated state
+    def _gather(self, t: torch.Tensor) -> torch.Tensor:
+        """All ranks' shards of a bucket buffer, concatenated in rank order."""
+        if self.world == 1:
+            return t
+        parts = [torch.empty_like(t) for _ in range(self.world)]
+        dist.all_gather(parts, t.contiguous(), group=self.pg)
+        return torch.cat(parts)
+
+    @torch.no_grad()
+    def consolidated_state_dict(self) -> dict:
+        """The whole optimizer state in CUDA8BitAdam.state_dict()'s format
+        (per parameter, keyed by its position in the parameter list; m/v int8
+        [numel], m_scale/v_scale f32 [ceil(numel / 256)]), independent of the
+        world size: it loads into CUDA8BitAdam or into a ShardedAdam8 over any
+        number of ranks.  Collective: every rank calls it and gets the whole
+        dict.  A parameter's blocks are its own blocks in the flat buffer
+        (parameters start at multiples of 256), so nothing is re-quantised."""
+        state = {}
+        for b in self.buckets:
+            m, v, ms, vs = (self._gather(t) for t in (b.m, b.v, b.ms, b.vs))
+            for s in b.slots:
+                i = self._index[id(s.param)]
+                b0, nb = s.offset // BLOCK, (s.numel + BLOCK - 1) // BLOCK
+                state[i] = {"m": m[s.offset:s.offset + s.numel].clone(), "v": v[s.offset:s.offset + s.numel].clone(),
+                            "m_scale": ms[b0:b0 + nb].clone(), "v_scale": vs[b0:b0 + nb].clone()}
+        group = {"lr": self.lr, "betas": tuple(self.betas), "eps": self.eps, "weight_decay": self.weight_decay,
+                 "params": list(range(len(self.params)))}
+        return {"state": state, "param_groups": [group], "packr_step_count": self.step_count}
+
+    @torch.no_grad()
+    def load_consolidated_state_dict(self, sd: dict) -> None:
+        """Loads a consolidated_state_dict() (or CUDA8BitAdam.state_dict()
+        over the same parameters in the same order): each rank copies the
+        ranges of its own shard."""
+        state = sd["state"]
+        if len([i for g in sd["param_groups"] for i in g["params"]]) != len(self.params):
+            raise ValueError("ShardedAdam8.load_consolidated_state_dict: different number of parameters")
+        for b in self.buckets:
+            shard = b.total // self.world
+            s0 = self.rank * shard
+            for s in b.slots:
+                st = state.get(self._index[id(s.param)])
+                a, e = max(s.offset, s0), min(s.offset + s.numel, s0 + shard)
+                if a >= e:
+                    continue
+                la, le = a - s0, e - s0
+                ba, be = la // BLOCK, (le + BLOCK - 1) // BLOCK
+                pa, pb = (a - s.offset) // BLOCK, (e - s.offset + BLOCK - 1) // BLOCK
+                if st is None:  # never stepped: the initial state
+                    b.m[la:le] = 0
+                    b.v[la:le] = 0
+                    b.ms[ba:be] = 1.0
+                    b.vs[ba:be] = 1.0
+                    continue
+                if st["m"].numel() != s.numel or st["m_scale"].numel() != (s.numel + BLOCK - 1) // BLOCK:
+                    raise ValueError("ShardedAdam8.load_consolidated_state_dict: state shape mismatch")
+                b.m[la:le].copy_(st["m"][a - s.offset:e - s.offset])
+                b.v[la:le].copy_(st["v"][a - s.offset:e - s.offset])
+                b.ms[ba:be].copy_(st["m_scale"][pa:pb])
+                b.vs[ba:be].copy_(st["v_scale"][pa:pb])
+        self.step_count = int(sd.get("packr_step_count", self.step_count))
+        self.lr = sd["param_groups"][0]["lr"]
 
     def load_state_dict(self, sd: dict) -> None:
         if sd["world"] != self.world or sd["rank"] != self.rank:

@@ -211,3 +211,45 @@ def test_state_layout_is_velvet_readable(cuda):
     opt2 = CUDA8BitAdam([p], lr=1e-3)
     opt2.load_state_dict(sd)
     assert opt2._step_count == 1
+
+
+def test_resume_from_state_dict_is_exact(cuda):
+    """Save after 3 steps (through torch.save), load into a new optimizer over
+    copies of the parameters, 2 more steps: identical to 5 uninterrupted
+    steps, bf16 and f32 parameters (the loader keeps the int8 codes and f32
+    scales of bf16 parameters)."""
+    import io
+    def make():
+        return [torch.nn.Parameter(adam_params(5000, dtype=torch.bfloat16, seed=1, device="cuda")),
+                torch.nn.Parameter(adam_params(777, dtype=torch.float32, seed=2, device="cuda"))]
+    def grads(s):
+        return [adam_grad(5000, s, dtype=torch.bfloat16, device="cuda"), adam_grad(777, s + 50, dtype=torch.float32, device="cuda")]
+    ref = make()
+    ropt = CUDA8BitAdam(ref, lr=1e-3, weight_decay=0.01)
+    run = make()
+    opt = CUDA8BitAdam(run, lr=1e-3, weight_decay=0.01)
+    for s in range(1, 4):
+        for p, g in zip(ref, grads(s)):
+            p.grad = g
+        ropt.step()
+        for p, g in zip(run, grads(s)):
+            p.grad = g
+        opt.step()
+    buf = io.BytesIO()
+    torch.save(opt.state_dict(), buf)
+    buf.seek(0)
+    resumed = [torch.nn.Parameter(p.detach().clone()) for p in run]
+    opt2 = CUDA8BitAdam(resumed, lr=1e-3, weight_decay=0.01)
+    opt2.load_state_dict(torch.load(buf, weights_only=False))
+    assert opt2.state[resumed[0]]["m"].dtype == torch.int8
+    assert opt2.state[resumed[0]]["m_scale"].dtype == torch.float32
+    for s in range(4, 6):
+        for p, g in zip(ref, grads(s)):
+            p.grad = g
+        ropt.step()
+        for p, g in zip(resumed, grads(s)):
+            p.grad = g
+        opt2.step()
+    torch.cuda.synchronize()
+    for a, b in zip(ref, resumed):
+        assert torch.equal(a.detach(), b.detach())

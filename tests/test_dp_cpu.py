@@ -153,3 +153,130 @@ def test_single_process_layout_and_views():
     opt.step()
     assert opt.step_count == 1
     assert all(not torch.equal(p.detach(), b) for p, b in zip(params, before))
+
+
+# ------------------------------------------------------------- checkpoints
+def expected_with_state(worlds):
+    """Single process: step s averages the gradients of worlds[s-1] ranks.
+    Returns (params, [(m, v, ms, vs)] per parameter) as numpy."""
+    params = [p.detach().clone() for p in make_params()]
+    state = [(np.zeros(p.numel(), np.int8), np.zeros(p.numel(), np.int8),
+              np.ones((p.numel() + 255) // 256, np.float32), np.ones((p.numel() + 255) // 256, np.float32))
+             for p in params]
+    for s, world in enumerate(worlds, start=1):
+        grads = [make_grads(r, s) for r in range(world)]
+        bc1, bc2 = oracle.adam8_bias_corrections(0.9, 0.999, s)
+        for i, p in enumerate(params):
+            avg = (sum(grads[r][i].double() for r in range(world)) / world).to(p.dtype)
+            m, v, ms, vs = state[i]
+            oracle.adam8_step(_np(p), _np(avg.contiguous()).copy(), m, v, ms, vs, 1e-3, 0.9, 0.999, 1e-8, bc1, bc2,
+                              0.01)
+    return [_np(p).copy() for p in params], state
+
+
+def _to_np(sd):
+    return {**sd, "state": {i: {k: v.numpy().copy() for k, v in st.items()} for i, st in sd["state"].items()}}
+
+
+def _from_np(sd):
+    return {**sd, "state": {i: {k: torch.from_numpy(v.copy()) for k, v in st.items()} for i, st in sd["state"].items()}}
+
+
+def _ckpt_worker(rank, world, port, first_step, last_step, init, q):
+    """Steps first_step..last_step on `world` ranks; with `init` = (param
+    values, consolidated state) it starts from a checkpoint."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        params = make_params()
+        if init is not None:
+            with torch.no_grad():
+                for p, v in zip(params, init[0]):
+                    p.copy_(v)
+        opt = ShardedAdam8(params, lr=1e-3, weight_decay=0.01, adam_fn=oracle_adam_fn, bucket_bytes=700)
+        if init is not None:
+            opt.load_consolidated_state_dict(_from_np(init[1]))
+        for s in range(first_step, last_step + 1):
+            for p, gr in zip(params, make_grads(rank, s)):
+                p.grad = gr
+            opt.step()
+        sd = opt.consolidated_state_dict()
+        # numpy through the queue: torch tensors would travel as shared-memory
+        # handles that vanish with this process
+        q.put((rank, [_np(p.detach()).copy() for p in params], _to_np(sd)))
+    finally:
+        dist.destroy_process_group()
+
+
+def _run(world, first, last, init):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ckpt_worker, args=(r, world, port, first, last, init, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = {}
+    for _ in range(world):
+        r, ps, sd = q.get(timeout=120)
+        out[r] = (ps, _from_np(sd))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    return out
+
+
+def test_consolidated_checkpoint_resumes_at_another_world_size():
+    """2 ranks for steps 1-2, a world-size independent checkpoint, then 3
+    ranks for step 3: state and parameters equal the single process with the
+    same averaged gradients, bit for bit."""
+    first = _run(2, 1, 2, None)
+    params2, sd2 = first[0]
+    want_p, want_s = expected_with_state([2, 2])
+    for i, (m, v, ms, vs) in enumerate(want_s):
+        st = sd2["state"][i]
+        assert st["m"].dtype == torch.int8 and st["m_scale"].dtype == torch.float32
+        assert np.array_equal(st["m"].numpy(), m) and np.array_equal(st["v"].numpy(), v), i
+        assert np.array_equal(st["m_scale"].numpy(), ms) and np.array_equal(st["v_scale"].numpy(), vs), i
+    assert sd2["packr_step_count"] == 2
+    for r in first:  # every rank gets the whole dict
+        assert all(torch.equal(first[r][1]["state"][i]["m"], sd2["state"][i]["m"]) for i in sd2["state"])
+    vals = [torch.from_numpy(a.view(np.int16)).view(torch.bfloat16) if a.dtype == np.uint16 else torch.from_numpy(a)
+            for a in params2]
+    second = _run(3, 3, 3, (vals, _to_np(sd2)))
+    want_p, want_s = expected_with_state([2, 2, 3])
+    for r in second:
+        for got, exp in zip(second[r][0], want_p):
+            assert np.array_equal(got, exp)
+    for i, (m, v, ms, vs) in enumerate(want_s):
+        st = second[0][1]["state"][i]
+        assert np.array_equal(st["m"].numpy(), m) and np.array_equal(st["v_scale"].numpy(), vs), i
+
+
+def test_cuda8bit_adam_loads_consolidated_state():
+    """The consolidated format is CUDA8BitAdam's: its loader keeps int8 codes
+    and f32 scales for bf16 parameters (torch's own loader casts them)."""
+    from packr_b200.cuda_adam import CUDA8BitAdam
+    params = make_params()
+    opt = ShardedAdam8(params, lr=1e-3, weight_decay=0.01, adam_fn=oracle_adam_fn)
+    for s in (1, 2):
+        for p, gr in zip(params, make_grads(0, s)):
+            p.grad = gr
+        opt.step()
+    sd = opt.consolidated_state_dict()
+    fresh = make_params()
+    single = CUDA8BitAdam(fresh, lr=1e-3, weight_decay=0.01)
+    single.load_state_dict(sd)
+    assert single._step_count == 2
+    for i, p in enumerate(fresh):
+        st = single.state[p]
+        assert st["m"].dtype == torch.int8 and st["v"].dtype == torch.int8
+        assert st["m_scale"].dtype == torch.float32 and st["v_scale"].dtype == torch.float32
+        assert torch.equal(st["m"], sd["state"][i]["m"]) and torch.equal(st["v_scale"], sd["state"][i]["v_scale"])
+    again = single.state_dict()
+    back = ShardedAdam8(make_params(), lr=1e-3, weight_decay=0.01, adam_fn=oracle_adam_fn)
+    back.load_consolidated_state_dict(again)
+    re = back.consolidated_state_dict()
+    for i in sd["state"]:
+        for k in ("m", "v", "m_scale", "v_scale"):
+            assert torch.equal(re["state"][i][k], sd["state"][i][k]), (i, k)
