@@ -283,8 +283,8 @@ def bench_adam8(args, world, rank, peaks, peak_kind):
                    "l2": "inputs larger than L2 (1.1 GB per step)", "parallelism": f"replicas x{world}"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / peaks["hbm_gbs"], 4),
-                     "traffic": load_traffic("adam8_multi_kernel", "adam8_110M"),
-                     "peak_source": f"{peak_kind} hbm_gbs", "kernel": "adam8_multi_kernel",
+                     "traffic": load_traffic("adam8_kernel", "adam8_110M"),
+                     "peak_source": f"{peak_kind} hbm_gbs", "kernel": "adam8_kernel<bf16>",
                      "algorithmic_bytes_per_launch": n * ADAM_BYTES_PER_PARAM},
         "e2e": {"value": round(e2e_val, 3), "unit": "Gparam/s", "h2d_bytes_per_step": 2 * n,
                 "d2h_bytes_per_step": 2 * n},
