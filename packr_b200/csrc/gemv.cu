@@ -111,9 +111,6 @@ __host__ __device__ constexpr size_t cluster_smem(int rows_per_cta) {
 #ifndef PACKR_GEMV_MIN_CTAS
 #define PACKR_GEMV_MIN_CTAS 3
 #endif
-#ifndef PACKR_GEMV_GROUPS_AHEAD
-#define PACKR_GEMV_GROUPS_AHEAD 1
-#endif
 template <int MB, int CPT, int U>
 __global__ void __launch_bounds__(kThreads, (MB <= 2 ? PACKR_GEMV_MIN_CTAS : 2))
     gemv_cluster_kernel(const void* __restrict__ x, int x_f32, int Mr, const uint8_t* __restrict__ W_p,
@@ -200,32 +197,6 @@ __global__ void __launch_bounds__(kThreads, (MB <= 2 ? PACKR_GEMV_MIN_CTAS : 2))
       for (int u = 0; u < U; ++u) consume(w[u], r + u);
     };
     int r = r0;
-#if PACKR_GEMV_GROUPS_AHEAD == 2
-    // three buffers in rotation: two groups in flight while one is consumed
-    WVec<CPT> a[U], b[U], c[U];
-    int g = 0;
-    if (full > 0) load(a);
-    if (full > 1) load(b);
-    for (; g + 3 <= full; g += 3) {
-      load(c);
-      eat(a, r);
-      r += U;
-      if (g + 3 < full) load(a);
-      eat(b, r);
-      r += U;
-      if (g + 4 < full) load(b);
-      eat(c, r);
-      r += U;
-    }
-    if (full - g >= 1) {
-      eat(a, r);
-      r += U;
-    }
-    if (full - g >= 2) {
-      eat(b, r);
-      r += U;
-    }
-#else
     WVec<CPT> a[U], b[U];
     if (full > 0) {
       load(a);
@@ -249,7 +220,6 @@ __global__ void __launch_bounds__(kThreads, (MB <= 2 ? PACKR_GEMV_MIN_CTAS : 2))
         r += U;
       }
     }
-#endif
     for (; r < r1; ++r) {  // the last rows, one at a time
       WVec<CPT> t;
       t.load(pf, pp);
