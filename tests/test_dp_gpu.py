@@ -92,6 +92,21 @@ def _worker(rank, world, port, q):
         gathered = [torch.empty_like(flat) for _ in range(world)]
         dist.all_gather(gathered, flat)
         same = all(torch.equal(gathered[0], g) for g in gathered)
+        # VelvetController's v means over the sharded state: one all-reduce,
+        # the same on every rank, and a controller step sets the same lr
+        from packr_b200 import VelvetController
+        means = dopt.v_means()
+        mv = torch.tensor([means[id(p)] for p in mp_], dtype=torch.float64, device=dev)
+        mg = [torch.empty_like(mv) for _ in range(world)]
+        dist.all_gather(mg, mv)
+        same = same and all(torch.equal(mg[0], m) for m in mg) and bool(torch.isfinite(mv).all()) and bool((mv > 0).all())
+        ctl = VelvetController(dopt, total_opt_steps=100)
+        ctl.step()
+        ctl.step()
+        lr = torch.tensor([dopt.lr], dtype=torch.float64, device=dev)
+        lg = [torch.empty_like(lr) for _ in range(world)]
+        dist.all_gather(lg, lr)
+        same = same and all(torch.equal(lg[0], x) for x in lg)
         q.put((rank, exact, same, (flat - p0).cpu().numpy(), first_grad.cpu().numpy()))
     finally:
         dist.destroy_process_group()
