@@ -18,6 +18,7 @@ from .config import PackRConfig, SchemeType
 from .optim import FusedQuantizedAdam
 from .cuda_adam import CUDA8BitAdam
 from .velvet import VelvetController
+from .offload import OffloadManager
 
 # Legacy aliases (reference packr/__init__.py:29-34)
 PHRConfig = PackRConfig
@@ -27,6 +28,6 @@ phr_matmul = packr_matmul
 
 __all__ = [
     "PackRConfig", "PackRLinear", "PackRMatmulFunction", "PackRLinearFunction", "packr_matmul", "compress_model",
-    "SchemeType", "FusedQuantizedAdam", "CUDA8BitAdam", "VelvetController",
+    "SchemeType", "FusedQuantizedAdam", "CUDA8BitAdam", "VelvetController", "OffloadManager",
     "PHRConfig", "PHRLinear", "PHRMatmulFunction", "phr_matmul",
 ]

@@ -81,8 +81,17 @@ def test_compress_model_scopes():
 
 def test_api_surface_matches_reference():
     for name in ["PackRConfig", "PackRLinear", "PackRMatmulFunction", "packr_matmul", "compress_model", "SchemeType",
-                 "FusedQuantizedAdam", "PHRConfig", "PHRLinear", "PHRMatmulFunction", "phr_matmul"]:
+                 "FusedQuantizedAdam", "OffloadManager", "VelvetController", "PHRConfig", "PHRLinear",
+                 "PHRMatmulFunction", "phr_matmul"]:
         assert hasattr(packr, name), name
+    with pytest.warns(RuntimeWarning):
+        mgr = packr.OffloadManager(prefetch_depth=2)
+    layer = PackRLinear(8, 4)
+    mgr.register_wp("l0", layer.W_p)
+    mgr.set_layer_sequence(["l0"])
+    layer.attach_offload(mgr, "l0")
+    mgr.prefetch_wp("l0"); mgr.ensure_wp("l0"); mgr.evict_wp("l0"); mgr.make_evict_cb("l0")()
+    assert mgr.num_chunks == 0
     from packr_b200.cuda_adam import CUDA8BitAdam  # noqa: F401
     cfg = PackRConfig()
     assert (cfg.mode, cfg.layer_scope, cfg.block_size, cfg.optimizer_type) == ("packr", "ffn", 256, "triton8")
