@@ -159,6 +159,25 @@ int packr_decode_bf16(const uint8_t* W_p, const uint16_t* W_f, const float* lut,
 int packr_predecode_bf16(const uint8_t* W_p, const uint16_t* W_f, const float* lut, uint16_t* out, int64_t K,
                          int64_t N, void* stream);
 
+/* Backward with the caller's decoded W (Wd [K, N] bf16, 16-byte aligned,
+ * equal to packr_predecode_bf16(W_p, W_f, lut)): where packr_backward would
+ * predecode W for the plain dX GEMM (M >= 1024, N % 16 == 0, 16-byte aligned
+ * W_p / W_f) it uses Wd instead; otherwise Wd is ignored.  A forward that
+ * predecodes (packr_predecode_bf16 + packr_forward_decoded, which is what
+ * packr_forward runs on the same route) can keep its W for the backward and
+ * save one decode pass.  Same results as packr_backward; workspace from
+ * packr_backward_decoded_workspace_bytes (no decoded-W buffer in it).  No
+ * counterpart in the reference (it decodes in both passes,
+ * packr/kernel.py:127-130 and packr/autograd.py:66-67). */
+size_t packr_backward_decoded_workspace_bytes(int64_t M, int64_t K, int64_t N, int x_dtype, int flags);
+int packr_backward_decoded(const float* dY, const void* x, int x_dtype, const uint8_t* W_p, const uint16_t* W_f,
+                           const float* lut, const uint16_t* Wd, const int32_t* lut_counts, void* dX,
+                           uint16_t* dW_f, float* dlut, uint16_t* dbias, int64_t M, int64_t K, int64_t N,
+                           int flags, void* workspace, size_t workspace_bytes, void* stream);
+/* 1 when packr_forward takes its predecode route for this problem (given a
+ * workspace of packr_forward_workspace_bytes), else 0. */
+int packr_predecode_route(int64_t M, int64_t K, int64_t N, const uint8_t* W_p, const uint16_t* W_f);
+
 /* ---- PackRLinear.from_linear (reference packr/layer.py:106-159) ----------
  * Step 1: the rank_lo-th and rank_hi-th smallest |w| (0-based; rank_hi is
  * rank_lo or rank_lo + 1) of n weights (f32 or bf16), as f32, written to

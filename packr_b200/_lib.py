@@ -59,6 +59,10 @@ SIGNATURES = {
     "packr_decode_bf16": (_I32, [_VP, _VP, _VP, _VP, _I64, _I64, _VP]),
     "packr_predecode_bf16": (_I32, [_VP, _VP, _VP, _VP, _I64, _I64, _VP]),
     "packr_selfcheck_rounding": (_I32, [_VP, _VP]),
+    "packr_backward_decoded_workspace_bytes": (_SZ, [_I64, _I64, _I64, _I32, _I32]),
+    "packr_backward_decoded": (_I32, [_VP, _VP, _I32, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _I64, _I64,
+                                      _I64, _I32, _VP, _SZ, _VP]),
+    "packr_predecode_route": (_I32, [_I64, _I64, _I64, _VP, _VP]),
     "packr_abs_order_stats_workspace_bytes": (_SZ, []),
     "packr_abs_order_stats": (_I32, [_VP, _I32, _I64, _I64, _I64, _VP, _VP, _SZ, _VP]),
     "packr_from_linear_encode": (_I32, [_VP, _I32, _I64, _I64, _VP, _VP, _VP, _VP, _VP, _VP, _VP]),

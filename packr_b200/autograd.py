@@ -17,9 +17,16 @@ ignored; evict_cb still fires at the end of backward.
 """
 from __future__ import annotations
 
+import os
+
 import torch
 
 from . import kernel as _k
+
+# PACKR_KEEP_DECODED_W=0 trades the second decode of W back for its memory
+# (the decoded W, 2 bytes per weight, is otherwise held from forward to
+# backward on the many-row route).
+KEEP_DECODED_W = os.environ.get("PACKR_KEEP_DECODED_W", "1") != "0"
 
 
 def grad_sink(param: torch.Tensor) -> torch.Tensor | None:
@@ -41,6 +48,21 @@ def grad_sink(param: torch.Tensor) -> torch.Tensor | None:
     return buf[off:off + n].view(param.shape)
 
 
+def _forward_keep_w(ctx, x, W_p, W_f, lut, bias):
+    """The forward; on the route where it decodes all of W first (many rows)
+    and dX will be needed, the decoded W is kept on ctx for the backward's
+    dX GEMM (2 bytes per weight held until the backward), so W is decoded
+    once per step instead of twice."""
+    ctx.wd = None
+    x2 = x.reshape(-1, x.shape[-1]) if x.dim() != 2 else x
+    M, K = x2.shape
+    N = W_p.shape[1]
+    if KEEP_DECODED_W and ctx.needs_input_grad[0] and _k.predecode_route(M, K, N, W_p, W_f):
+        ctx.wd = _k.predecode_bf16(W_p, W_f, lut)
+        return _k.forward_decoded(x, ctx.wd, bias)
+    return _k.forward(x, W_p, W_f, lut, bias)
+
+
 class PackRLinearFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, W_p, W_f, lut, bias=None, counts=None, evict_cb=None):
@@ -50,7 +72,7 @@ class PackRLinearFunction(torch.autograd.Function):
         ctx.has_bias = bias is not None
         ctx.evict_cb = evict_cb
         ctx.wf_param = W_f
-        return _k.forward(x, W_p, W_f, lut, bias)
+        return _forward_keep_w(ctx, x, W_p, W_f, lut, bias)
 
     @staticmethod
     def backward(ctx, grad_out):
@@ -58,7 +80,9 @@ class PackRLinearFunction(torch.autograd.Function):
         nx, _, nwf, nlut, nb = ctx.needs_input_grad[:5]
         dX, dW, dlut, dbias = _k.backward(grad_out, x, W_p, W_f, lut, counts, need_dx=nx, need_dw=nwf,
                                           need_dlut=nlut, need_dbias=ctx.has_bias and nb,
-                                          dW_out=grad_sink(ctx.wf_param) if nwf else None)
+                                          dW_out=grad_sink(ctx.wf_param) if nwf else None,
+                                          Wd=ctx.wd if nx else None)
+        ctx.wd = None
         if ctx.evict_cb is not None:
             ctx.evict_cb()
         if dX is not None and dX.dtype != x.dtype:

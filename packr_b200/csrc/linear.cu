@@ -76,9 +76,9 @@ struct BwdPlan {
 
 size_t plan_backward(Carve& c, BwdPlan& p, long long M, long long K, long long N, int x_dtype, int flags,
                      bool want_dx, bool want_dw, bool want_dlut, bool want_dbias, bool have_counts, bool pre,
-                     bool sk = false) {
+                     bool sk = false, bool wd_given = false) {
   const bool split = (flags & PACKR_BWD_DW_SPLIT) != 0 && (want_dw || want_dlut);
-  p.wd = pre && want_dx ? c.take<uint16_t>((size_t)K * N) : nullptr;
+  p.wd = pre && want_dx && !wd_given ? c.take<uint16_t>((size_t)K * N) : nullptr;
   const bool use_sk = sk && ((pre && want_dx) || want_dw || want_dlut);
   const int msub = pre && want_dx ? plain_msub(M) : 1;
   p.skp = use_sk ? c.take<float>(gemm::sk_partial_bytes(sk_pairs(), msub) / sizeof(float)) : nullptr;
@@ -284,10 +284,15 @@ extern "C" size_t packr_backward_workspace_bytes(int64_t M, int64_t K, int64_t N
   return plan_backward(c, p, M, K, N, x_dtype, flags, true, true, true, true, false, predecode_eligible(M, N), true);
 }
 
-extern "C" int packr_backward(const float* dY, const void* x, int x_dtype, const uint8_t* W_p, const uint16_t* W_f,
-                              const float* lut, const int32_t* lut_counts, void* dX, uint16_t* dW_f, float* dlut,
-                              uint16_t* dbias, int64_t M, int64_t K, int64_t N, int flags, void* workspace,
-                              size_t workspace_bytes, void* stream) {
+namespace packr {
+namespace linear {
+// The backward launch sequence; wd_given (nullable) is W decoded by the
+// caller exactly as packr_predecode_bf16 decodes it, used instead of a
+// predecode of its own by the plain dX GEMM.
+static int backward_impl(const float* dY, const void* x, int x_dtype, const uint8_t* W_p, const uint16_t* W_f,
+                         const float* lut, const uint16_t* wd_given, const int32_t* lut_counts, void* dX,
+                         uint16_t* dW_f, float* dlut, uint16_t* dbias, int64_t M, int64_t K, int64_t N, int flags,
+                         void* workspace, size_t workspace_bytes, void* stream) {
   int st = check_common(x, x_dtype, W_p, W_f, lut, M, K, N);
   if (st != PACKR_OK) return st;
   if (M > 0 && dY == nullptr) return PACKR_ERR_INVALID_ARGUMENT;
@@ -317,7 +322,7 @@ extern "C" int packr_backward(const float* dY, const void* x, int x_dtype, const
     if (t[0] && !pre_ok) continue;
     c = Carve{static_cast<uint8_t*>(workspace)};
     need = plan_backward(c, p, M, K, N, x_dtype, flags, want_dx, want_dw, want_dlut, want_dbias,
-                         lut_counts != nullptr, t[0], t[1]);
+                         lut_counts != nullptr, t[0], t[1], wd_given != nullptr);
     pre = t[0];
     if (workspace_bytes >= need) break;
   }
@@ -349,8 +354,12 @@ extern "C" int packr_backward(const float* dY, const void* x, int x_dtype, const
     P.sk_flags = p.skf;
     P.sk_slots = p.skp != nullptr ? sk_pairs() : 0;
     if (pre) {
-      if ((st = gemm::predecode(W_p, W_f, lut, p.wd, K, N, s)) != PACKR_OK) return st;
-      if ((st = gemm::make_map(&maps.b[0], p.wd, N, K, N * 2, gemm::BN_CTA)) != PACKR_OK) return st;
+      const uint16_t* wd = wd_given;
+      if (wd == nullptr) {
+        if ((st = gemm::predecode(W_p, W_f, lut, p.wd, K, N, s)) != PACKR_OK) return st;
+        wd = p.wd;
+      }
+      if ((st = gemm::make_map(&maps.b[0], wd, N, K, N * 2, gemm::BN_CTA)) != PACKR_OK) return st;
       st = gemm::launch_plain<gemm::DX>(P, maps, s);
     } else {
       st = gemm::launch<gemm::DX>(P, maps, s);
@@ -400,6 +409,42 @@ extern "C" int packr_backward(const float* dY, const void* x, int x_dtype, const
     counts = p.counts;
   }
   return prep::finalize(dlut, p.dlut_sum, counts, dbias, p.colsum, N, s);
+}
+}  // namespace linear
+}  // namespace packr
+
+extern "C" int packr_backward(const float* dY, const void* x, int x_dtype, const uint8_t* W_p, const uint16_t* W_f,
+                              const float* lut, const int32_t* lut_counts, void* dX, uint16_t* dW_f, float* dlut,
+                              uint16_t* dbias, int64_t M, int64_t K, int64_t N, int flags, void* workspace,
+                              size_t workspace_bytes, void* stream) {
+  return backward_impl(dY, x, x_dtype, W_p, W_f, lut, nullptr, lut_counts, dX, dW_f, dlut, dbias, M, K, N, flags,
+                       workspace, workspace_bytes, stream);
+}
+
+extern "C" size_t packr_backward_decoded_workspace_bytes(int64_t M, int64_t K, int64_t N, int x_dtype, int flags) {
+  Carve c{nullptr};
+  BwdPlan p;
+  M = M > 0 ? M : 0;
+  K = K > 0 ? K : 0;
+  N = N > 0 ? N : 0;
+  return plan_backward(c, p, M, K, N, x_dtype, flags, true, true, true, true, false, predecode_eligible(M, N), true,
+                       true);
+}
+
+extern "C" int packr_backward_decoded(const float* dY, const void* x, int x_dtype, const uint8_t* W_p,
+                                      const uint16_t* W_f, const float* lut, const uint16_t* Wd,
+                                      const int32_t* lut_counts, void* dX, uint16_t* dW_f, float* dlut,
+                                      uint16_t* dbias, int64_t M, int64_t K, int64_t N, int flags, void* workspace,
+                                      size_t workspace_bytes, void* stream) {
+  if (Wd == nullptr) return PACKR_ERR_INVALID_ARGUMENT;
+  if (!aligned(Wd, 16)) return PACKR_ERR_ALIGNMENT;
+  return backward_impl(dY, x, x_dtype, W_p, W_f, lut, Wd, lut_counts, dX, dW_f, dlut, dbias, M, K, N, flags,
+                       workspace, workspace_bytes, stream);
+}
+
+extern "C" int packr_predecode_route(int64_t M, int64_t K, int64_t N, const uint8_t* W_p, const uint16_t* W_f) {
+  (void)K;
+  return predecode_eligible(M, N) && gemm::wtma_ok(W_p, W_f, N) ? 1 : 0;
 }
 
 extern "C" int packr_bincount256(const uint8_t* W_p, int64_t n, int32_t* counts, void* stream) {

@@ -151,12 +151,20 @@ def dw_split_for(x_dtype: torch.dtype) -> bool:
     return x_dtype == torch.float32
 
 
+def predecode_route(M: int, K: int, N: int, W_p: torch.Tensor, W_f: torch.Tensor) -> bool:
+    """True when packr_forward decodes all of W first (then a plain GEMM) for
+    this problem: the forward can keep that W for the backward."""
+    return bool(_lib.load().packr_predecode_route(M, K, N, _ptr(W_p), _ptr(W_f)))
+
+
 def backward(dY: torch.Tensor, x: torch.Tensor, W_p: torch.Tensor, W_f: torch.Tensor, lut: torch.Tensor,
              counts: torch.Tensor | None, need_dx: bool, need_dw: bool, need_dlut: bool, need_dbias: bool,
-             dW_out: torch.Tensor | None = None):
+             dW_out: torch.Tensor | None = None, Wd: torch.Tensor | None = None):
     """Returns (dX, dW_f, dlut, dbias); entries not requested are None.
     dW_out: optional contiguous bf16 [K, N] tensor the dW_f result is written
-    into (for example a view of an optimizer's flat gradient buffer)."""
+    into (for example a view of an optimizer's flat gradient buffer).
+    Wd: optional W decoded by predecode_bf16 (kept from the forward); the dX
+    GEMM uses it instead of decoding W again."""
     lib = _lib.load()
     x = _as_operand(x)
     M, K = x.shape
@@ -178,6 +186,16 @@ def backward(dY: torch.Tensor, x: torch.Tensor, W_p: torch.Tensor, W_f: torch.Te
     xd = _dtype_code(x)
     flags = _lib.PACKR_BWD_DW_SPLIT if dw_split_for(x.dtype) else 0
     with torch.cuda.device(dev):
+        if Wd is not None:
+            if Wd.dtype != torch.bfloat16 or tuple(Wd.shape) != (K, N) or not Wd.is_contiguous():
+                raise ValueError("Wd must be the contiguous bf16 [K, N] decoded W")
+            ws = _workspace(lib.packr_backward_decoded_workspace_bytes(M, K, N, xd, flags), dev)
+            code = lib.packr_backward_decoded(_ptr(dY), _ptr(x), xd, _ptr(W_p), _ptr(W_f.contiguous()),
+                                              _ptr(lut.detach().float().contiguous()), _ptr(Wd), _ptr(counts),
+                                              _ptr(dX), _ptr(dW), _ptr(dlut), _ptr(dbias), M, K, N, flags, _ptr(ws),
+                                              0 if ws is None else ws.numel(), _stream(dev))
+            _lib.check("packr_backward_decoded", code)
+            return dX, dW, dlut, dbias
         ws = _workspace(lib.packr_backward_workspace_bytes(M, K, N, xd, flags), dev)
         code = lib.packr_backward(_ptr(dY), _ptr(x), xd, _ptr(W_p), _ptr(W_f.contiguous()),
                                   _ptr(lut.detach().float().contiguous()), _ptr(counts), _ptr(dX), _ptr(dW),

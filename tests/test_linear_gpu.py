@@ -264,3 +264,43 @@ def test_empty_batch(cuda):
     dX, dW, dlut, dbias = K.backward(c["dY"][:0], x, c["W_p"], c["W_f"], c["lut"], None, True, True, True, True)
     torch.cuda.synchronize()
     assert dX.shape == (0, 64) and (dW.float() == 0).all() and (dlut == 0).all() and (dbias.float() == 0).all()
+
+
+@pytest.mark.parametrize("M,Kd,Nd,dt", [(1024, 768, 3072, torch.bfloat16), (1500, 320, 528, torch.float32),
+                                        (4096, 256, 512, torch.bfloat16)])
+def test_backward_with_forward_decoded_w(cuda, M, Kd, Nd, dt):
+    """packr_backward_decoded with the forward's decoded W gives the same
+    gradients as packr_backward decoding W itself (dlut and dbias: the same
+    sums added by atomics in a run-dependent order)."""
+    c = to_cuda(linear_case(M, Kd, Nd, x_dtype=dt, bias=True, seed=M + 3))
+    assert K.predecode_route(M, Kd, Nd, c["W_p"], c["W_f"])
+    Wd = K.predecode_bf16(c["W_p"], c["W_f"], c["lut"])
+    counts = K.bincount256(c["W_p"])
+    a = K.backward(c["dY"], c["x"], c["W_p"], c["W_f"], c["lut"], counts, True, True, True, True)
+    b = K.backward(c["dY"], c["x"], c["W_p"], c["W_f"], c["lut"], counts, True, True, True, True, Wd=Wd)
+    torch.cuda.synchronize()
+    assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
+    assert torch.allclose(a[2], b[2], rtol=1e-5, atol=1e-6 * a[2].abs().max().item())
+    assert torch.allclose(a[3].float(), b[3].float(), rtol=2 ** -7, atol=0)
+
+
+def test_layer_keeps_decoded_w_for_backward(cuda):
+    """PackRLinear on the many-row route decodes W once per step: forward and
+    gradients equal the explicit forward + backward."""
+    from packr_b200 import PackRLinear
+    M, Kd, Nd = 1024, 512, 1024
+    c = to_cuda(linear_case(M, Kd, Nd, x_dtype=torch.bfloat16, bias=True, seed=21))
+    layer = PackRLinear(Kd, Nd).to("cuda")
+    with torch.no_grad():
+        layer.W_p.copy_(c["W_p"]); layer.W_f.copy_(c["W_f"]); layer.lut.copy_(c["lut"]); layer.bias_f.copy_(c["bias"])
+    x = c["x"].clone().requires_grad_(True)
+    out = layer(x)
+    out.backward(c["dY"])
+    ref_out = K.forward(c["x"], c["W_p"], c["W_f"], c["lut"], c["bias"])
+    dX, dW, dlut, dbias = K.backward(c["dY"], c["x"], c["W_p"], c["W_f"], c["lut"], K.bincount256(c["W_p"]),
+                                     True, True, True, True)
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref_out)
+    assert torch.equal(x.grad, dX) and torch.equal(layer.W_f.grad, dW)
+    assert torch.allclose(layer.bias_f.grad.float(), dbias.float(), rtol=2 ** -7, atol=0)
+    assert torch.allclose(layer.lut.grad, dlut, rtol=1e-5, atol=1e-6 * dlut.abs().max().item())
