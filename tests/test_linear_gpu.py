@@ -190,6 +190,8 @@ CASES = [
     (1100, 192, 264, torch.float32, True),     # large M but N % 16 != 0: fused register-ring route
     (1024, 2048, 9728, torch.bfloat16, True),  # stream-K split of 76 FWD tiles over 74 pairs
     (512, 1024, 5120, torch.float32, True),    # f32 x: 3 dW reduction segments
+    (128, 2560, 2048, torch.bfloat16, False),  # dW: 80 tiles on 74 pairs (a second, partial wave)
+    (96, 2304, 2112, torch.float32, True),     # dW: 81 tiles, the last column tile ragged (64 valid columns)
     (4096, 2560, 512, torch.bfloat16, False),  # stream-K split of 80 DX tiles over 74 pairs
     (3, 200, 264, torch.float32, True),        # few-row CUDA-core forward, row bound 4
     (9, 512, 1000, torch.bfloat16, False),     # row bound 12, 4 columns per thread
