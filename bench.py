@@ -818,6 +818,9 @@ def bench_from_linear(args, world, rank, peaks, peak_kind):
 def reference_arm(args, world, rank):
     if rank != 0:
         return None
+    # torchrun sets OMP_NUM_THREADS=1 in every rank; this arm runs in rank 0
+    # alone and may use every host thread the process is allowed
+    torch.set_num_threads(len(os.sched_getaffinity(0)))
     if args.workload == "adam8":
         cb = cpu_adam_reference(1 << 24, max(2.0, 0.5 * args.steps))
         return {"impl": "reference", "metric": "8-bit AdamW Gparam/s", "value": round(cb["value"], 5),
