@@ -25,9 +25,10 @@ PHRConfig = PackRConfig
 PHRLinear = PackRLinear
 PHRMatmulFunction = PackRMatmulFunction
 phr_matmul = packr_matmul
+CV2LRTController = VelvetController
 
 __all__ = [
     "PackRConfig", "PackRLinear", "PackRMatmulFunction", "PackRLinearFunction", "packr_matmul", "compress_model",
     "SchemeType", "FusedQuantizedAdam", "CUDA8BitAdam", "VelvetController", "OffloadManager",
-    "PHRConfig", "PHRLinear", "PHRMatmulFunction", "phr_matmul",
+    "PHRConfig", "PHRLinear", "PHRMatmulFunction", "phr_matmul", "CV2LRTController",
 ]

@@ -82,8 +82,10 @@ def test_compress_model_scopes():
 def test_api_surface_matches_reference():
     for name in ["PackRConfig", "PackRLinear", "PackRMatmulFunction", "packr_matmul", "compress_model", "SchemeType",
                  "FusedQuantizedAdam", "OffloadManager", "VelvetController", "PHRConfig", "PHRLinear",
-                 "PHRMatmulFunction", "phr_matmul"]:
+                 "PHRMatmulFunction", "phr_matmul", "CV2LRTController"]:
         assert hasattr(packr, name), name
+        assert name in packr.__all__, name
+    assert packr.CV2LRTController is packr.VelvetController and packr.PHRLinear is PackRLinear
     with pytest.warns(RuntimeWarning):
         mgr = packr.OffloadManager(prefetch_depth=2)
     layer = PackRLinear(8, 4)
