@@ -42,6 +42,7 @@
 // packr_selfcheck_rounding (every positive normal reciprocal argument, every
 // square-root argument in [2^-100, 2^128)).  Other blocks take the IEEE
 // operations.
+#include <atomic>
 #include <cstring>
 #include <type_traits>
 
@@ -693,19 +694,22 @@ __global__ void selfcheck_kernel(unsigned long long* bad, const Hyper h, unsigne
 
 template <bool BF16>
 int launch_dtype(const packr_adam_tensor* tensors, int n_tensors, const Hyper& h, cudaStream_t stream) {
-  static int occ[kMaxDevices] = {};
+  // per-device cache; relaxed atomics: concurrent first calls store the same value
+  static std::atomic<int> occ[kMaxDevices];
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= kMaxDevices) return PACKR_ERR_DEVICE;
   constexpr int kSmem = Stage<BF16>::kCtaBytes;
-  if (occ[dev] == 0) {
+  int occ_dev = occ[dev].load(std::memory_order_relaxed);
+  if (occ_dev == 0) {
     if (cudaFuncSetAttribute(adam8_kernel<BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess)
       return launch_status();
     int o = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, adam8_kernel<BF16>, kThreads, kSmem) != cudaSuccess || o < 1) o = 1;
-    occ[dev] = o;
+    occ[dev].store(o, std::memory_order_relaxed);
+    occ_dev = o;
   }
-  const int max_ctas = sm_count() * occ[dev];
+  const int max_ctas = sm_count() * occ_dev;
   const int want_dtype = BF16 ? PACKR_DTYPE_BF16 : PACKR_DTYPE_F32;
   Launch L;
   int i = 0;

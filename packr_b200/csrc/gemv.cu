@@ -21,6 +21,8 @@
 //
 // gemv_reduce_kernel (a fixed-order sum of split partials plus the bias) is
 // the final pass of the skinny tensor-core forward.
+#include <atomic>
+
 #include "common.cuh"
 #include "sm100.cuh"
 
@@ -351,14 +353,15 @@ template <int MB, int CPT, int U = PACKR_GEMV_ROWS_IN_FLIGHT>
 int launch(const Plan& p, const void* x, int x_f32, int Mr, const uint8_t* W_p, const uint16_t* W_f, const float* lut,
            const void* bias, int bias_f32, float* out, long long K, long long N, cudaStream_t st) {
   auto kern = gemv_cluster_kernel<MB, CPT, U>;
-  static int attr_done[64] = {0};
+  // per-device flag; relaxed atomics: concurrent first calls set the same attributes
+  static std::atomic<int> attr_done[64];
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!attr_done[dev & 63]) {
+  if (!attr_done[dev & 63].load(std::memory_order_relaxed)) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024) != cudaSuccess ||
         cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
       return PACKR_ERR_CUDA;
-    attr_done[dev & 63] = 1;
+    attr_done[dev & 63].store(1, std::memory_order_relaxed);
   }
   Plan q = p;
   for (;;) {

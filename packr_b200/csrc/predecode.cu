@@ -11,6 +11,8 @@
 // warps, and the add is the same add.rn.bf16x2, so both decodes give the same
 // bits.  W_f and W_p are read with the evict-first hint so that the decoded
 // array stays in L2 for the GEMM that follows.
+#include <atomic>
+
 #include "common.cuh"
 
 namespace packr {
@@ -68,18 +70,19 @@ int predecode(const uint8_t* W_p, const uint16_t* W_f, const float* lut, uint16_
   const long long chunks = K * N / 8;
   if (chunks == 0) return PACKR_OK;
   // as many resident blocks as fit (smem, registers), one wave: the loop
-  // strides over the chunks
-  static int per_sm[64] = {0};
+  // strides over the chunks.  Blocks per SM are cached per device (relaxed
+  // atomics: concurrent first calls store the same value).
+  static std::atomic<int> per_sm[64];
   int dev = 0;
   cudaGetDevice(&dev);
-  if (per_sm[dev & 63] == 0) {
-    int n = 0;
+  int n = per_sm[dev & 63].load(std::memory_order_relaxed);
+  if (n == 0) {
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, predecode_kernel, kPredecodeThreads, 0) != cudaSuccess || n < 1)
       n = 4;
-    per_sm[dev & 63] = n;
+    per_sm[dev & 63].store(n, std::memory_order_relaxed);
   }
   const long long want = (chunks + kPredecodeThreads - 1) / kPredecodeThreads;
-  const long long cap = (long long)per_sm[dev & 63] * sm_count();
+  const long long cap = (long long)n * sm_count();
   predecode_kernel<<<(int)(want < cap ? want : cap), kPredecodeThreads, 0, st>>>(
       reinterpret_cast<const uint2*>(W_p), reinterpret_cast<const uint4*>(W_f), lut, reinterpret_cast<uint4*>(out),
       chunks);
