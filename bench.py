@@ -202,7 +202,6 @@ def cpu_adam_reference(n: int, reps_budget_s: float, min_reps: int = 3):
     built from source into oracle/_ref) on n fp32 params; single-threaded as
     written.  Falls back to the oracle's C port when the build is absent."""
     import importlib.util
-    import numpy as np
     so = REPO / "oracle" / "_ref" / "ref_cpu_adam8.so"
     g = torch.Generator().manual_seed(0)
     p = (torch.randn(n, generator=g) * 0.02)

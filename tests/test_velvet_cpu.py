@@ -6,7 +6,7 @@ import pytest
 import torch
 
 from packr_b200 import VelvetController
-from velvet_replay import META, replay
+from velvet_replay import replay
 
 
 @pytest.mark.parametrize("setting", range(3))
