@@ -861,6 +861,14 @@ def reference_arm(args, world, rank):
                 "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
                 "e2e": {"value": round(cb["value"], 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
+    if args.workload == "llama8b":
+        return {"impl": "reference", "unavailable": "no CPU arm for the Llama-3-8B-shaped step: that configuration "
+                "is a scale-out measurement (a host step of the 8B-parameter model would take hours); the ffn "
+                "workload's reference arm times the same PackRLinear op sequence on the host"}
+    if args.workload == "bert":
+        return {"impl": "reference", "unavailable": "no CPU arm for the BERT-base training step (encoder, loss and "
+                "optimizer on the host exceed a bounded sample); the ffn workload's reference arm times the same "
+                "PackRLinear op sequence on the host"}
     raise SystemExit(f"unknown workload {args.workload}")
 
 

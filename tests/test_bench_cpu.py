@@ -34,6 +34,12 @@ def test_reference_arm_line(workload):
     assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
 
 
+@pytest.mark.parametrize("workload", ["bert", "llama8b"])
+def test_reference_arm_without_cpu_baseline_says_so(workload):
+    lines = run_bench("bench.py", "--impl", "reference", "--workload", workload, "--steps", "1", "--warmup", "3")
+    assert len(lines) == 1 and lines[0]["impl"] == "reference" and lines[0]["unavailable"]
+
+
 def test_reference_arm_two_ranks_prints_once():
     lines = run_bench("-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2", "--master-addr",
                       "127.0.0.1", "--master-port", "29541", "bench.py", "--impl", "reference", "--workload", "adam8",
