@@ -42,3 +42,10 @@ def test_adam_rejects_bad_arguments_before_touching_the_device():
     assert lib.packr_adam8_multi(None, -1, 1e-3, .9, .999, 1e-8, .1, .001, 0., None) == 1
     assert lib.packr_adam8_multi(None, 3, 1e-3, .9, .999, 1e-8, .1, .001, 0., None) == 1
     assert lib.packr_adam8_multi(None, 0, 1e-3, .9, .999, 1e-8, .1, .001, 0., None) == 0
+
+
+def test_variant_build_needs_its_own_output():
+    import pytest
+    from packr_b200 import build
+    with pytest.raises(ValueError):
+        build.build(defines=["PACKR_SKINNY_N16=1"])  # would overwrite the in-tree library
