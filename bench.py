@@ -196,6 +196,30 @@ def timed(fn, steps: int, warmup: int, world: int, flush=None, warm_seconds: flo
     return max_over_ranks(total, world), ms
 
 
+def b2b_ms(fn, reps: int, warm: int = 3, min_seconds: float = 0.0) -> float:
+    """Mean device time of one fn() call over `reps` calls launched back to
+    back between one pair of CUDA events on the current stream (after `warm`
+    untimed calls; more calls while the first `reps` took under
+    `min_seconds`), so that the host's launch gaps between calls are not
+    counted where the GPU has queued work."""
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = reps
+    while True:
+        a.record(s)
+        for _ in range(n):
+            fn()
+        b.record(s)
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b)
+        if ms * 1e-3 >= min_seconds or n >= 64 * reps:
+            return ms / n
+        n *= 2
+
+
 # ---------------------------------------------------------------- CPU baselines
 def cpu_adam_reference(n: int, reps_budget_s: float, min_reps: int = 3):
     """Times the reference's C++ CPU 8-bit AdamW (packr/offload.py:39-130,
@@ -613,15 +637,15 @@ def bench_ffn(args, world, rank, peaks, peak_kind):
     # the forward of the gate layer (predecode + GEMM), then its two kernels
     # timed alone: the GEMM over the decoded W (the dominant kernel) and the
     # HBM-bound predecode (5 bytes per weight)
+    # (each timed over back-to-back calls between one event pair; a call's
+    # operands and results, 0.3 GB for the GEMM, exceed L2)
     lay, x = layers[0], xs[0].detach()
+    reps = max(args.steps, 10)
     fwd = lambda: K.forward(x, lay.W_p, lay.W_f, lay.lut, None)
-    _, f_per = timed(fwd, max(args.steps, 10), 3, 1)
-    f_ms = statistics.mean(f_per)
+    f_ms = b2b_ms(fwd, reps)
     Wd = K.predecode_bf16(lay.W_p, lay.W_f, lay.lut)
-    _, g_per = timed(lambda: K.forward_decoded(x, Wd, None), max(args.steps, 10), 3, 1)
-    g_ms = statistics.mean(g_per)
-    _, p_per = timed(lambda: K.predecode_bf16(lay.W_p, lay.W_f, lay.lut), max(args.steps, 10), 3, 1)
-    p_ms = statistics.mean(p_per)
+    g_ms = b2b_ms(lambda: K.forward_decoded(x, Wd, None), reps)
+    p_ms = b2b_ms(lambda: K.predecode_bf16(lay.W_p, lay.W_f, lay.lut), reps)
     del Wd
     f_flops = 2.0 * M * FFN_HIDDEN * FFN_INTER
     achieved = f_flops / (g_ms * 1e-3) / 1e12
@@ -629,7 +653,7 @@ def bench_ffn(args, world, rank, peaks, peak_kind):
     pre_gbs = pre_bytes / (p_ms * 1e-3) / 1e9
     cnt = lay.lut_counts()
     bwd = lambda: K.backward(dys[0], x, lay.W_p, lay.W_f, lay.lut, cnt, True, True, True, False)
-    _, b_per = timed(bwd, max(args.steps, 10), 3, 1)
+    b_ms = b2b_ms(bwd, reps)
     # end to end: every step copies x and dY from pinned host memory and reads dlut back
     hx = [t.detach().cpu().pin_memory() for t in xs]
     hdy = [t.cpu().pin_memory() for t in dys]
@@ -679,7 +703,8 @@ def bench_ffn(args, world, rank, peaks, peak_kind):
                    "parallelism": f"dp{world}, ZeRO-1 sharded 8-bit optimizer state"},
         "fwd_bwd_only": {"tflops": round(world * flops / (fb_ms * 1e-3) / 1e12, 2), "ms_per_step": round(fb_ms, 4)},
         "phases_ms_gate_layer": {"forward": round(f_ms, 4), "forward_gemm": round(g_ms, 4),
-                                 "predecode": round(p_ms, 4), "backward": round(statistics.mean(b_per), 4)},
+                                 "predecode": round(p_ms, 4), "backward": round(b_ms, 4),
+                                 "timing": "back-to-back calls between one pair of CUDA events"},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peaks["bf16_tflops"],
                      "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
                      "traffic": load_traffic("packr_gemm_kernel<FWD,plain>", "ffn_gate_M%d" % M),
@@ -698,7 +723,156 @@ def bench_ffn(args, world, rank, peaks, peak_kind):
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_linear_port(args.cpu_seconds)
+    del layers, xs, dys, opt, hx, hdy, dx_in, ddy_in
+    torch.cuda.empty_cache()
+    if not args.no_extras:
+        line.update(ffn_extras(args, world, rank, peaks))
     return line
+
+
+# ---------------------------------------------------------------- extras of the default line
+SWEEP_M = (1, 16, 256, 4096, 16384)
+
+
+def ffn_bytes(M: int) -> float:
+    """Algorithmic bytes of one fwd+bwd of the three FFN layers: per layer
+    8KN + 6MK + 8MN (W_f / W_p read by the forward and by the dX GEMM, dW_f
+    written; x, dX, out and dY once each)."""
+    return float(sum(8 * k * n + 6 * M * k + 8 * M * n for _, k, n in FFN_LAYERS))
+
+
+def replayable(fn):
+    """fn captured in a CUDA graph (its launches then run without the host's
+    gaps between them), or fn itself when capture is not possible."""
+    try:
+        return graph_of(fn), "CUDA graph replay"
+    except Exception:
+        torch.cuda.synchronize()
+        return fn, "eager"
+
+
+def ffn_sweep(dev, peaks) -> dict:
+    """fwd+bwd of the gate/up/down layers through PackRLinear's autograd at
+    each token count of the sweep (bf16 x, f32 dY, dW_f + dlut + dX)."""
+    from packr_b200 import PackRLinear
+    layers = [PackRLinear.synthetic(k, n, bias=False, device=dev, seed=200 + i, lut_std=0.02 * math.sqrt(768 / k),
+                                    wf_std=0.002 * math.sqrt(768 / k)) for i, (_, k, n) in enumerate(FFN_LAYERS)]
+    for lay in layers:
+        lay.lut_counts()
+    ridge = peaks["bf16_tflops"] * 1e12 / (peaks["hbm_gbs"] * 1e9)
+    out = {}
+    for M in SWEEP_M:
+        g = torch.Generator(device=dev).manual_seed(7000 + M)
+        xs = [torch.randn(M, k, generator=g, device=dev).to(torch.bfloat16).requires_grad_(True)
+              for _, k, _ in FFN_LAYERS]
+        dys = [torch.randn(M, n, generator=g, device=dev).to(torch.bfloat16).float() for _, _, n in FFN_LAYERS]
+
+        def fb():
+            for lay, x, dy in zip(layers, xs, dys):
+                lay.W_f.grad = None
+                lay.lut.grad = None
+                x.grad = None
+                lay(x).backward(dy)
+        run, how = replayable(fb) if M <= 256 else (fb, "eager")
+        ms = b2b_ms(run, 10, min_seconds=0.05)
+        flops, nbytes = ffn_flops(M), ffn_bytes(M)
+        tf, gbs = flops / (ms * 1e-3) / 1e12, nbytes / (ms * 1e-3) / 1e9
+        bound = "tensor" if flops / nbytes >= ridge else "hbm"
+        out[str(M)] = {"ms": round(ms, 4), "tflops": round(tf, 2), "gbs": round(gbs, 1), "bound": bound,
+                       "frac": round(tf / peaks["bf16_tflops"] if bound == "tensor" else gbs / peaks["hbm_gbs"], 4),
+                       "launch": how}
+        del xs, dys, run
+    return out
+
+
+def decode_points(dev, peaks) -> dict:
+    """Forward of the three FFN layers at 1 and 16 tokens, replayed from a
+    CUDA graph; GB/s of packed weights (3 bytes per weight)."""
+    from packr_b200 import kernel as K
+    from packr_b200.synthetic import linear_case
+    wbytes = sum(3.0 * k * n for _, k, n in FFN_LAYERS)
+    out = {}
+    for M in (1, 16):
+        cases = []
+        for i, (_, k, n) in enumerate(FFN_LAYERS):
+            c = linear_case(M, k, n, x_dtype=torch.bfloat16, bias=False, seed=100 + i, fanin_scaled=True)
+            cases.append({kk: (v.to(dev) if v is not None else None) for kk, v in c.items()})
+
+        def fwd():
+            for c in cases:
+                K.forward(c["x"], c["W_p"], c["W_f"], c["lut"], None)
+        ms = b2b_ms(graph_of(fwd), 50)
+        algo = sum(3.0 * k * n + 2.0 * M * k + 4.0 * M * n for _, k, n in FFN_LAYERS)
+        out[str(M)] = {"ms": round(ms, 5), "gbs": round(wbytes / (ms * 1e-3) / 1e9, 1),
+                       "frac": round(algo / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
+                       "kernel": "gemv_cluster_kernel" if M <= 4 else "skinny_kernel + gemv_reduce_kernel"}
+        del cases
+    return out
+
+
+def adam8_point(dev, peaks) -> dict:
+    """CUDA8BitAdam over one 110,000,000-element bf16 parameter (lr 2e-5,
+    betas (0.9, 0.999), eps 1e-8, wd 0.01): Gparam/s and HBM fraction at
+    10.0625 algorithmic bytes per parameter."""
+    from packr_b200.cuda_adam import CUDA8BitAdam
+    from packr_b200.synthetic import adam_grad, adam_params
+    n = ADAM_N
+    p = torch.nn.Parameter(adam_params(n, dtype=torch.bfloat16, seed=0, device=dev))
+    p.grad = adam_grad(n, 1, dtype=torch.bfloat16, device=dev)
+    opt = CUDA8BitAdam([p], lr=2e-5, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01)
+    ms = b2b_ms(opt.step, 20)
+    gbs = n * ADAM_BYTES_PER_PARAM / (ms * 1e-3) / 1e9
+    return {"ms": round(ms, 5), "gparam_s": round(n / (ms * 1e-3) / 1e9, 2), "gbs": round(gbs, 1),
+            "frac": round(gbs / peaks["hbm_gbs"], 4), "kernel": "adam8_kernel<bf16>",
+            "bytes_per_param": ADAM_BYTES_PER_PARAM}
+
+
+def llama8b_point(args, world, rank, dev) -> dict:
+    """The Llama-3-8B-shaped decoder (32 x 4096, FFN 14336, 32/8 heads, vocab
+    128256, every Linear a PackRLinear), seq 2048, micro-batch 1 per GPU,
+    data parallel over all ranks with ShardedAdam8: whole-job tokens/s."""
+    from packr_b200 import workloads as wl
+    from packr_b200.dp import ShardedAdam8
+    layers = int(os.environ.get("PACKR_BENCH_LLAMA_LAYERS", "32"))
+    t0 = time.perf_counter()
+    model = wl.llama_decoder(dev, layers=layers, seed=0)
+    model.train()
+    opt = ShardedAdam8([p for p in model.parameters() if p.requires_grad], lr=2e-5, weight_decay=0.01,
+                       overlap_grad_reduce=True)
+    ids = wl.llama_batch(dev, seq=2048, seed=rank)
+    build_s = time.perf_counter() - t0
+
+    def step():
+        opt.zero_grad(set_to_none=True)
+        model(input_ids=ids, labels=ids).loss.backward()
+        opt.step()
+    steps = 5
+    total_ms, _ = timed(step, steps, 3, world)
+    ms = total_ms / steps
+    del model, opt
+    torch.cuda.empty_cache()
+    return {"tokens_s": round(world * 2048 / (ms * 1e-3), 1), "ms_per_step": round(ms, 2), "n_gpus": world,
+            "layers": layers, "steps": steps, "warmup": 3, "build_s": round(build_s, 1),
+            "workload": "Llama-3-8B shape, every Linear a PackRLinear, seq 2048, micro-batch 1 per GPU, "
+                        "dp with ShardedAdam8 (max over ranks)"}
+
+
+def ffn_extras(args, world, rank, peaks) -> dict:
+    """The rest of the headline metric beside the ffn step: the 8-bit AdamW
+    rate, the fwd+bwd token-count sweep and the decode-bound forward (one
+    GPU), and the Llama-3-8B-shaped data-parallel step (every N)."""
+    dev = torch.device("cuda", torch.cuda.current_device())
+    ex = {}
+    if world == 1:
+        ex["adam8"] = adam8_point(dev, peaks)
+        torch.cuda.empty_cache()
+        ex["sweep"] = ffn_sweep(dev, peaks)
+        torch.cuda.empty_cache()
+        ex["decode"] = decode_points(dev, peaks)
+        torch.cuda.empty_cache()
+    if not args.no_llama:
+        ex["llama8b"] = llama8b_point(args, world, rank, dev)
+    return ex
 
 
 def profile_once(args):
@@ -725,17 +899,17 @@ LLAMA_LINEARS = [("q_proj", 4096, 4096), ("k_proj", 4096, 1024), ("v_proj", 4096
 
 def cpu_from_linear_port(budget_s: float):
     """The reference's from_linear operation sequence (packr/layer.py:106-159,
-    restated op for op in PackRLinear._from_linear_torch) on the host cores,
-    on a 1024 -> 4096 bf16 layer (the reference's torch.quantile refuses the
-    full Llama layers)."""
-    from packr_b200 import PackRLinear
+    restated op for op in oracle/reference_port.py) on the host cores, on a
+    1024 -> 4096 bf16 layer (the reference's torch.quantile refuses the full
+    Llama layers)."""
+    from oracle import reference_port
     torch.manual_seed(0)
     lin = torch.nn.Linear(1024, 4096, bias=False).to(torch.bfloat16)
     times = []
     t0 = time.perf_counter()
     while len(times) < 2 or time.perf_counter() - t0 < budget_s:
         a = time.perf_counter()
-        PackRLinear._from_linear_torch(lin)
+        reference_port.from_linear(lin.weight, None)
         times.append(time.perf_counter() - a)
     sec = statistics.median(times)
     return {"value": 1024 * 4096 / sec / 1e9, "unit": "Gweights/s", "cores": torch.get_num_threads(),
@@ -883,6 +1057,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="ffn: leave out the adam8 / sweep / decode / llama8b keys of the default line")
+    ap.add_argument("--no-llama", action="store_true", help="ffn: leave out the llama8b key")
     ap.add_argument("--profile-once", action="store_true",
                     help="ffn: run each kernel of one gate-layer step once (for ncu captures), print nothing")
     args = ap.parse_args()

@@ -15,8 +15,10 @@
  *   - W_p and W_f are [K, N] row-major (in_features x out_features), exactly
  *     as PackRLinear stores them (reference packr/layer.py:53-59).
  *   - No entry point keeps mutable global state except the per-device
- *     attribute cache and the device-side wait-timeout word read by
- *     packr_device_status().
+ *     attribute cache, the device-side wait-timeout word read by
+ *     packr_device_status(), and the static scratch array (with its cached
+ *     per-device address) of packr_backward_static_scratch, the one entry
+ *     point that brings its own workspace.
  */
 #ifndef PACKR_B200_H
 #define PACKR_B200_H
@@ -42,6 +44,7 @@ extern "C" {
 /* ---- dtypes ------------------------------------------------------------ */
 #define PACKR_DTYPE_F32 0
 #define PACKR_DTYPE_BF16 1
+#define PACKR_DTYPE_F16 2 /* weights of packr_from_linear_encode only */
 
 const char* packr_error_string(int code);
 int packr_abi_version(void);
@@ -188,9 +191,10 @@ int packr_predecode_route(int64_t M, int64_t K, int64_t N, const uint8_t* W_p, c
 size_t packr_abs_order_stats_workspace_bytes(void);
 int packr_abs_order_stats(const void* w, int dtype, int64_t n, int64_t rank_lo, int64_t rank_hi,
                           float* out2, void* workspace, size_t workspace_bytes, void* stream);
-/* Step 2: weight [out_features, in_features] (nn.Linear layout, f32 or bf16)
- * -> W_p u8 and W_f bf16 [in_features, out_features], lut f32 [256]:
- * t = clamp(w * target_scale, -1.6, 1.6) (bf16-rounded for a bf16 weight),
+/* Step 2: weight [out_features, in_features] (nn.Linear layout, f32, bf16 or
+ * f16) -> W_p u8 and W_f bf16 [in_features, out_features], lut f32 [256]:
+ * t = clamp(w * target_scale, -1.6, 1.6) (rounded to the weight's type for
+ * bf16 / f16, the clamp bounds too),
  * W_p = the nearest codebook entry (lowest index on ties; layer.py:137-141),
  * lut = codebook / scale (layer.py:144), W_f = bf16(w - lut[W_p])
  * (layer.py:148).  codebook (256 f32), scale and target_scale (1 f32 each;
@@ -202,7 +206,7 @@ int packr_from_linear_encode(const void* weight, int dtype, int64_t out_features
 /* ---- VelvetController support ---------------------------------------------
  * sums[i] (double, device) = sum of parameter i's int8 second-moment codes,
  * each times its block's v_scale when block_size > 0, unweighted when
- * block_size == 0 (reference packr/velvet.py:296-320
+ * block_size == 0 (reference packr/velvet.py:270-300
  * takes the mean of the [blocks, block_size] view, or of the raw codes when
  * that view would need padding; the caller divides by numel).  One launch for
  * all parameters (the reference reads one `.item()` per parameter). */
@@ -223,11 +227,17 @@ int packr_state_v_sums(const packr_vsum_desc* descs, int n, double* sums, void* 
  * scratch is one static device array of PACKR_STATIC_SCRATCH_BYTES per GPU,
  * held from the library's load until process exit.  Problems whose scratch
  * need exceeds that size return PACKR_ERR_WORKSPACE before any launch (the
- * need for bf16 x without PACKR_BWD_DW_SPLIT is about M*round8(N)*2 bytes;
- * dX then always takes the fused-decode route).
- * The first call on each device looks up the array's device address (make
- * it before any stream capture).  Every call shares the array; calls that
- * overlap on the GPU (different streams, different threads) race on it. */
+ * need for bf16 x without PACKR_BWD_DW_SPLIT is about M*round8(N)*2 bytes).
+ * Within the array the backward takes the fastest route whose scratch fits,
+ * exactly as packr_backward does with a workspace of that size: for dX the
+ * decode-first route (W decoded into the array, K*N*2 more bytes, plus the
+ * stream-K partial tiles when those fit too) from 1024 rows on, otherwise
+ * the GEMM that decodes W in shared memory.
+ * The first successful call on each device looks up the array's device
+ * address (make it before any stream capture; a failed lookup is retried by
+ * the next call).  Every call shares the array and finds the previous call's
+ * contents there; calls that overlap on the GPU (different streams,
+ * different threads) race on it. */
 #define PACKR_STATIC_SCRATCH_BYTES (32u << 20)
 int packr_backward_static_scratch(const float* dY, const void* x, int x_dtype, const uint8_t* W_p,
                                   const uint16_t* W_f, const float* lut, const int32_t* lut_counts, void* dX,

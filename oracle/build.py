@@ -1,7 +1,11 @@
 """Builds the CPU oracle (test infrastructure) and, when the reference sources
 are present, the reference's own code for this path into oracle/_ref/.
 
-    python -m oracle.build [--force]
+    python -m oracle.build [--force] [--reference-root DIR]
+
+The reference tree's location comes from --reference-root or the
+PACKR_REFERENCE_ROOT environment variable; without either only the oracle's
+own C library is built.
 
 Outputs (all git-ignored, all travel with the working tree):
   oracle/liboracle.so            C restatement of the 8-bit AdamW step.
@@ -26,7 +30,6 @@ import sys
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
-REF_ROOT = Path(os.environ.get("PACKR_REFERENCE_ROOT", "/root/reference"))
 REF_OUT = HERE / "_ref"
 ORACLE_LIB = HERE / "liboracle.so"
 
@@ -60,11 +63,21 @@ def _torch_ext(name: str, sources: list[str], cuda: bool) -> None:
     shutil.copy2(built, REF_OUT / f"{name}.so")
 
 
-def build_reference(force: bool = False) -> list[Path]:
-    """Compiles the reference's Adam kernels; returns the .so files made."""
+def reference_root(root: str | os.PathLike | None = None) -> Path | None:
+    """The reference tree: `root`, else $PACKR_REFERENCE_ROOT, else None."""
+    r = root if root is not None else os.environ.get("PACKR_REFERENCE_ROOT")
+    return Path(r) if r else None
+
+
+def build_reference(force: bool = False, root: str | os.PathLike | None = None) -> list[Path]:
+    """Compiles the reference's Adam kernels from the tree at `root` (or
+    $PACKR_REFERENCE_ROOT); returns the .so files made (none without a tree)."""
     out: list[Path] = []
-    cu = REF_ROOT / "packr" / "cuda_adam_kernel.cu"
-    off = REF_ROOT / "packr" / "offload.py"
+    ref = reference_root(root)
+    if ref is None:
+        return out
+    cu = ref / "packr" / "cuda_adam_kernel.cu"
+    off = ref / "packr" / "offload.py"
     if not cu.exists():
         return out
     REF_OUT.mkdir(exist_ok=True)
@@ -93,10 +106,11 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--no-ref", action="store_true")
+    ap.add_argument("--reference-root", default=None, help="the reference tree (default: $PACKR_REFERENCE_ROOT)")
     a = ap.parse_args()
     print(build_oracle(a.force))
     if not a.no_ref:
-        for p in build_reference(a.force):
+        for p in build_reference(a.force, a.reference_root):
             print(p)
 
 

@@ -18,6 +18,7 @@ _lib = None
 PACKR_OK = 0
 PACKR_DTYPE_F32 = 0
 PACKR_DTYPE_BF16 = 1
+PACKR_DTYPE_F16 = 2
 
 _ERRORS = {
     1: "invalid argument", 2: "bad shape", 3: "misaligned pointer or stride", 4: "workspace too small",

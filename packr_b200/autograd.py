@@ -23,10 +23,11 @@ import torch
 
 from . import kernel as _k
 
-# PACKR_KEEP_DECODED_W=0 trades the second decode of W back for its memory
-# (the decoded W, 2 bytes per weight, is otherwise held from forward to
-# backward on the many-row route).
-KEEP_DECODED_W = os.environ.get("PACKR_KEEP_DECODED_W", "1") != "0"
+# Off by default: between forward and backward a layer holds only its packed
+# weights (3 bytes per weight), as PackR promises.  PACKR_KEEP_DECODED_W=1
+# trades 2 more bytes per weight, held from forward to backward on the
+# many-row route, for the second decode of W in the backward.
+KEEP_DECODED_W = os.environ.get("PACKR_KEEP_DECODED_W", "0") == "1"
 
 
 def grad_sink(param: torch.Tensor) -> torch.Tensor | None:

@@ -2,7 +2,7 @@
 
     python -m packr_b200.build          # incremental
     python -m packr_b200.build --force  # rebuild
-    python -m packr_b200.build -D PACKR_SKINNY_N16=1 --output /tmp/lib.so
+    python -m packr_b200.build -D PACKR_STREAM_K=0 --output /tmp/lib.so
                                         # a variant with compile-time switches,
                                         # loaded through PACKR_B200_LIB=/tmp/lib.so
 

@@ -2,9 +2,9 @@
 //
 //   q99   = torch.quantile(|W|, 0.99) + 1e-6          (layer.py:127)
 //   scale = 1.6 / q99                                  (:128)
-//   t     = clamp(W * scale, -1.6, 1.6)                (:129; for a bf16 W the
-//           product is rounded to bf16 and the multiplier is the one torch
-//           uses, passed as target_scale)
+//   t     = clamp(W * scale, -1.6, 1.6)                (:129; for a bf16 or f16
+//           W the product is rounded to the weight's type and the
+//           multiplier is the one torch uses, passed as target_scale)
 //   W_p   = argmin_i |t - codebook[i]| (first index)   (:137-141)
 //   lut   = codebook / scale                           (:144)
 //   W_f   = bf16(W - lut[W_p])                         (:148)
@@ -30,6 +30,8 @@
 // found by bisection.  Per weight this leaves one 8-byte bucket record (a
 // bucket is 2^-9 wide, two boundaries are at least 0.0066 apart, so a bucket
 // holds at most one) and one comparison against its threshold.
+#include <cuda_fp16.h>
+
 #include "common.cuh"
 
 namespace packr {
@@ -349,13 +351,25 @@ __device__ __forceinline__ void encode_setup(EncodeSm& S, const float* __restric
   __syncthreads();
 }
 
-template <bool BF16>
+// Weight element types of the encode pass.
+enum WType { W_F32 = 0, W_BF16 = 1, W_F16 = 2 };
+
+// A 16-bit weight (bits in the low half) as the f32 it equals exactly.
+template <int WT>
+__device__ __forceinline__ float half_to_f32(unsigned int h) {
+  if constexpr (WT == W_BF16) return __uint_as_float(h << 16);
+  return __half2float(__ushort_as_half((unsigned short)h));
+}
+
+template <int WT>
 __global__ void __launch_bounds__(kEncThreads) encode_kernel(const void* __restrict__ weight, long long out_f,
                                                              long long in_f, const float* __restrict__ codebook,
                                                              const float* __restrict__ scale_p,
                                                              const float* __restrict__ target_scale_p,
                                                              uint8_t* __restrict__ W_p, uint16_t* __restrict__ W_f,
                                                              float* __restrict__ lut) {
+  constexpr bool BF16 = WT == W_BF16;
+  constexpr bool HALF = WT != W_F32;  // 16-bit weights
   __shared__ EncodeSm S;
   __shared__ __align__(16) float tile[kTile * kTile];
   const int tid = threadIdx.x;
@@ -365,7 +379,7 @@ __global__ void __launch_bounds__(kEncThreads) encode_kernel(const void* __restr
 
   const long long tiles_i = (in_f + kTile - 1) / kTile, tiles_o = (out_f + kTile - 1) / kTile;
   const long long ntiles = tiles_i * tiles_o;
-  constexpr int kVec = BF16 ? 8 : 4;  // elements per 16-byte load
+  constexpr int kVec = HALF ? 8 : 4;  // elements per 16-byte load
   const bool vec_rows = (in_f % kVec) == 0 && (reinterpret_cast<uintptr_t>(weight) & 15) == 0;
   for (long long tl = blockIdx.x; tl < ntiles; tl += gridDim.x) {
     const long long i0 = (tl % tiles_i) * kTile;  // in (columns of weight)
@@ -377,7 +391,7 @@ __global__ void __launch_bounds__(kEncThreads) encode_kernel(const void* __restr
       const long long o = o0 + r, i = i0 + c0;
       float v[16];
       if (o < out_f && vec_rows && i + 16 <= in_f) {
-        if constexpr (BF16) {
+        if constexpr (HALF) {
           const uint4* src = reinterpret_cast<const uint4*>(static_cast<const unsigned short*>(weight) + o * in_f + i);
 #pragma unroll
           for (int k = 0; k < 2; ++k) {
@@ -385,8 +399,8 @@ __global__ void __launch_bounds__(kEncThreads) encode_kernel(const void* __restr
             const unsigned int ws[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              v[8 * k + 2 * e] = __uint_as_float(ws[e] << 16);
-              v[8 * k + 2 * e + 1] = __uint_as_float(ws[e] & 0xFFFF0000u);
+              v[8 * k + 2 * e] = half_to_f32<WT>(ws[e] & 0xFFFFu);
+              v[8 * k + 2 * e + 1] = half_to_f32<WT>(ws[e] >> 16);
             }
           }
         } else {
@@ -405,7 +419,7 @@ __global__ void __launch_bounds__(kEncThreads) encode_kernel(const void* __restr
         for (int c = 0; c < 16; ++c) {
           v[c] = 0.0f;
           if (o < out_f && i + c < in_f)
-            v[c] = BF16 ? bf16_to_f32(static_cast<const unsigned short*>(weight)[o * in_f + i + c])
+            v[c] = HALF ? half_to_f32<WT>(static_cast<const unsigned short*>(weight)[o * in_f + i + c])
                         : static_cast<const float*>(weight)[o * in_f + i + c];
         }
       }
@@ -433,6 +447,12 @@ __global__ void __launch_bounds__(kEncThreads) encode_kernel(const void* __restr
             // clamp bound rounds to bf16(1.6) = 1.6015625
             t = bf16_to_f32(f32_to_bf16_rne(__fmul_rn(w, tscale)));
             t = fminf(fmaxf(t, -1.6015625f), 1.6015625f);
+          } else if constexpr (WT == W_F16) {
+            // f16 * f32 scalar: the product in f32, rounded to f16 (RN, with
+            // f16's own overflow to inf); the clamp bound rounds to
+            // f16(1.6) = 1.599609375
+            t = __half2float(__float2half_rn(__fmul_rn(w, tscale)));
+            t = fminf(fmaxf(t, -1.599609375f), 1.599609375f);
           } else {
             t = fminf(fmaxf(__fmul_rn(w, tscale), -1.6f), 1.6f);
           }
@@ -529,7 +549,8 @@ extern "C" int packr_from_linear_encode(const void* weight, int dtype, int64_t o
   using namespace packr::compress;
   if (!weight || !codebook || !scale || !W_p || !W_f || !lut) return PACKR_ERR_INVALID_ARGUMENT;
   if (target_scale == nullptr) target_scale = scale;
-  if (dtype != PACKR_DTYPE_F32 && dtype != PACKR_DTYPE_BF16) return PACKR_ERR_INVALID_ARGUMENT;
+  if (dtype != PACKR_DTYPE_F32 && dtype != PACKR_DTYPE_BF16 && dtype != PACKR_DTYPE_F16)
+    return PACKR_ERR_INVALID_ARGUMENT;
   if (out_features < 1 || in_features < 1) return PACKR_ERR_SHAPE;
   if (!aligned(weight, dtype == PACKR_DTYPE_F32 ? 4 : 2) || !aligned(W_f, 2) || !aligned(codebook, 4) ||
       !aligned(scale, 4) || !aligned(target_scale, 4) || !aligned(lut, 4))
@@ -540,9 +561,13 @@ extern "C" int packr_from_linear_encode(const void* weight, int dtype, int64_t o
   const int grid = (int)(tiles < sm_count() * 8 ? tiles : sm_count() * 8);
   cudaStream_t s = as_stream(stream);
   if (dtype == PACKR_DTYPE_BF16)
-    encode_kernel<true><<<grid, kEncThreads, 0, s>>>(weight, out_features, in_features, codebook, scale, target_scale, W_p, W_f, lut);
+    encode_kernel<W_BF16><<<grid, kEncThreads, 0, s>>>(weight, out_features, in_features, codebook, scale,
+                                                       target_scale, W_p, W_f, lut);
+  else if (dtype == PACKR_DTYPE_F16)
+    encode_kernel<W_F16><<<grid, kEncThreads, 0, s>>>(weight, out_features, in_features, codebook, scale,
+                                                      target_scale, W_p, W_f, lut);
   else
-    encode_kernel<false><<<grid, kEncThreads, 0, s>>>(weight, out_features, in_features, codebook, scale, target_scale, W_p,
-                                                      W_f, lut);
+    encode_kernel<W_F32><<<grid, kEncThreads, 0, s>>>(weight, out_features, in_features, codebook, scale,
+                                                      target_scale, W_p, W_f, lut);
   return launch_status();
 }

@@ -113,14 +113,6 @@ __host__ __device__ constexpr size_t cluster_smem(int rows_per_cta) {
 #ifndef PACKR_GEMV_MIN_CTAS
 #define PACKR_GEMV_MIN_CTAS 3
 #endif
-// Programmatic dependent launch (1: on; off until measured on a B200): the
-// next kernel of the stream is launched while this one runs, and each
-// launch reads nothing from global memory before the kernel ahead of it in
-// the stream has completed (griddepcontrol.wait), so only the launch and the
-// CTAs' start overlap the previous kernel's tail.
-#ifndef PACKR_GEMV_PDL
-#define PACKR_GEMV_PDL 0
-#endif
 template <int MB, int CPT, int U>
 __global__ void __launch_bounds__(kThreads, (MB <= 2 ? PACKR_GEMV_MIN_CTAS : 2))
     gemv_cluster_kernel(const void* __restrict__ x, int x_f32, int Mr, const uint8_t* __restrict__ W_p,
@@ -141,10 +133,6 @@ __global__ void __launch_bounds__(kThreads, (MB <= 2 ? PACKR_GEMV_MIN_CTAS : 2))
   const int k0 = rank * rows_per_cta;
   const int k1 = min(K, k0 + rows_per_cta);
   const int nrows_cta = max(0, k1 - k0);
-#if PACKR_GEMV_PDL
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-#endif
   {
     // thread t loads lut[t] once and writes its 32 lane copies, rotated so
     // that the warp's stores fall in 32 different banks
@@ -385,18 +373,13 @@ int launch(const Plan& p, const void* x, int x_f32, int Mr, const uint8_t* W_p, 
     cfg.blockDim = dim3(kThreads, 1, 1);
     cfg.dynamicSmemBytes = q.smem;
     cfg.stream = st;
-    cudaLaunchAttribute attr[2];
+    cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 1;
     attr[0].val.clusterDim.y = (unsigned)q.cluster;
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-#if PACKR_GEMV_PDL
-    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[1].val.programmaticStreamSerializationAllowed = 1;
-    cfg.numAttrs = 2;
-#endif
     int clusters = 0;
     if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess) {
       cudaGetLastError();

@@ -68,7 +68,7 @@ size_t plan_forward(Carve& c, FwdPlan& p, long long M, long long K, long long N,
 struct BwdPlan {
   uint16_t *dh, *dl, *xh, *xl;
   uint16_t* wd;  // decoded W [K, N] (predecode route for dX only)
-  float* skp;    // stream-K partials / flags, shared by the dX and dW GEMMs
+  float* skp;    // stream-K partials / flags of the plain dX GEMM
   int* skf;
   float *colsum, *dlut_sum;
   int32_t* counts;
@@ -79,7 +79,7 @@ size_t plan_backward(Carve& c, BwdPlan& p, long long M, long long K, long long N
                      bool sk = false, bool wd_given = false) {
   const bool split = (flags & PACKR_BWD_DW_SPLIT) != 0 && (want_dw || want_dlut);
   p.wd = pre && want_dx && !wd_given ? c.take<uint16_t>((size_t)K * N) : nullptr;
-  const bool use_sk = sk && ((pre && want_dx) || want_dw || want_dlut);
+  const bool use_sk = sk && pre && want_dx;  // only the plain dX GEMM splits tiles (stream-K)
   const int msub = pre && want_dx ? plain_msub(M) : 1;
   p.skp = use_sk ? c.take<float>(gemm::sk_partial_bytes(sk_pairs(), msub) / sizeof(float)) : nullptr;
   p.skf = use_sk ? c.take<int>(gemm::sk_flag_bytes(sk_pairs()) / sizeof(int)) : nullptr;

@@ -16,17 +16,16 @@
 namespace packr {
 namespace gemm {
 
-// Stage slots of the barrier block (8 with the 16-token configuration).
-constexpr int kSkMaxStages = PACKR_SKINNY_N16 ? 8 : 6;
+// Stage slots of the barrier block.
+constexpr int kSkMaxStages = 6;
 
 template <int NPAD>
 struct SkCfg {
   // as many stages as shared memory holds: under full load a stage's TMA
-  // takes ~2.3 us to land, so the ring's depth sets the streaming rate.  The
-  // 16-token MMA width (a 2 KB x tile) with a lut of two bf16 entries per
-  // shared-memory word (16 KB instead of 32 KB) fits 8.
-  static constexpr bool kPackedLut = NPAD == 16;
-  static constexpr int kStages = NPAD == 16 ? 8 : NPAD <= 64 ? 6 : NPAD <= 128 ? 4 : 3;
+  // takes ~2.3 us to land, so the ring's depth sets the streaming rate.  (A
+  // 16-token MMA width with a lut of two bf16 entries per shared-memory word,
+  // which fits 8 stages, measured 14 % slower at 16 tokens on a B200.)
+  static constexpr int kStages = NPAD <= 64 ? 6 : NPAD <= 128 ? 4 : 3;
   static constexpr int kWBytes = BN_CTA * BK * 2;  // W_f / decoded A tile: 64 k x 128 n, two 64-column blocks
   static constexpr int kXBytes = NPAD * BK * 2;    // x tile: NPAD tokens x 64 k, K-major
   static constexpr int kPBytes = BN_CTA * BK;      // W_p tile, u8 row-major 64 x 128
@@ -41,7 +40,7 @@ struct SkCfg {
   static constexpr int kDecWarp0 = 2 + kEpiWarps;
   static constexpr int kThreads = (2 + kEpiWarps + kDecWarps) * 32;
   static constexpr int kTmemCols = 2 * NPAD;  // two accumulator slots
-  static constexpr int kLutBytes = kPackedLut ? LUT_BYTES / 2 : LUT_BYTES;
+  static constexpr int kLutBytes = LUT_BYTES;
   static constexpr int kBarOff = kStages * kStageBytes + kLutBytes;
   static constexpr int kSmemBytes = kBarOff + 256 + 1024;
   static constexpr uint32_t kIdesc = idesc_bf16_f32(128, NPAD, /*A MN-major*/ true, /*B MN-major*/ false);
@@ -68,54 +67,6 @@ struct SkParams {
 struct SkMaps {
   CUtensorMap wf, wp, x;
 };
-
-#if PACKR_SKINNY_N16
-// decode_in_place<FWD, NT> over the two-entries-per-word lut: entry e is the
-// low (e even) or high (e odd) half of word (e / 2) * 32 + lane, picked by
-// the prmt selector (bytes 0-1 or 2-3 of the first word, 4-5 or 6-7 of the
-// second).  Same loads, add and stores, so the same bits.
-template <int NT>
-__device__ __forceinline__ void decode_in_place_packed(const Params& P, uint8_t* b_stage, const uint8_t* wp_stage,
-                                                       const uint32_t* lut_lane, int t, int nb0, int k0) {
-  constexpr int NCH = BN_CTA * BK / 8 / NT;
-  uint4 f[NCH];
-  uint2 w[NCH];
-  int nv[NCH];
-  uint32_t off[NCH];
-#pragma unroll
-  for (int i = 0; i < NCH; ++i) {
-    int brow, bcol8;
-    chunk_coords<FWD, NT>(t, i, brow, bcol8);
-    off[i] = chunk_smem_off<FWD>(brow, bcol8);
-    const long long wr = (long long)k0 + brow, wc = (long long)nb0 + 8 * bcol8;
-    nv[i] = (wr < P.w_rows && wc < P.w_cols) ? (int)min(8ll, (long long)P.w_cols - wc) : 0;
-    f[i] = *reinterpret_cast<const uint4*>(b_stage + off[i]);
-    w[i] = *reinterpret_cast<const uint2*>(wp_stage + brow * BN_CTA + 8 * bcol8);
-  }
-#pragma unroll
-  for (int i = 0; i < NCH; ++i) {
-    const uint32_t ww[2] = {w[i].x, w[i].y};
-    const uint32_t ff[4] = {f[i].x, f[i].y, f[i].z, f[i].w};
-    uint32_t r[4];
-#pragma unroll
-    for (int p = 0; p < 4; ++p) {
-      const uint32_t word = ww[p >> 1];
-      const int sh = 16 * (p & 1);
-      const uint32_t e0 = (word >> sh) & 0xFFu, e1 = (word >> (sh + 8)) & 0xFFu;
-      const uint32_t l0 = lut_lane[(e0 >> 1) * 32];
-      const uint32_t l1 = lut_lane[(e1 >> 1) * 32];
-      const uint32_t sel = (0x10u + 0x22u * (e0 & 1u)) | ((0x54u + 0x22u * (e1 & 1u)) << 8);
-      r[p] = bf16x2_add(ff[p], prmt(l0, l1, sel));
-    }
-    if (nv[i] < 8) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        if (j >= nv[i]) r[j >> 1] &= (j & 1) ? 0x0000FFFFu : 0xFFFF0000u;
-    }
-    *reinterpret_cast<uint4*>(b_stage + off[i]) = make_uint4(r[0], r[1], r[2], r[3]);
-  }
-}
-#endif
 
 template <int NPAD>
 __global__ void __launch_bounds__(SkCfg<NPAD>::kThreads, 1)
@@ -167,14 +118,7 @@ __global__ void __launch_bounds__(SkCfg<NPAD>::kThreads, 1)
   }
   if (warp >= C::kDecWarp0) {
     const int dw = warp - C::kDecWarp0;
-    if constexpr (C::kPackedLut) {
-      // word (e / 2) * 32 + l: bf16(lut[e & ~1]) in the low half, bf16(lut[e | 1]) in the high half
-      for (int e2 = dw; e2 < 128; e2 += C::kDecWarps)
-        lut_s[e2 * 32 + lane] =
-            f32_to_bf16_rne(__ldg(P.dec.lut + 2 * e2)) | (f32_to_bf16_rne(__ldg(P.dec.lut + 2 * e2 + 1)) << 16);
-    } else {
-      for (int e = dw; e < 256; e += C::kDecWarps) lut_s[e * 32 + lane] = f32_to_bf16_rne(__ldg(P.dec.lut + e));
-    }
+    for (int e = dw; e < 256; e += C::kDecWarps) lut_s[e * 32 + lane] = f32_to_bf16_rne(__ldg(P.dec.lut + e));
   }
   tc_fence_before();
   __syncthreads();
@@ -249,18 +193,6 @@ __global__ void __launch_bounds__(SkCfg<NPAD>::kThreads, 1)
       tc_fence_after();
       const long long n = (long long)n0 + q * 32 + lane;
       float* dst = P.partial + (long long)split * P.M * P.N + n;
-#if PACKR_SKINNY_N16
-      if constexpr (NPAD == 16) {
-        uint32_t v[16];
-        tmem_ld_32x32b_x16(tmem_base + (uint32_t)(acc * NPAD) + ((uint32_t)(q * 32) << 16), v);
-        tmem_ld_wait();
-        if (n < P.N) {
-#pragma unroll
-          for (int m = 0; m < 16; ++m)
-            if (m < P.M) __stcg(dst + (long long)m * P.N, __uint_as_float(v[m]));
-        }
-      }
-#endif
 #pragma unroll
       for (int c = 0; c < NPAD / 32; ++c) {
         uint32_t v[32];
@@ -292,12 +224,7 @@ __global__ void __launch_bounds__(SkCfg<NPAD>::kThreads, 1)
         const uint32_t ph = (uint32_t)(it / S) & 1u;
         if (!mbar_wait_warp(&bars->full[s], ph, abort_flag)) { ok = false; break; }
         if (t == 0) PACKR_TRACE_EVENT(6, it);
-#if PACKR_SKINNY_N16
-        if constexpr (C::kPackedLut)
-          decode_in_place_packed<C::kDecWarps * 32>(P.dec, w_tile(s), p_tile(s), lut_lane, t, n0, kk * BK);
-        else
-#endif
-          decode_in_place<FWD, C::kDecWarps * 32>(P.dec, w_tile(s), p_tile(s), lut_lane, t, n0, kk * BK);
+        decode_in_place<FWD, C::kDecWarps * 32>(P.dec, w_tile(s), p_tile(s), lut_lane, t, n0, kk * BK);
         fence_proxy_async_smem();
         __syncwarp();
         if (t == 0) PACKR_TRACE_EVENT(7, it);
@@ -317,7 +244,7 @@ __global__ void __launch_bounds__(SkCfg<NPAD>::kThreads, 1)
 
 // Padded MMA width for the token count (the skinny route serves up to 128).
 inline int skinny_npad(long long M) {
-  return PACKR_SKINNY_N16 && M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128;
+  return M <= 32 ? 32 : M <= 64 ? 64 : 128;
 }
 
 struct SkPlan {
@@ -403,11 +330,6 @@ int skinny_forward(const uint16_t* x_bf16, long long ldx, const uint8_t* W_p, co
   P.dec.w_rows = (int)K;
   P.dec.w_cols = (int)N;
   if (M > 128) return PACKR_ERR_SHAPE;
-#if PACKR_SKINNY_N16
-  if (pl.npad == 16)
-    rc = skinny_launch<16>(P, maps, pl.grid, st);
-  else
-#endif
   rc = pl.npad == 32   ? skinny_launch<32>(P, maps, pl.grid, st)
        : pl.npad == 64 ? skinny_launch<64>(P, maps, pl.grid, st)
                        : skinny_launch<128>(P, maps, pl.grid, st);

@@ -9,13 +9,6 @@
 
 #include "common.cuh"
 
-// Skinny forward (skinny.cu) with an MMA N of 16 and a two-entries-per-word
-// lut for up to 16 tokens, 8 stages instead of 6 (1: on).  Off: not yet
-// measured on a B200.
-#ifndef PACKR_SKINNY_N16
-#define PACKR_SKINNY_N16 0
-#endif
-
 namespace packr {
 namespace sm100 {
 
@@ -194,18 +187,6 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
       : "r"(taddr)
       : "memory");
 }
-#if PACKR_SKINNY_N16
-// 16 consecutive 32-bit columns of the warp's 32 TMEM lanes (lane l: row l).
-__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr)
-      : "memory");
-}
-#endif
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // UMMA shared-memory matrix descriptor for a 128-byte-swizzled canonical

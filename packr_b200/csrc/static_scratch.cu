@@ -6,6 +6,7 @@
 // partial sums) lives in one file-scope device array of
 // PACKR_STATIC_SCRATCH_BYTES that every GPU loading this library holds until
 // the process exits.
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -16,20 +17,31 @@ namespace static_scratch {
 static __device__ __align__(256) unsigned char g_scratch[PACKR_STATIC_SCRATCH_BYTES];
 
 constexpr int kMaxDevices = 64;
-std::once_flag g_once[kMaxDevices];
-void* g_ptr[kMaxDevices];
-cudaError_t g_err[kMaxDevices];
+std::mutex g_mu[kMaxDevices];
+std::atomic<void*> g_ptr[kMaxDevices];
 
 // Device address of g_scratch on the current device.  The host-side name
 // g_scratch is only a stand-in for the symbol and must never be passed to a
-// kernel; cudaGetSymbolAddress is asked once per device, with that device
-// current (the first call on each device performs this set-up).
+// kernel; cudaGetSymbolAddress is asked with that device current, and only a
+// successful answer is kept (the first successful call on each device
+// performs this set-up; a failed lookup, e.g. one made during a stream
+// capture, is retried by the next call).
 int device_ptr(void** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return PACKR_ERR_CUDA;
-  std::call_once(g_once[dev], [dev] { g_err[dev] = cudaGetSymbolAddress(&g_ptr[dev], g_scratch); });
-  if (g_err[dev] != cudaSuccess || g_ptr[dev] == nullptr) return PACKR_ERR_CUDA;
-  *out = g_ptr[dev];
+  void* p = g_ptr[dev].load(std::memory_order_acquire);
+  if (p == nullptr) {
+    std::lock_guard<std::mutex> lock(g_mu[dev]);
+    p = g_ptr[dev].load(std::memory_order_relaxed);
+    if (p == nullptr) {
+      if (cudaGetSymbolAddress(&p, g_scratch) != cudaSuccess || p == nullptr) {
+        cudaGetLastError();
+        return PACKR_ERR_CUDA;
+      }
+      g_ptr[dev].store(p, std::memory_order_release);
+    }
+  }
+  *out = p;
   return PACKR_OK;
 }
 

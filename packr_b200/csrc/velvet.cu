@@ -1,5 +1,5 @@
 // Per-parameter means of the int8 second-moment state, for VelvetController
-// (reference packr/velvet.py:296-320 computes one `.item()` per parameter).
+// (reference packr/velvet.py:270-300 computes one `.item()` per parameter).
 // One launch covers every parameter: CTAs (chunk, parameter) each add up a
 // 64K-element chunk in double and fold it into the parameter's slot with one
 // atomic add per warp; the host reads all slots with a single copy.

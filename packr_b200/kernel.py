@@ -220,51 +220,62 @@ def abs_order_stats(w: torch.Tensor, rank_lo: int, rank_hi: int) -> torch.Tensor
     return out
 
 
-def quantile_abs(w: torch.Tensor, q: float) -> torch.Tensor:
-    """torch.quantile(w.abs().float(), q) (linear interpolation) on the
-    device, for any size: the same rank arithmetic (f32 q * (n - 1), floor,
-    ceil, fractional weight) and the same torch.lerp, over order statistics
-    found by the library's radix select instead of a full sort."""
+def quantile_abs(w: torch.Tensor, q: float, lerp_device=None) -> torch.Tensor:
+    """torch.quantile(w.abs().float(), q) (linear interpolation) for any size:
+    the same rank arithmetic (f32 q * (n - 1), floor, ceil, fractional weight)
+    and the same torch.lerp, over order statistics found on w's GPU by the
+    library's radix select instead of a full sort.  The lerp runs on
+    `lerp_device` (default: w's device): torch.quantile of a host tensor
+    interpolates with the CPU kernel."""
     n = w.numel()
     pos = torch.tensor(q, dtype=torch.float32) * (n - 1)
     lo, hi = int(torch.floor(pos)), int(torch.ceil(pos))
     v = abs_order_stats(w, lo, hi)
-    return torch.lerp(v[0], v[1], (pos - lo).to(w.device))
+    if lerp_device is not None:
+        v = v.to(lerp_device)
+    return torch.lerp(v[0], v[1], (pos - lo).to(v.device))
 
 
-def bf16_product_multiplier(scale: torch.Tensor) -> torch.Tensor:
-    """The f32 multiplier torch uses in `bf16_tensor * scale` for a 0-dim f32
-    device tensor `scale` (the product is computed in f32 and rounded to
-    bf16): probed once per device with torch itself."""
-    dev = scale.device
-    key = str(dev)
-    mode = _BF16_SCALAR_MODE.get(key)
+def half_product_multiplier(scale: torch.Tensor, dtype: torch.dtype, device=None) -> torch.Tensor:
+    """The f32 multiplier torch uses in `w * scale` for a bf16 or f16 tensor
+    w and a 0-dim f32 tensor `scale` on `device` (default: scale's device):
+    the product is computed in f32 and rounded to w's type, with the scalar
+    either kept in f32 or first rounded to w's type, which differs between
+    torch's CPU and CUDA kernels; probed once per (device type, dtype) with
+    torch itself."""
+    dev = torch.device(device) if device is not None else scale.device
+    key = (dev.type, dtype)
+    mode = _HALF_SCALAR_MODE.get(key)
     if mode is None:
         g = torch.Generator(device="cpu").manual_seed(0)
-        probe_w = torch.randn(4096, generator=g).to(torch.bfloat16).to(dev)
+        probe_w = torch.randn(4096, generator=g).to(dtype).to(dev)
         probe_s = torch.tensor(1.0 + 2 ** -8 + 2 ** -12 + 2 ** -19, dtype=torch.float32, device=dev)
         got = probe_w * probe_s
-        as_f32 = (probe_w.float() * probe_s).to(torch.bfloat16)
-        as_bf16 = (probe_w.float() * probe_s.to(torch.bfloat16).float()).to(torch.bfloat16)
+        as_f32 = (probe_w.float() * probe_s).to(dtype)
+        as_half = (probe_w.float() * probe_s.to(dtype).float()).to(dtype)
         if torch.equal(got, as_f32):
             mode = "f32"
-        elif torch.equal(got, as_bf16):
-            mode = "bf16"
+        elif torch.equal(got, as_half):
+            mode = "half"
         else:
-            raise RuntimeError("bf16 * f32 scalar: torch's product matches neither rounding")
-        _BF16_SCALAR_MODE[key] = mode
-    return scale if mode == "f32" else scale.to(torch.bfloat16).float()
+            raise RuntimeError(f"{dtype} * f32 scalar: torch's product matches neither rounding")
+        _HALF_SCALAR_MODE[key] = mode
+    return scale if mode == "f32" else scale.to(dtype).float()
 
 
-_BF16_SCALAR_MODE: dict = {}
+_HALF_SCALAR_MODE: dict = {}
 
 
 def from_linear_encode(weight: torch.Tensor, codebook: torch.Tensor, scale: torch.Tensor,
                        target_scale: torch.Tensor | None = None):
     """(W_p u8 [in, out], W_f bf16 [in, out], lut f32 [256]) from an
-    nn.Linear weight [out, in] (packr_from_linear_encode)."""
+    nn.Linear weight [out, in] of f32, bf16 or f16 (packr_from_linear_encode)."""
     lib = _lib.load()
     w = weight.contiguous()
+    code = {torch.float32: _lib.PACKR_DTYPE_F32, torch.bfloat16: _lib.PACKR_DTYPE_BF16,
+            torch.float16: _lib.PACKR_DTYPE_F16}.get(w.dtype)
+    if code is None:
+        raise TypeError(f"unsupported weight dtype {w.dtype}")
     dev = w.device
     out_f, in_f = w.shape
     W_p = torch.empty(in_f, out_f, dtype=torch.uint8, device=dev)
@@ -274,9 +285,9 @@ def from_linear_encode(weight: torch.Tensor, codebook: torch.Tensor, scale: torc
     sc = scale.to(device=dev, dtype=torch.float32).reshape(1).contiguous()
     ts = target_scale.to(device=dev, dtype=torch.float32).reshape(1).contiguous() if target_scale is not None else sc
     with torch.cuda.device(dev):
-        code = lib.packr_from_linear_encode(_ptr(w), _dtype_code(w), out_f, in_f, _ptr(cb), _ptr(sc), _ptr(ts),
-                                            _ptr(W_p), _ptr(W_f), _ptr(lut), _stream(dev))
-    _lib.check("packr_from_linear_encode", code)
+        rc = lib.packr_from_linear_encode(_ptr(w), code, out_f, in_f, _ptr(cb), _ptr(sc), _ptr(ts),
+                                          _ptr(W_p), _ptr(W_f), _ptr(lut), _stream(dev))
+    _lib.check("packr_from_linear_encode", rc)
     return W_p, W_f, lut
 
 

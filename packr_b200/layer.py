@@ -29,21 +29,6 @@ def _build_codebook() -> torch.Tensor:
     return (((g - 7.5) / 7.5) * ((s + 1.0) / 10.0)).to(torch.float32)
 
 
-def _quantile_abs(w: torch.Tensor, q: float) -> torch.Tensor:
-    """torch.quantile(|w|, q) (linear interpolation), also for tensors above
-    torch.quantile's 2^24-element limit (exact order statistics by kthvalue)."""
-    a = w.abs().float().reshape(-1)
-    n = a.numel()
-    if n <= (1 << 24):
-        return torch.quantile(a, q)
-    pos = torch.tensor(q, dtype=torch.float32) * (n - 1)
-    lo = int(torch.floor(pos).item())
-    hi = min(lo + 1, n - 1)
-    v_lo = torch.kthvalue(a, lo + 1).values
-    v_hi = torch.kthvalue(a, hi + 1).values if hi != lo else v_lo
-    return torch.lerp(v_lo, v_hi, (pos - lo).to(a.device))
-
-
 class PackRLinear(nn.Module):
     """PackR linear layer with learnable LUT: out = x @ (W_f + lut[W_p]) + bias."""
 
@@ -97,53 +82,42 @@ class PackRLinear(nn.Module):
         99th percentile maps to 1.6, take the nearest codebook entry per weight
         (lowest index on ties), lut = codebook / scale, W_f = W - lut[W_p].
 
-        A CUDA f32/bf16 weight is compressed by the library's kernels (exact
-        order statistics for the quantile, one encode pass; no size limit);
-        other weights by the same torch operations as the reference."""
+        The compression always runs in the library's kernels (exact order
+        statistics for the quantile, one encode pass; no size limit), on the
+        weight's own GPU or, for a weight held in host memory, on the current
+        CUDA device, after which the new layer's tensors are moved back to
+        the weight's device, as the reference leaves them there.  f32, bf16
+        and f16 weights give the reference's results bit for bit (W * scale
+        rounded to the weight's type with the multiplier torch uses on the
+        weight's device); a weight of another dtype (f64) is compressed from
+        its values rounded to f32."""
         if not isinstance(module, nn.Linear):
             raise TypeError(f"Expected nn.Linear, got {type(module)}")
-        if module.weight.is_cuda and module.weight.dtype in (torch.float32, torch.bfloat16):
-            return cls._from_linear_cuda(module)
-        return cls._from_linear_torch(module)
-
-    @classmethod
-    def _from_linear_torch(cls, module: nn.Linear):
-        """The reference's torch operation sequence (any device)."""
-        packr = cls(module.in_features, module.out_features, bias=module.bias is not None)
-        device = module.weight.device
-        codebook = _build_codebook().to(device)
-        W_orig = module.weight.detach().t()
-        q99 = _quantile_abs(W_orig, 0.99) + 1e-6
-        scale = 1.6 / q99
-        W_target = torch.clamp(W_orig * scale, -1.6, 1.6)
-        in_f, out_f = W_orig.shape
-        best = torch.empty(in_f, out_f, dtype=torch.uint8, device=device)
-        cb = codebook.view(1, 1, 256)
-        # chunk rows so the [rows, out, 256] distance temporary stays ~256 MB
-        chunk = max(1, min(256, (1 << 26) // max(out_f * 256, 1)))
-        for s in range(0, in_f, chunk):
-            e = min(s + chunk, in_f)
-            diff = torch.abs(W_target[s:e].unsqueeze(-1) - cb)
-            best[s:e] = torch.argmin(diff, dim=-1).to(torch.uint8)
-        dequant_lut = codebook / scale
-        quantized = dequant_lut[best.long()]
-        packr.W_p.data = best.contiguous()
-        packr.lut.data = dequant_lut.contiguous().to(device=device, dtype=torch.float32)
-        packr.W_f.data = (W_orig - quantized).contiguous().to(device=device, dtype=torch.bfloat16)
-        if module.bias is not None:
-            packr.bias_f.data = module.bias.detach().to(device=device, dtype=torch.bfloat16)
-        return packr
-
-    @classmethod
-    def _from_linear_cuda(cls, module: nn.Linear):
-        from . import kernel
         w = module.weight.detach()
+        home = w.device
+        if not w.is_cuda:
+            if not torch.cuda.is_available():
+                raise RuntimeError("PackRLinear.from_linear compresses on a CUDA device; none is available "
+                                   "(the B200 build has no CPU path)")
+            w = w.to(torch.device("cuda", torch.cuda.current_device()))
+        if w.dtype not in (torch.float32, torch.bfloat16, torch.float16):
+            w = w.float()
+        m = cls._from_linear_cuda(w, module.bias, home)
+        return m if home.type == "cuda" else m.to(home)
+
+    @classmethod
+    def _from_linear_cuda(cls, w: torch.Tensor, bias: torch.Tensor | None, home: torch.device):
+        from . import kernel
         device = w.device
-        in_f, out_f = module.in_features, module.out_features
-        q99 = kernel.quantile_abs(w, 0.99) + 1e-6
+        out_f, in_f = w.shape
+        # the scalar arithmetic on the weight's own device, as the reference;
+        # |f16| values are exact in f32, which the order statistics read
+        q99 = kernel.quantile_abs(w if w.dtype != torch.float16 else w.float(), 0.99, home) + 1e-6
         scale = 1.6 / q99
-        # W_orig * scale for a bf16 weight: the multiplier as torch applies it
-        target_scale = kernel.bf16_product_multiplier(scale) if w.dtype == torch.bfloat16 else scale
+        # W_orig * scale for a 16-bit weight: the multiplier as torch applies
+        # it on the weight's own device, where the reference computes it
+        half = w.dtype in (torch.bfloat16, torch.float16)
+        target_scale = kernel.half_product_multiplier(scale, w.dtype, home) if half else scale
         W_p, W_f, lut = kernel.from_linear_encode(w, _build_codebook().to(device), scale, target_scale)
         m = cls.__new__(cls)
         nn.Module.__init__(m)
@@ -151,8 +125,8 @@ class PackRLinear(nn.Module):
         m.W_p = nn.Parameter(W_p, requires_grad=False)
         m.W_f = nn.Parameter(W_f)
         m.lut = nn.Parameter(lut)
-        m.bias_f = (nn.Parameter(module.bias.detach().to(device=device, dtype=torch.bfloat16).clone())
-                    if module.bias is not None else None)
+        m.bias_f = (nn.Parameter(bias.detach().to(device=device, dtype=torch.bfloat16).clone())
+                    if bias is not None else None)
         m._counts = None
         m._counts_key = None
         m._offload_mgr = None

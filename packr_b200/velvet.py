@@ -1,5 +1,5 @@
 """VelvetController — velocity-to-learning-rate translation driven by the
-8-bit optimizer's second-moment state (reference packr/velvet.py:22-320).
+8-bit optimizer's second-moment state (reference packr/velvet.py:22-300).
 
 Same constructor, `warmup_step`, `step` (called after `optimizer.step()`),
 `get_stats`, and the same per-parameter arithmetic.  The difference is how
@@ -49,7 +49,7 @@ def state_v_sums(items, device) -> torch.Tensor:
 
 
 def _v_means(states) -> List[float]:
-    """Mean of each state's v as reference velvet.py:296-320 defines it, with
+    """Mean of each state's v as reference velvet.py:270-300 defines it, with
     one device->host copy.  `states`: list of (v, v_scale or None)."""
     if not states:
         return []

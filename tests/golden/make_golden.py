@@ -1,7 +1,7 @@
 """Generates tests/golden/packr_linear_golden.npz by running the REFERENCE
 package's own PackRLinear forward/backward on the CPU.
 
-    python tests/golden/make_golden.py        (needs the reference tree)
+    PACKR_REFERENCE_ROOT=<reference tree> python tests/golden/make_golden.py
 
 The reference's packr_matmul asserts CUDA tensors (packr/kernel.py:117); this
 script runs that same function with only the assert line removed and with the
@@ -25,7 +25,9 @@ from pathlib import Path
 import numpy as np
 import torch
 
-REF = Path(os.environ.get("PACKR_REFERENCE_ROOT", "/root/reference"))
+if not os.environ.get("PACKR_REFERENCE_ROOT"):
+    raise SystemExit("set PACKR_REFERENCE_ROOT to the reference tree (the directory holding packr/)")
+REF = Path(os.environ["PACKR_REFERENCE_ROOT"])
 REPO = Path(__file__).resolve().parents[2]
 sys.dont_write_bytecode = True
 sys.path.insert(0, str(REF))

@@ -2,7 +2,7 @@
 package's VelvetController (packr/velvet.py) on a stand-in optimizer whose
 second-moment states follow a seeded schedule.
 
-    python tests/golden/make_velvet_golden.py        (needs the reference tree)
+    PACKR_REFERENCE_ROOT=<reference tree> python tests/golden/make_velvet_golden.py
 
 Two scenarios:
   f32   every state's v is float32 (velvet.py:307-308, `v.mean()`); three
@@ -30,7 +30,9 @@ from pathlib import Path
 import numpy as np
 import torch
 
-REF = Path(os.environ.get("PACKR_REFERENCE_ROOT", "/root/reference"))
+if not os.environ.get("PACKR_REFERENCE_ROOT"):
+    raise SystemExit("set PACKR_REFERENCE_ROOT to the reference tree (the directory holding packr/)")
+REF = Path(os.environ["PACKR_REFERENCE_ROOT"])
 sys.dont_write_bytecode = True
 sys.path.insert(0, str(REF))
 

@@ -253,3 +253,40 @@ def test_resume_from_state_dict_is_exact(cuda):
     torch.cuda.synchronize()
     for a, b in zip(ref, resumed):
         assert torch.equal(a.detach(), b.detach())
+
+
+def test_fused_quantized_adam_step_with_closure(cuda):
+    """FusedQuantizedAdam (the reference's Triton optimizer name, packr/
+    optim.py:167-285) on the GPU: step(closure) re-evaluates the closure
+    with gradients enabled and returns its loss, and the update equals
+    CUDA8BitAdam's on the same gradients bit for bit (parameters, codes and
+    scales; bf16 and f32 parameters, two parameter groups)."""
+    from packr_b200.optim import FusedQuantizedAdam
+    def make():
+        return [torch.nn.Parameter(adam_params(3 * 256 + 77, dtype=torch.bfloat16, seed=3, device="cuda")),
+                torch.nn.Parameter(adam_params(1000, dtype=torch.float32, seed=4, device="cuda"))]
+    a, b = make(), make()
+    fq = FusedQuantizedAdam([{"params": [a[0]]}, {"params": [a[1]], "lr": 3e-4}], lr=1e-3, weight_decay=0.01,
+                            block_size=256)
+    ref = CUDA8BitAdam([{"params": [b[0]]}, {"params": [b[1]], "lr": 3e-4}], lr=1e-3, weight_decay=0.01)
+    for s in range(1, 4):
+        targets = [adam_grad(p.numel(), s, dtype=torch.float32, device="cuda", std=1e-2) for p in a]
+        calls = []
+
+        def closure():
+            fq.zero_grad(set_to_none=True)
+            loss = sum((p.float() * t).sum() for p, t in zip(a, targets))
+            loss.backward()
+            calls.append(loss.detach())
+            return loss
+        loss = fq.step(closure)
+        assert len(calls) == 1 and loss is not None and torch.equal(loss.detach(), calls[0])
+        for p, q in zip(a, b):
+            q.grad = p.grad.clone()
+        ref.step()
+    torch.cuda.synchronize()
+    for p, q in zip(a, b):
+        assert torch.equal(p.detach(), q.detach())
+        for k in ("m", "v", "m_scale", "v_scale"):
+            assert torch.equal(fq.state[p][k], ref.state[q][k]), k
+    assert fq.step() is None  # without a closure there is no loss to return

@@ -2,14 +2,16 @@
 packr_from_linear_encode): the order statistics against a full sort, the
 quantile against torch.quantile, the compressed layer against the reference's
 own outputs (golden fixtures) and against the reference's torch operation
-sequence run on the same GPU, for f32 and bf16 weights, and a weight above
-torch.quantile's 2^24-element limit."""
+sequence run on the weight's own device (f32, bf16 and f16 weights, on the
+GPU or in host memory), and a weight above torch.quantile's 2^24-element
+limit."""
 from pathlib import Path
 
 import numpy as np
 import pytest
 import torch
 
+from oracle import reference_port
 from packr_b200 import PackRLinear
 from packr_b200 import kernel
 
@@ -78,11 +80,48 @@ def test_from_linear_matches_torch_sequence(cuda, dtype, shape):
         lin.weight.mul_(3.0)
         lin.weight[0, 0] = 0.0
     fast = PackRLinear.from_linear(lin)
-    ref = PackRLinear._from_linear_torch(lin)
-    assert torch.equal(fast.W_p, ref.W_p)
-    assert np.array_equal(bits(fast.W_f), bits(ref.W_f))
-    assert np.array_equal(bits(fast.lut), bits(ref.lut))
-    assert torch.equal(fast.bias_f, ref.bias_f)
+    ref = reference_port.from_linear(lin.weight, lin.bias)
+    assert torch.equal(fast.W_p, ref["W_p"])
+    assert np.array_equal(bits(fast.W_f), bits(ref["W_f"]))
+    assert np.array_equal(bits(fast.lut), bits(ref["lut"]))
+    assert torch.equal(fast.bias_f, ref["bias_f"])
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_from_linear_of_host_weight(cuda, dtype):
+    """A Linear held in host memory is compressed by the same kernels on the
+    current GPU; the new layer's tensors come back to the host and equal the
+    reference's sequence on the host (for bf16 torch's CPU kernel rounds
+    W * scale differently from its CUDA kernel, and the host's rounding is
+    the one reproduced)."""
+    torch.manual_seed(11)
+    lin = torch.nn.Linear(300, 130, bias=True).to(dtype)
+    pk = PackRLinear.from_linear(lin)
+    assert all(t.device.type == "cpu" for t in (pk.W_p, pk.W_f, pk.lut, pk.bias_f))
+    ref = reference_port.from_linear(lin.weight, lin.bias)
+    assert torch.equal(pk.W_p, ref["W_p"])
+    assert np.array_equal(bits(pk.W_f), bits(ref["W_f"]))
+    assert np.array_equal(bits(pk.lut), bits(ref["lut"]))
+    assert torch.equal(pk.bias_f, ref["bias_f"])
+
+
+@pytest.mark.parametrize("home", ["cuda", "cpu"])
+def test_from_linear_of_f16_weight(cuda, home):
+    """An f16 weight (on the GPU or the host) equals the reference's f16
+    sequence on the same device: W * scale rounded to f16 with the
+    multiplier torch uses there, the clamp at f16(1.6)."""
+    torch.manual_seed(12)
+    lin = torch.nn.Linear(256, 192, bias=True).to(dtype=torch.float16)
+    with torch.no_grad():
+        lin.weight.mul_(3.0)
+    lin = lin.to(home)
+    pk = PackRLinear.from_linear(lin)
+    ref = reference_port.from_linear(lin.weight, lin.bias)
+    assert pk.W_p.device.type == home
+    assert torch.equal(pk.W_p, ref["W_p"])
+    assert np.array_equal(bits(pk.W_f), bits(ref["W_f"]))
+    assert np.array_equal(bits(pk.lut), bits(ref["lut"]))
+    assert torch.equal(pk.bias_f, ref["bias_f"])
 
 
 def test_from_linear_beyond_quantile_limit(cuda):

@@ -1,6 +1,6 @@
-"""Host-side logic that needs no GPU: model surgery, from_linear against the
-reference's own compression (golden), config, API surface and the loud
-failure of the GPU-only ops on CPU tensors."""
+"""Host-side logic that needs no GPU: model surgery, the oracle's from_linear
+restatement against the reference's own compression (golden), config, API
+surface and the loud failure of the GPU-only ops on CPU tensors."""
 from pathlib import Path
 
 import numpy as np
@@ -9,7 +9,8 @@ import torch
 
 import packr_b200 as packr
 from packr_b200 import PackRConfig, PackRLinear, compress_model
-from packr_b200.layer import _build_codebook, _quantile_abs
+from packr_b200.layer import _build_codebook
+from oracle import reference_port
 
 GOLD = np.load(Path(__file__).resolve().parent / "golden" / "packr_linear_golden.npz")
 
@@ -22,25 +23,31 @@ def bits(t):
 
 
 @pytest.mark.parametrize("name", ["fl_small", "fl_wide"])
-def test_from_linear_matches_reference(name):
+def test_oracle_from_linear_matches_reference(name):
+    """The oracle's restatement of the reference's from_linear (the checker of
+    the GPU path) reproduces the reference's own outputs bit for bit."""
     w = torch.from_numpy(GOLD[f"{name}/weight"].copy())
     has_b = f"{name}/bias" in GOLD.files
-    lin = torch.nn.Linear(w.shape[1], w.shape[0], bias=has_b)
-    with torch.no_grad():
-        lin.weight.copy_(w)
-        if has_b:
-            lin.bias.copy_(torch.from_numpy(GOLD[f"{name}/bias"].copy()))
-    pl = PackRLinear.from_linear(lin)
-    assert np.array_equal(bits(pl.W_p), GOLD[f"{name}/W_p"])
-    assert np.array_equal(bits(pl.lut), GOLD[f"{name}/lut"])
-    assert np.array_equal(bits(pl.W_f), GOLD[f"{name}/W_f"])
+    b = torch.from_numpy(GOLD[f"{name}/bias"].copy()) if has_b else None
+    r = reference_port.from_linear(w, b)
+    assert np.array_equal(bits(r["W_p"]), GOLD[f"{name}/W_p"])
+    assert np.array_equal(bits(r["lut"]), GOLD[f"{name}/lut"])
+    assert np.array_equal(bits(r["W_f"]), GOLD[f"{name}/W_f"])
     if has_b:
-        assert np.array_equal(bits(pl.bias_f), GOLD[f"{name}/bias_f"])
-    assert not pl.W_p.requires_grad and pl.W_f.dtype == torch.bfloat16 and pl.lut.dtype == torch.float32
+        assert np.array_equal(bits(r["bias_f"]), GOLD[f"{name}/bias_f"])
+
+
+def test_from_linear_needs_a_gpu():
+    """No CPU path: without a CUDA device from_linear refuses loudly."""
+    if torch.cuda.is_available():
+        pytest.skip("a CUDA device is present")
+    with pytest.raises(RuntimeError):
+        PackRLinear.from_linear(torch.nn.Linear(8, 4))
 
 
 def test_codebook_definition():
     cb = _build_codebook()
+    assert torch.equal(cb, reference_port.codebook())
     for i in (0, 15, 16, 255, 0x5A):
         g, s = i & 15, (i >> 4) & 15
         assert cb[i].item() == np.float32(((g - 7.5) / 7.5) * ((s + 1.0) / 10.0))
@@ -49,7 +56,7 @@ def test_codebook_definition():
 def test_quantile_above_torch_limit_matches_order_statistics():
     g = torch.Generator().manual_seed(0)
     w = torch.randn((1 << 24) + 5, generator=g)
-    q = _quantile_abs(w, 0.99).item()
+    q = reference_port.quantile_abs(w, 0.99).item()
     a = np.sort(np.abs(w.numpy()).astype(np.float64))
     pos = 0.99 * (a.size - 1)
     lo = int(np.floor(pos))
@@ -57,7 +64,12 @@ def test_quantile_above_torch_limit_matches_order_statistics():
     assert abs(q - want) <= 1e-6 * want
 
 
-def test_compress_model_scopes():
+def test_compress_model_scopes(monkeypatch):
+    """Which layers compress_model replaces (the name-scope rules); the
+    conversion itself runs on a GPU and is stubbed here."""
+    monkeypatch.setattr(PackRLinear, "from_linear",
+                        classmethod(lambda cls, lin: cls(lin.in_features, lin.out_features, lin.bias is not None)))
+
     class Block(torch.nn.Module):
         def __init__(self):
             super().__init__()

@@ -243,8 +243,13 @@ def torch_reference(c):
     return out, dX, dW, s / (cnt + 1e-8)
 
 
-@pytest.mark.parametrize("M,Kd,Nd", [(4096, 4096, 11008), (4096, 11008, 4096)])
+@pytest.mark.parametrize("M,Kd,Nd", [(256, 4096, 11008), (256, 11008, 4096),
+                                     (4096, 4096, 11008), (4096, 11008, 4096),
+                                     (16384, 4096, 11008), (16384, 11008, 4096)])
 def test_llama_ffn_full_size(cuda, M, Kd, Nd):
+    """The Llama-7B FFN shapes (gate/up 4096 -> 11008, down 11008 -> 4096) at
+    the sweep's many-row token counts: 256 (the fused-decode GEMM route),
+    4096 and 16384 (the predecode route), against the fp32 torch reference."""
     c = to_cuda(linear_case(M, Kd, Nd, x_dtype=torch.bfloat16, bias=False, seed=1, device="cpu", fanin_scaled=True))
     out, dX, dW, dlut, _ = run_ours(c)
     r_out, r_dX, r_dW, r_dlut = torch_reference(c)
@@ -286,10 +291,12 @@ def test_backward_with_forward_decoded_w(cuda, M, Kd, Nd, dt):
     assert torch.allclose(a[3].float(), b[3].float(), rtol=2 ** -7, atol=0)
 
 
-def test_layer_keeps_decoded_w_for_backward(cuda):
-    """PackRLinear on the many-row route decodes W once per step: forward and
-    gradients equal the explicit forward + backward."""
-    from packr_b200 import PackRLinear
+def test_layer_keeps_decoded_w_for_backward(cuda, monkeypatch):
+    """With PACKR_KEEP_DECODED_W=1, PackRLinear on the many-row route decodes
+    W once per step: forward and gradients equal the explicit forward +
+    backward."""
+    from packr_b200 import PackRLinear, autograd
+    monkeypatch.setattr(autograd, "KEEP_DECODED_W", True)
     M, Kd, Nd = 1024, 512, 1024
     c = to_cuda(linear_case(M, Kd, Nd, x_dtype=torch.bfloat16, bias=True, seed=21))
     layer = PackRLinear(Kd, Nd).to("cuda")
@@ -306,3 +313,27 @@ def test_layer_keeps_decoded_w_for_backward(cuda):
     assert torch.equal(x.grad, dX) and torch.equal(layer.W_f.grad, dW)
     assert torch.allclose(layer.bias_f.grad.float(), dbias.float(), rtol=2 ** -7, atol=0)
     assert torch.allclose(layer.lut.grad, dlut, rtol=1e-5, atol=1e-6 * dlut.abs().max().item())
+
+
+def test_no_decoded_weight_held_between_forward_and_backward(cuda):
+    """By default a PackRLinear holds only its packed weights from forward to
+    backward (the memory budget of the reference's VRAM regression tests,
+    tests/test_vram_regression.py:33-77, at the Llama-7B gate shape and the
+    many-row route): what the forward leaves allocated is its output, not a
+    decoded [K, N] bf16 W (90 MB here)."""
+    from packr_b200 import PackRLinear, autograd
+    assert not autograd.KEEP_DECODED_W
+    M, Kd, Nd = 4096, 4096, 11008
+    lay = PackRLinear.synthetic(Kd, Nd, bias=False, device=cuda, seed=1, lut_std=0.01, wf_std=0.001)
+    x = torch.randn(M, Kd, device=cuda).to(torch.bfloat16).requires_grad_(True)
+    lay.lut_counts()
+    torch.cuda.synchronize()
+    base = torch.cuda.memory_allocated()
+    out = lay(x)
+    torch.cuda.synchronize()
+    held = torch.cuda.memory_allocated() - base
+    wd_bytes = Kd * Nd * 2
+    assert held <= out.numel() * out.element_size() + wd_bytes // 8, held
+    out.backward(torch.randn_like(out))
+    torch.cuda.synchronize()
+    assert lay.W_f.grad is not None and x.grad is not None

@@ -63,6 +63,42 @@ def test_static_scratch_matches_workspace_backward(cuda, dtype, flags):
             assert oracle.max_rel(_f32(g), _f32(w)) <= (TOL_LUT if i == 2 else TOL), (call, i)
 
 
+def _bf16_need(M, K, N, pre, sk_bytes=0):
+    """Scratch bytes of the backward for bf16 x (K % 8 == 0), no split, every
+    gradient wanted, lut counts given: the carve of packr_backward (256-byte
+    aligned pieces: [decoded W, stream-K slots,] bf16 dY, bias sums, lut
+    sums)."""
+    a = lambda v: (v + 255) // 256 * 256
+    r8 = lambda v: (v + 7) // 8 * 8
+    need = (a(K * N * 2) + a(sk_bytes) if pre else 0) + a(M * r8(N) * 2) + a(N * 4) + a(256 * 4)
+    return need
+
+
+@pytest.mark.parametrize("M,K,N,route,near_limit", [
+    (1024, 1024, 1024, "decode-first", False),  # dX from W decoded into the static array
+    (1024, 3584, 3584, "decode-first", True),   # decoded W + bf16 dY just under the array's size
+    (4000, 512, 4096, "fused", True),           # bf16 dY alone just under it: dX decodes W in shared memory
+])
+def test_static_scratch_routes_near_the_limit(cuda, M, K, N, route, near_limit):
+    """The large-row shapes, where the backward picks its dX route by what
+    fits in the array, on two calls in a row against the workspace
+    backward (bf16 x, no split)."""
+    pre_need = _bf16_need(M, K, N, pre=True)
+    assert (pre_need <= STATIC_BYTES) == (route == "decode-first")
+    used = pre_need if route == "decode-first" else _bf16_need(M, K, N, pre=False)
+    assert used <= STATIC_BYTES and (used > 0.95 * STATIC_BYTES) == near_limit
+    lib = _lib.load()
+    for call in range(2):
+        c = {k: (v.cuda() if v is not None else None)
+             for k, v in linear_case(M, K, N, x_dtype=torch.bfloat16, bias=True, seed=10 + call,
+                                     fanin_scaled=True).items()}
+        want = _run(lib, c, static=False, flags=0)
+        got = _run(lib, c, static=True, flags=0)
+        for i, (g, w) in enumerate(zip(got, want)):
+            assert torch.isfinite(g.float()).all(), (call, i)
+            assert oracle.max_rel(_f32(g), _f32(w)) <= (TOL_LUT if i == 2 else TOL), (call, i)
+
+
 def test_static_scratch_rejects_oversized_problems(cuda):
     lib = _lib.load()
     M, K, N = 4096, 64, 8192  # bf16(dY) alone needs 64 MiB > the 32 MiB array
