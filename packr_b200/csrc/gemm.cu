@@ -75,11 +75,22 @@ constexpr int DEC_WARPS_TMA = 8;       // decode warps, TMA-staged path
 constexpr int DEC_THREADS = DEC_WARPS * 32;
 constexpr int CHUNKS = BN_CTA * BK / 8 / DEC_THREADS;  // chunks of 8 weights per thread per stage (ring path)
 constexpr int LUT_BYTES = 256 * 32 * 4;  // one u32 per (entry, lane)
-// lut-gradient histogram copies per CTA (DW).  Copy c is lane-interleaved:
-// bin b of lane l is word b*32 + l, so the 32 lanes of a red.shared always
-// hit 32 different banks.  Epilogue warps 2-5 share copy 0, warps 6-9 copy 1.
+// lut-gradient histogram of the DW epilogue, in fixed point.  Shared f32
+// atomics retire ~1.7 elements per clock per SM on B200 against ~6.5 for
+// 32-bit integer ones (measured), so each tile's f32 dW values are scaled to
+// integers of at most 2^21 relative to the tile's largest |dW| (one shared
+// exponent per tile, agreed by the epilogue warps at a named barrier),
+// added by red.shared.add.u32 into lane-interleaved integer copies (bin b of
+// lane l is word b*32 + l: the 32 lanes of a red always hit 32 banks;
+// epilogue warps 2-5 share copy 0, warps 6-9 copy 1), and after the tile
+// folded into a per-CTA f32 sum per bin (lane l of epilogue warp w owns bin
+// 32w + l).  A word takes at most 512 values per tile (4 warps x 4 chunks x
+// 32), so |word| <= 2^30.  Tiles holding Inf / NaN or only values below
+// 2^-106 add their f32 values to the per-CTA sums directly.
 constexpr int HIST_COPIES = 2;
 constexpr int HIST_COPY_BYTES = 256 * 32 * 4;
+constexpr int HIST_SUM_BYTES = 256 * 4;   // per-CTA f32 bin sums
+constexpr int HIST_XCHG_BYTES = 2 * 8 * 4;  // tile maxima: [tile parity][epilogue warp]
 constexpr int ACC_COLS = BN;
 // Epilogue warps wait a whole mainloop for their accumulator: they poll
 // with the hardware's suspend hint (ns) so their polls do not take issue
@@ -145,7 +156,7 @@ struct Cfg {
   static constexpr int kThreads = kWarps * 32;
   static constexpr bool kAmn = MODE == DW;   // A stored MN-major in smem
   static constexpr bool kBmn = MODE != DX;   // B stored MN-major in smem
-  static constexpr int kHistBytes = HIST_COPIES * HIST_COPY_BYTES;
+  static constexpr int kHistBytes = HIST_COPIES * HIST_COPY_BYTES + HIST_SUM_BYTES + HIST_XCHG_BYTES;
   static constexpr int kLutBytes = kDecode ? LUT_BYTES : 0;
   static constexpr int kAuxBytes = MODE == DW ? kHistBytes : kLutBytes + kStgBytes;
   static constexpr int kBarOff = kStages * kStageBytes + kAuxBytes;
@@ -523,6 +534,8 @@ __global__ void __launch_bounds__(Cfg<MODE, BSRC, MSUB>::kThreads, 1)
     packr_gemm_kernel(const Params P, const __grid_constant__ Maps maps) {
   using C = Cfg<MODE, BSRC, MSUB>;
   constexpr int STAGES = C::kStages;
+  static_assert(C::kSmemBytes <= 227 * 1024, "shared memory per CTA");
+  static_assert(MODE != DW || MSUB == 1, "the DW epilogue's histogram runs per 256-row tile");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte aligned base for the 128-byte-swizzled tiles; offsetting the
   // __shared__ array keeps the compiler emitting shared-memory accesses.
@@ -568,8 +581,8 @@ __global__ void __launch_bounds__(Cfg<MODE, BSRC, MSUB>::kThreads, 1)
     }
   }
   if (MODE == DW && warp >= 2 && warp < C::kDecWarp0) {
-    float* hist = reinterpret_cast<float*>(sAux);
-    for (int i = threadIdx.x - 64; i < C::kHistBytes / 4; i += C::kEpiWarps * 32) hist[i] = 0.0f;
+    uint32_t* hist = reinterpret_cast<uint32_t*>(sAux);
+    for (int i = threadIdx.x - 64; i < C::kHistBytes / 4; i += C::kEpiWarps * 32) hist[i] = 0u;
   }
   if (warp == 1) {
     tmem_alloc_pair(&bars->tmem_base, TMEM_COLS);
@@ -747,14 +760,24 @@ __global__ void __launch_bounds__(Cfg<MODE, BSRC, MSUB>::kThreads, 1)
     if (want_hist && have) fetch_idx(u.tile);
     int t_local = 0;
     bool alive = true;
-    for (; have && alive; ++t_local) {
+    // With the histogram, every epilogue warp takes the per-tile named
+    // barriers of every tile of its schedule, also after an abort (then
+    // without waiting on or reading the accumulator), so that the barrier
+    // sequence of the eight warps always matches.
+    for (; have && (alive || want_hist); ++t_local) {
     const bool have_next = next_unit(sc, un);
     const int tile = u.tile;
     for (int sub = 0; sub < MSUB; ++sub) {
       const int acc = MSUB == 1 ? (t_local & 1) : sub;
       const uint32_t aph = MSUB == 1 ? ((uint32_t)(t_local >> 1) & 1u) : ((uint32_t)t_local & 1u);
       // one lane polls; the warp proceeds only if every lane saw the phase
-      if (!mbar_wait_warp(&bars->tfull[acc], aph, abort_flag, kEpilogueSleepNs)) { alive = false; break; }
+      const bool ready = alive && mbar_wait_warp(&bars->tfull[acc], aph, abort_flag, kEpilogueSleepNs);
+      if (!ready) {
+        alive = false;
+        if (!want_hist) break;
+      }
+      uint32_t hmax = 0;  // DW: this lane's largest |dW| bits of the tile
+      if (ready) {
       if (warp == 2 && lane == 0) PACKR_TRACE_EVENT(4, t_local);
       tc_fence_after();
       const int m0 = (tile % P.m_tiles) * (2 * BM * MSUB) + sub * 2 * BM + (int)rank * BM;
@@ -866,22 +889,89 @@ __global__ void __launch_bounds__(Cfg<MODE, BSRC, MSUB>::kThreads, 1)
           }
           if (warp == 2 && lane == 0) PACKR_TRACE_EVENT(13, (t_local * 2 + sub) * 8 + c);
           if (MODE == DW && want_hist) {
-            const uint32_t w[8] = {wpa[c].x, wpa[c].y, wpa[c].z, wpa[c].w, wpb[c].x, wpb[c].y, wpb[c].z, wpb[c].w};
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              if (j < nval) {
-                const uint32_t bin = (w[j >> 2] >> (8 * (j & 3))) & 0xFFu;
-                asm volatile("red.shared.add.f32 [%0], %1;" ::"r"(hist_lane + bin * 128), "f"(__uint_as_float(v[j]))
-                             : "memory");
-              }
-            }
+            for (int j = 0; j < 32; ++j)
+              if (j < nval) hmax = max(hmax, v[j] & 0x7FFFFFFFu);  // NaN and Inf order above every finite value
           }
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (warp == 2 && lane == 0) PACKR_TRACE_EVENT(5, t_local);
-      if (lane == 0) mbar_arrive_cluster(acc ? tempty1 : tempty0);
+      }  // ready
+      if constexpr (MODE == DW) {
+        if (want_hist) {
+          // tile max |dW| over the eight epilogue warps
+          uint32_t* xchg = reinterpret_cast<uint32_t*>(sAux + HIST_COPIES * HIST_COPY_BYTES + HIST_SUM_BYTES) +
+                           (t_local & 1) * 8;
+          const uint32_t wmax = __reduce_max_sync(0xFFFFFFFFu, hmax);
+          if (lane == 0) xchg[ew] = wmax;
+          asm volatile("bar.sync 1, %0;" ::"n"(C::kEpiWarps * 32) : "memory");
+          uint32_t tmax = 0;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) tmax = max(tmax, xchg[i]);
+          const uint32_t E = tmax >> 23;  // biased exponent of the tile max
+          const bool fixed = tmax != 0 && tmax < 0x7F800000u && E >= 21;
+          float* bin_sum = reinterpret_cast<float*>(sAux + HIST_COPIES * HIST_COPY_BYTES);
+          if (ready && tmax != 0) {
+            // q = RN(dW * 2^(20 - e)) for a tile max in [2^e, 2^(e+1)): |q| <= 2^21,
+            // rounded by adding 1.5 * 2^23 (exact for |dW * scale| < 2^22)
+            const float scale = __int_as_float((int)((274u - E) << 23));
+            const int m0 = (tile % P.m_tiles) * (2 * BM * MSUB) + sub * 2 * BM + (int)rank * BM;
+            const int n0 = (tile / P.m_tiles) * BN;
+#pragma unroll
+            for (int c = 0; c < C::kChunksPerEpiWarp; ++c) {
+              const int cc = cc0 + c;
+              uint32_t v[32];
+              tmem_ld_32x32b_x32(tmem_base + (uint32_t)(acc * ACC_COLS + cc * 32) + ((uint32_t)(q * 32) << 16), v);
+              tmem_ld_wait();
+              const int gn0 = n0 + cc * 32;
+              if (gn0 >= P.Ng || m0 + q * 32 >= P.Mg) continue;
+              const int nval = min(32, P.Ng - gn0);
+              const uint32_t w[8] = {wpa[c].x, wpa[c].y, wpa[c].z, wpa[c].w, wpb[c].x, wpb[c].y, wpb[c].z, wpb[c].w};
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                if (j < nval) {
+                  const uint32_t bin = (w[j >> 2] >> (8 * (j & 3))) & 0xFFu;
+                  if (fixed) {
+                    const int qv = __float_as_int(__fmaf_rn(__uint_as_float(v[j]), scale, 12582912.0f)) - 0x4B400000;
+                    asm volatile("red.shared.add.u32 [%0], %1;" ::"r"(hist_lane + bin * 128), "r"(qv) : "memory");
+                  } else {
+                    asm volatile("red.shared.add.f32 [%0], %1;" ::"r"(smem_u32(bin_sum + bin)),
+                                 "f"(__uint_as_float(v[j]))
+                                 : "memory");
+                  }
+                }
+              }
+            }
+          }
+          if (ready) {
+            tc_fence_before();
+            __syncwarp();
+            if (warp == 2 && lane == 0) PACKR_TRACE_EVENT(5, t_local);
+            if (lane == 0) mbar_arrive_cluster(acc ? tempty1 : tempty0);
+          }
+          asm volatile("bar.sync 1, %0;" ::"n"(C::kEpiWarps * 32) : "memory");
+          if (fixed) {
+            // bin 32 * ew + lane: its 64 integer words (read skewed by lane,
+            // so the warp's loads hit 32 banks), cleared for the next tile
+            uint32_t* words = reinterpret_cast<uint32_t*>(sAux);
+            const int b = ew * 32 + lane;
+            long long sum = 0;
+#pragma unroll 8
+            for (int i = 0; i < HIST_COPIES * 32; ++i) {
+              const int wi = (i >> 5) * (HIST_COPY_BYTES / 4) + b * 32 + ((i + lane) & 31);
+              sum += (int)words[wi];
+              words[wi] = 0u;
+            }
+            const float inv = __int_as_float((int)((E - 20u) << 23));  // 2^(e - 20)
+            bin_sum[b] = __fadd_rn(bin_sum[b], __fmul_rn(__ll2float_rn(sum), inv));
+          }
+        }
+      }
+      if (!(MODE == DW && want_hist) && ready) {
+        tc_fence_before();
+        __syncwarp();
+        if (warp == 2 && lane == 0) PACKR_TRACE_EVENT(5, t_local);
+        if (lane == 0) mbar_arrive_cluster(acc ? tempty1 : tempty0);
+      }
     }
     if (C::kStreamK && alive && u.kind == 1) {  // publish this warp's part of the head partial
       __threadfence();
@@ -895,18 +985,11 @@ __global__ void __launch_bounds__(Cfg<MODE, BSRC, MSUB>::kThreads, 1)
     u = un;
     have = have_next;
     }
-    if (MODE == DW && P.dlut_sum != nullptr) {
+    if (MODE == DW && want_hist && P.dlut_sum != nullptr) {
       asm volatile("bar.sync 1, %0;" ::"n"(C::kEpiWarps * 32) : "memory");
-      // bin b: every copy's 32 lane words, summed across the warp
-      const float* h0 = reinterpret_cast<const float*>(sAux);
-      for (int b = warp - 2; b < 256; b += C::kEpiWarps) {
-        float s = 0.0f;
-#pragma unroll
-        for (int c = 0; c < HIST_COPIES; ++c) s += h0[c * (HIST_COPY_BYTES / 4) + b * 32 + lane];
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
-        if (lane == 0 && s != 0.0f) atomicAdd(P.dlut_sum + b, s);
-      }
+      // this CTA's bin sums (bin 32 * ew + lane) into the launch's
+      const float s = reinterpret_cast<const float*>(sAux + HIST_COPIES * HIST_COPY_BYTES)[ew * 32 + lane];
+      if (alive && s != 0.0f) atomicAdd(P.dlut_sum + ew * 32 + lane, s);
     }
   } else if (C::kDecode && !C::kWtma && warp == C::kSignalWarp) {
     // ------------------------------------------------ decode-completion signaller

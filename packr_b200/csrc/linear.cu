@@ -38,6 +38,10 @@ constexpr long long kSkinnyMaxM = 128;
 inline bool skinny_eligible(long long M, long long N) {
   return M >= PACKR_SKINNY_MIN_M && M <= kSkinnyMaxM && (N & 15) == 0;
 }
+// dX of up to 128 tokens takes the skinny GEMM (W rows as the MMA's 128-row
+// operand, split over N): the 256 x 256 tile GEMM has only K / 256 output
+// tiles there (16 for a 4096-wide layer), which leaves most SMs idle.
+inline bool skinny_dx_eligible(long long M, long long N) { return M >= 1 && M <= kSkinnyMaxM && (N & 15) == 0; }
 
 // FWD / DX take the predecode + plain GEMM route for M >= PACKR_PREDECODE_MIN_M
 // when W's layout allows TMA (N % 16 == 0, 16-byte aligned W_p / W_f) and the
@@ -68,6 +72,7 @@ size_t plan_forward(Carve& c, FwdPlan& p, long long M, long long K, long long N,
 struct BwdPlan {
   uint16_t *dh, *dl, *xh, *xl;
   uint16_t* wd;  // decoded W [K, N] (predecode route for dX only)
+  float* skdx;   // split partial sums of the skinny dX GEMM (few tokens)
   float* skp;    // stream-K partials / flags of the plain dX GEMM
   int* skf;
   float *colsum, *dlut_sum;
@@ -76,9 +81,10 @@ struct BwdPlan {
 
 size_t plan_backward(Carve& c, BwdPlan& p, long long M, long long K, long long N, int x_dtype, int flags,
                      bool want_dx, bool want_dw, bool want_dlut, bool want_dbias, bool have_counts, bool pre,
-                     bool sk = false, bool wd_given = false) {
+                     bool sk = false, bool wd_given = false, bool skdx = false) {
   const bool split = (flags & PACKR_BWD_DW_SPLIT) != 0 && (want_dw || want_dlut);
   p.wd = pre && want_dx && !wd_given ? c.take<uint16_t>((size_t)K * N) : nullptr;
+  p.skdx = skdx && want_dx ? c.take<float>(gemm::skinny_partial_bytes(M, N, K) / sizeof(float)) : nullptr;
   const bool use_sk = sk && pre && want_dx;  // only the plain dX GEMM splits tiles (stream-K)
   const int msub = pre && want_dx ? plain_msub(M) : 1;
   p.skp = use_sk ? c.take<float>(gemm::sk_partial_bytes(sk_pairs(), msub) / sizeof(float)) : nullptr;
@@ -281,7 +287,8 @@ extern "C" size_t packr_backward_workspace_bytes(int64_t M, int64_t K, int64_t N
   M = M > 0 ? M : 0;
   K = K > 0 ? K : 0;
   N = N > 0 ? N : 0;
-  return plan_backward(c, p, M, K, N, x_dtype, flags, true, true, true, true, false, predecode_eligible(M, N), true);
+  return plan_backward(c, p, M, K, N, x_dtype, flags, true, true, true, true, false, predecode_eligible(M, N), true,
+                       false, M > 0 && K > 0 && skinny_dx_eligible(M, N));
 }
 
 namespace packr {
@@ -311,18 +318,20 @@ static int backward_impl(const float* dY, const void* x, int x_dtype, const uint
     if (want_dbias && cudaMemsetAsync(dbias, 0, (size_t)N * 2, s) != cudaSuccess) return PACKR_ERR_CUDA;
     return PACKR_OK;
   }
-  // the richest route the workspace holds (predecode for dX, stream-K)
+  // the richest route the workspace holds (for dX: predecode with stream-K,
+  // predecode, or the skinny GEMM for few tokens; else the fused decode)
   const bool pre_ok = want_dx && predecode_eligible(M, N) && gemm::wtma_ok(W_p, W_f, N);
+  const bool skdx_ok = want_dx && skinny_dx_eligible(M, N) && gemm::wtma_ok(W_p, W_f, N);
   Carve c{static_cast<uint8_t*>(workspace)};
   BwdPlan p;
   bool pre = false;
   size_t need = 0;
-  const bool tries[4][2] = {{true, true}, {true, false}, {false, true}, {false, false}};
+  const bool tries[4][3] = {{true, true, false}, {true, false, false}, {false, false, true}, {false, false, false}};
   for (const auto& t : tries) {
-    if (t[0] && !pre_ok) continue;
+    if ((t[0] && !pre_ok) || (t[2] && !skdx_ok)) continue;
     c = Carve{static_cast<uint8_t*>(workspace)};
     need = plan_backward(c, p, M, K, N, x_dtype, flags, want_dx, want_dw, want_dlut, want_dbias,
-                         lut_counts != nullptr, t[0], t[1], wd_given != nullptr);
+                         lut_counts != nullptr, t[0], t[1], wd_given != nullptr, t[2]);
     pre = t[0];
     if (workspace_bytes >= need) break;
   }
@@ -333,7 +342,10 @@ static int backward_impl(const float* dY, const void* x, int x_dtype, const uint
   // bf16(dY) (+ its residual for the split dW) and the bias gradient sums
   st = prep::split_rows(dY, 1, N, M, N, p.dh, p.dl, ldN, p.colsum, s);
   if (st != PACKR_OK) return st;
-  if (want_dx) {
+  if (want_dx && p.skdx != nullptr) {
+    st = gemm::skinny_dx(p.dh, ldN, W_p, W_f, lut, dX, x_dtype == PACKR_DTYPE_F32, M, K, N, p.skdx, s);
+    if (st != PACKR_OK) return st;
+  } else if (want_dx) {
     gemm::Maps maps;
     if ((st = gemm::make_map(&maps.a[0], p.dh, N, M, ldN * 2, gemm::BM)) != PACKR_OK) return st;
     gemm::Params P{};

@@ -1,16 +1,20 @@
-// Forward for few tokens (up to 128) on the tensor cores, where streaming W
-// from HBM is the bound ("skinny" GEMM):
-//   out^T[n, m] = W^T[n, k] . x^T[k, m]      (kernel.py:133-139 transposed)
-// One CTA per SM (no cluster), tcgen05.mma.cta_group::1 with M = 128 weight
-// columns and N = the padded token count, so no MMA row is wasted on absent
-// tokens.  The A operand is this CTA's 128-column slice of W, staged by TMA
-// (W_f straight into its 128-byte-swizzled MN-major layout, W_p beside it)
-// and decoded in place by the same routine as the large GEMMs; the B operand
-// is the K-major x tile.  Work units are (128-column tile, K split) pairs,
-// walked by a persistent grid; each unit's f32 accumulator (one of two TMEM
-// slots, so a unit's epilogue overlaps the next unit's mainloop) goes to
-// partial[split][m][n] and gemv_reduce_kernel adds the splits in a fixed
-// order plus the bias.  Every wait is bounded like the large GEMMs'.
+// Few-token (up to 128) GEMMs of the forward and of dX on the tensor cores,
+// where streaming W from HBM is the bound ("skinny" GEMMs):
+//   FWD  out^T[n, m] = W^T[n, k] . x^T[k, m]      (kernel.py:133-139 transposed)
+//   DX   dX^T[k, m]  = W[k, n] . bf16(dY)^T[n, m] (autograd.py:70 transposed)
+// One CTA per SM (no cluster), tcgen05.mma.cta_group::1 with M = 128 output
+// features (weight columns for FWD, weight rows for DX) and N = the padded
+// token count, so no MMA row is wasted on absent tokens.  The A operand is
+// this CTA's 128-feature slice of W, staged by TMA (W_f straight into its
+// 128-byte-swizzled layout, MN-major for FWD and K-major for DX, W_p beside
+// it) and decoded in place by the same routine as the large GEMMs; the B
+// operand is the K-major activation tile (x, or bf16(dY) for DX).  Work units
+// are (128-feature tile, reduction split) pairs, walked by a persistent grid;
+// each unit's f32 accumulator (one of two TMEM slots, so a unit's epilogue
+// overlaps the next unit's mainloop) goes to partial[split][m][feature] and a
+// reduce kernel adds the splits in a fixed order (FWD: plus the bias, f32
+// out; DX: rounded to bf16 like the large dX GEMM).  Every wait is bounded
+// like the large GEMMs'.
 #include "common.cuh"
 
 namespace packr {
@@ -19,16 +23,16 @@ namespace gemm {
 // Stage slots of the barrier block.
 constexpr int kSkMaxStages = 6;
 
-template <int NPAD>
+template <int MODE, int NPAD>
 struct SkCfg {
   // as many stages as shared memory holds: under full load a stage's TMA
   // takes ~2.3 us to land, so the ring's depth sets the streaming rate.  (A
   // 16-token MMA width with a lut of two bf16 entries per shared-memory word,
   // which fits 8 stages, measured 14 % slower at 16 tokens on a B200.)
   static constexpr int kStages = NPAD <= 64 ? 6 : NPAD <= 128 ? 4 : 3;
-  static constexpr int kWBytes = BN_CTA * BK * 2;  // W_f / decoded A tile: 64 k x 128 n, two 64-column blocks
+  static constexpr int kWBytes = BN_CTA * BK * 2;  // W_f / decoded A tile: 128 features x 64 reduction
   static constexpr int kXBytes = NPAD * BK * 2;    // x tile: NPAD tokens x 64 k, K-major
-  static constexpr int kPBytes = BN_CTA * BK;      // W_p tile, u8 row-major 64 x 128
+  static constexpr int kPBytes = BN_CTA * BK;      // W_p tile, u8 row-major (FWD 64 x 128, DX 128 x 64)
   static constexpr int kStageBytes = kWBytes + kXBytes + kPBytes;
   static constexpr int kEpiWarps = 4;
   // 16 decode warps (two 8-column chunks per thread and stage): a stage is
@@ -43,7 +47,9 @@ struct SkCfg {
   static constexpr int kLutBytes = LUT_BYTES;
   static constexpr int kBarOff = kStages * kStageBytes + kLutBytes;
   static constexpr int kSmemBytes = kBarOff + 256 + 1024;
-  static constexpr uint32_t kIdesc = idesc_bf16_f32(128, NPAD, /*A MN-major*/ true, /*B MN-major*/ false);
+  // A: W^T (FWD: the tile's rows of W are K, so A is MN-major) or W (DX:
+  // W's rows are the output features and the reduction runs along them: K-major)
+  static constexpr uint32_t kIdesc = idesc_bf16_f32(128, NPAD, /*A MN-major*/ MODE == FWD, /*B MN-major*/ false);
   static constexpr uint32_t kTxBytes = kWBytes + kXBytes + kPBytes;
 };
 
@@ -58,7 +64,7 @@ struct SkBars {
 };
 
 struct SkParams {
-  int M, N, K;
+  int M, N, K;                            // tokens, output features, reduction length
   int n_tiles, k_blocks, splits, kb_per;  // split s: k-blocks [s * kb_per, min(k_blocks, (s + 1) * kb_per))
   float* partial;                         // [splits][M][N]
   Params dec;                             // W bounds for the decode (w_rows = K, w_cols = N)
@@ -68,10 +74,11 @@ struct SkMaps {
   CUtensorMap wf, wp, x;
 };
 
-template <int NPAD>
-__global__ void __launch_bounds__(SkCfg<NPAD>::kThreads, 1)
+template <int MODE, int NPAD>
+__global__ void __launch_bounds__(SkCfg<MODE, NPAD>::kThreads, 1)
     skinny_kernel(const SkParams P, const __grid_constant__ SkMaps maps) {
-  using C = SkCfg<NPAD>;
+  static_assert(MODE == FWD || MODE == DX, "forward or dX");
+  using C = SkCfg<MODE, NPAD>;
   constexpr int S = C::kStages;
   static_assert(S <= kSkMaxStages, "barrier slots");
   static_assert(C::kBarOff + (int)sizeof(SkBars) <= C::kSmemBytes - 1024, "barrier block");
@@ -140,9 +147,14 @@ __global__ void __launch_bounds__(SkCfg<NPAD>::kThreads, 1)
           PACKR_TRACE_EVENT(0, it);
           const int k0 = kk * BK;
           mbar_arrive_expect_tx(&bars->full[s], C::kTxBytes);
-          tma_load_2d(w_tile(s), &maps.wf, &bars->full[s], n0, k0);
-          tma_load_2d(w_tile(s) + 8192, &maps.wf, &bars->full[s], n0 + 64, k0);
-          tma_load_2d(p_tile(s), &maps.wp, &bars->full[s], n0, k0);
+          if (MODE == FWD) {  // W rows k0.., columns n0..n0+127: two 64-column boxes
+            tma_load_2d(w_tile(s), &maps.wf, &bars->full[s], n0, k0);
+            tma_load_2d(w_tile(s) + 8192, &maps.wf, &bars->full[s], n0 + 64, k0);
+            tma_load_2d(p_tile(s), &maps.wp, &bars->full[s], n0, k0);
+          } else {            // W rows n0..n0+127, columns k0..k0+63: one box each
+            tma_load_2d(w_tile(s), &maps.wf, &bars->full[s], k0, n0);
+            tma_load_2d(p_tile(s), &maps.wp, &bars->full[s], k0, n0);
+          }
           tma_load_2d(x_tile(s), &maps.x, &bars->full[s], k0, 0);
         }
       }
@@ -170,7 +182,7 @@ __global__ void __launch_bounds__(SkCfg<NPAD>::kThreads, 1)
           const uint32_t a_s = smem_u32(w_tile(s)), b_s = smem_u32(x_tile(s));
 #pragma unroll
           for (int k = 0; k < BK / UK; ++k) {
-            const uint64_t ad = sdesc_sw128(a_s + k * 2048, 8192, 1024);
+            const uint64_t ad = MODE == FWD ? sdesc_sw128(a_s + k * 2048, 8192, 1024) : sdesc_sw128(a_s + k * 32, 16, 1024);
             const uint64_t bd = sdesc_sw128(b_s + k * 32, 16, 1024);
             umma_bf16_ss(tmem_base + (uint32_t)(acc * NPAD), ad, bd, C::kIdesc, (kk != kb0 || k != 0) ? 1u : 0u);
           }
@@ -182,7 +194,7 @@ __global__ void __launch_bounds__(SkCfg<NPAD>::kThreads, 1)
     }
   } else if (warp < C::kDecWarp0) {
     // ------------------------------------------------ epilogue: partial[split][m][n]
-    const int q = warp & 3;  // TMEM lane quarter = weight columns q*32 .. q*32+31 of the tile
+    const int q = warp & 3;  // TMEM lane quarter = output features q*32 .. q*32+31 of the tile
     int t_local = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++t_local) {
       int n0, split, kb0, kb1;
@@ -224,7 +236,7 @@ __global__ void __launch_bounds__(SkCfg<NPAD>::kThreads, 1)
         const uint32_t ph = (uint32_t)(it / S) & 1u;
         if (!mbar_wait_warp(&bars->full[s], ph, abort_flag)) { ok = false; break; }
         if (t == 0) PACKR_TRACE_EVENT(6, it);
-        decode_in_place<FWD, C::kDecWarps * 32>(P.dec, w_tile(s), p_tile(s), lut_lane, t, n0, kk * BK);
+        decode_in_place<MODE, C::kDecWarps * 32>(P.dec, w_tile(s), p_tile(s), lut_lane, t, n0, kk * BK);
         fence_proxy_async_smem();
         __syncwarp();
         if (t == 0) PACKR_TRACE_EVENT(7, it);
@@ -251,15 +263,16 @@ struct SkPlan {
   int npad, n_tiles, k_blocks, splits, kb_per, grid;
 };
 
-// K splits: the fewest waves of units over the resident CTAs (one per SM),
-// each unit at least 4 k-blocks, the partial sums at most 1/8 of W's bytes.
-inline SkPlan skinny_plan(long long M, long long K, long long N) {
+// Reduction splits (R = reduction length, Out = output features): the fewest
+// waves of units over the resident CTAs (one per SM), each unit at least 4
+// k-blocks, the partial sums at most 1/8 of W's bytes.
+inline SkPlan skinny_plan(long long M, long long R, long long Out) {
   SkPlan p{};
   p.npad = skinny_npad(M);
-  p.n_tiles = (int)((N + BN_CTA - 1) / BN_CTA);
-  p.k_blocks = (int)((K + BK - 1) / BK);
+  p.n_tiles = (int)((Out + BN_CTA - 1) / BN_CTA);
+  p.k_blocks = (int)((R + BK - 1) / BK);
   const int sms = sm_count();
-  long long cap = (3 * K) / (32 * M);  // splits * M * N * 4 <= 3 * K * N / 8
+  long long cap = (3 * R) / (32 * M);  // splits * M * Out * 4 <= 3 * R * Out / 8
   const long long cap_k = p.k_blocks / 4 > 0 ? p.k_blocks / 4 : 1;
   if (cap > cap_k) cap = cap_k;
   if (cap < 1) cap = 1;
@@ -282,42 +295,46 @@ inline SkPlan skinny_plan(long long M, long long K, long long N) {
   return p;
 }
 
-inline size_t skinny_partial_bytes(long long M, long long K, long long N) {
-  const SkPlan p = skinny_plan(M, K, N);
-  return (size_t)p.splits * M * N * sizeof(float);
+inline size_t skinny_partial_bytes(long long M, long long R, long long Out) {
+  const SkPlan p = skinny_plan(M, R, Out);
+  return (size_t)p.splits * M * Out * sizeof(float);
 }
 
-template <int NPAD>
+template <int MODE, int NPAD>
 int skinny_launch(const SkParams& P, const SkMaps& maps, int grid, cudaStream_t st) {
-  using C = SkCfg<NPAD>;
+  using C = SkCfg<MODE, NPAD>;
   static std::once_flag once[64];
   int dev = 0;
   cudaGetDevice(&dev);
   int rc = 0;
   std::call_once(once[dev & 63], [&] {
-    rc = cudaFuncSetAttribute(skinny_kernel<NPAD>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) !=
-         cudaSuccess;
+    rc = cudaFuncSetAttribute(skinny_kernel<MODE, NPAD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              C::kSmemBytes) != cudaSuccess;
   });
   if (rc) return PACKR_ERR_CUDA;
-  skinny_kernel<NPAD><<<grid, C::kThreads, C::kSmemBytes, st>>>(P, maps);
+  skinny_kernel<MODE, NPAD><<<grid, C::kThreads, C::kSmemBytes, st>>>(P, maps);
   return launch_status();
 }
 
-// x_bf16: [M, ldx] bf16 with ldx % 8 == 0; W as for the TMA-staged decode
-// (wtma_ok); partial: skinny_partial_bytes(M, K, N).
-int skinny_forward(const uint16_t* x_bf16, long long ldx, const uint8_t* W_p, const uint16_t* W_f, const float* lut,
-                   const void* bias, int bias_f32, float* out, long long M, long long K, long long N, float* partial,
-                   cudaStream_t st) {
-  const SkPlan pl = skinny_plan(M, K, N);
+// The skinny GEMM's main launch: act_bf16 [M, ld_act] (x for FWD, bf16(dY)
+// for DX; ld_act % 8 == 0), W [K, N] as for the TMA-staged decode (wtma_ok),
+// partial [splits][M][Out].
+template <int MODE>
+int skinny_run(const uint16_t* act_bf16, long long ld_act, const uint8_t* W_p, const uint16_t* W_f, const float* lut,
+               long long M, long long K, long long N, float* partial, SkPlan& pl, cudaStream_t st) {
+  const long long R = MODE == FWD ? K : N, Out = MODE == FWD ? N : K;
+  if (M < 1 || M > 128) return PACKR_ERR_SHAPE;
+  pl = skinny_plan(M, R, Out);
   SkMaps maps;
-  int rc = make_map(&maps.wf, W_f, N, K, N * 2, BK);
-  if (rc == PACKR_OK) rc = make_map_u8(&maps.wp, W_p, N, K, N, BN_CTA, BK);
-  if (rc == PACKR_OK) rc = make_map(&maps.x, x_bf16, K, M, ldx * 2, pl.npad);
+  int rc = MODE == FWD ? make_map(&maps.wf, W_f, N, K, N * 2, BK) : make_map(&maps.wf, W_f, N, K, N * 2, BN_CTA);
+  if (rc == PACKR_OK)
+    rc = MODE == FWD ? make_map_u8(&maps.wp, W_p, N, K, N, BN_CTA, BK) : make_map_u8(&maps.wp, W_p, N, K, N, BK, BN_CTA);
+  if (rc == PACKR_OK) rc = make_map(&maps.x, act_bf16, R, M, ld_act * 2, pl.npad);
   if (rc != PACKR_OK) return rc;
   SkParams P{};
   P.M = (int)M;
-  P.N = (int)N;
-  P.K = (int)K;
+  P.N = (int)Out;
+  P.K = (int)R;
   P.n_tiles = pl.n_tiles;
   P.k_blocks = pl.k_blocks;
   P.splits = pl.splits;
@@ -329,10 +346,48 @@ int skinny_forward(const uint16_t* x_bf16, long long ldx, const uint8_t* W_p, co
   P.dec.ldw = N;
   P.dec.w_rows = (int)K;
   P.dec.w_cols = (int)N;
-  if (M > 128) return PACKR_ERR_SHAPE;
-  rc = pl.npad == 32   ? skinny_launch<32>(P, maps, pl.grid, st)
-       : pl.npad == 64 ? skinny_launch<64>(P, maps, pl.grid, st)
-                       : skinny_launch<128>(P, maps, pl.grid, st);
+  return pl.npad == 32   ? skinny_launch<MODE, 32>(P, maps, pl.grid, st)
+         : pl.npad == 64 ? skinny_launch<MODE, 64>(P, maps, pl.grid, st)
+                         : skinny_launch<MODE, 128>(P, maps, pl.grid, st);
+}
+
+// dX[m, k] = bf16(sum over splits of partial[split][m][k]), summed in split
+// order, stored as bf16 or as the f32 value of that bf16 (f32 x).
+__global__ void __launch_bounds__(256) skinny_reduce_dx_kernel(const float* __restrict__ partial, int splits, int M,
+                                                               int Kout, void* __restrict__ dX, int out_f32) {
+  const int m = blockIdx.y;
+  const long long k = (long long)blockIdx.x * 256 + threadIdx.x;
+  if (k >= Kout) return;
+  const float* p = partial + (long long)m * Kout + k;
+  const long long step = (long long)M * Kout;
+  float s = 0.0f;
+  for (int sp = 0; sp < splits; ++sp) s = __fadd_rn(s, __ldcs(p + sp * step));
+  const uint32_t h = pack_bf16x2_rne(s, 0.0f) & 0xFFFFu;
+  if (out_f32)
+    static_cast<float*>(dX)[(long long)m * Kout + k] = bf16_to_f32(h);
+  else
+    static_cast<uint16_t*>(dX)[(long long)m * Kout + k] = (uint16_t)h;
+}
+
+// dX of few tokens: dY_bf16 [M, ldd] (ldd % 8 == 0), dX [M, K] bf16 or f32;
+// partial: skinny_partial_bytes(M, N, K).
+int skinny_dx(const uint16_t* dY_bf16, long long ldd, const uint8_t* W_p, const uint16_t* W_f, const float* lut,
+              void* dX, int out_f32, long long M, long long K, long long N, float* partial, cudaStream_t st) {
+  SkPlan pl;
+  int rc = skinny_run<DX>(dY_bf16, ldd, W_p, W_f, lut, M, K, N, partial, pl, st);
+  if (rc != PACKR_OK) return rc;
+  skinny_reduce_dx_kernel<<<dim3((unsigned)((K + 255) / 256), (unsigned)M), 256, 0, st>>>(partial, pl.splits, (int)M,
+                                                                                         (int)K, dX, out_f32);
+  return launch_status();
+}
+
+// x_bf16: [M, ldx] bf16 with ldx % 8 == 0; W as for the TMA-staged decode
+// (wtma_ok); partial: skinny_partial_bytes(M, K, N).
+int skinny_forward(const uint16_t* x_bf16, long long ldx, const uint8_t* W_p, const uint16_t* W_f, const float* lut,
+                   const void* bias, int bias_f32, float* out, long long M, long long K, long long N, float* partial,
+                   cudaStream_t st) {
+  SkPlan pl;
+  int rc = skinny_run<FWD>(x_bf16, ldx, W_p, W_f, lut, M, K, N, partial, pl, st);
   if (rc != PACKR_OK) return rc;
   gemv::gemv_reduce_kernel<<<dim3((unsigned)((N + 31) / 32), (unsigned)M), 256, 0, st>>>(partial, pl.splits, (int)M,
                                                                                          (int)N, bias, bias_f32, out,

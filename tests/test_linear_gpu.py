@@ -205,6 +205,8 @@ CASES = [
     (8, 300, 1000, torch.bfloat16, True),      # row bound 8, 4 columns per lane (N % 16 != 0)
     (16, 4096, 11008, torch.bfloat16, True),   # Llama-7B gate/up, decode-bound M
     (16, 11008, 4096, torch.bfloat16, True),   # Llama-7B down
+    (128, 4096, 11008, torch.bfloat16, True),  # skinny dX at its 128-token bound (32 row tiles x N splits)
+    (5, 11008, 4096, torch.float32, True),     # skinny dX with f32 x (dX stored as f32 of bf16)
 ]
 
 
@@ -337,3 +339,66 @@ def test_no_decoded_weight_held_between_forward_and_backward(cuda):
     out.backward(torch.randn_like(out))
     torch.cuda.synchronize()
     assert lay.W_f.grad is not None and x.grad is not None
+
+
+def _dlut_case(M, Kd, Nd, seed, x_scale_rows=None, x_scale=1.0, x_dtype=torch.float32):
+    c = linear_case(M, Kd, Nd, x_dtype=torch.float32, bias=False, seed=seed)
+    x = c["x"] * x_scale
+    if x_scale_rows is not None:
+        x = x * x_scale_rows[None, :]
+    c["x"] = x.to(x_dtype)
+    if x_dtype == torch.bfloat16:
+        c["dY"] = c["dY"].to(torch.bfloat16).float()
+    return c
+
+
+def _dlut_of(c_cpu):
+    c = to_cuda(c_cpu)
+    counts = K.bincount256(c["W_p"])
+    _, _, dlut, _ = K.backward(c["dY"], c["x"], c["W_p"], c["W_f"], c["lut"], counts, False, False, True, False)
+    torch.cuda.synchronize()
+    n = {k: bits(v) for k, v in c_cpu.items() if v is not None}
+    ref = oracle.linear_backward(n["dY"], n["x"], n["W_p"], n["W_f"], n["lut"], has_bias=False,
+                                 x_is_bf16=c_cpu["x"].dtype == torch.bfloat16)
+    return bits(dlut), ref["dlut"]
+
+
+@pytest.mark.parametrize("M,Kd,Nd", [(64, 512, 768), (1, 1024, 1024)])
+def test_dlut_tiles_of_very_different_magnitude(cuda, M, Kd, Nd):
+    """The lut gradient's histogram scales each dW tile by its own largest
+    value: tiles (128-row blocks of K) whose magnitudes differ by up to
+    2^+-30 each keep their precision, bin by bin (error against the bin's
+    sum of |dW| terms, the scale of an f32 accumulation's error)."""
+    scales = torch.tensor([2.0 ** (30 * ((k // 128) % 3 - 1)) for k in range(Kd)], dtype=torch.float32)
+    c = _dlut_case(M, Kd, Nd, seed=3, x_scale_rows=scales)
+    got, ref = _dlut_of(c)
+    n = {k: bits(v) for k, v in c.items() if v is not None}
+    dW = n["x"].astype(np.float64).T @ n["dY"].astype(np.float64)
+    w = n["W_p"].reshape(-1).astype(np.int64)
+    cnt = np.bincount(w, minlength=256).astype(np.float64)
+    abs_sum = np.bincount(w, weights=np.abs(dW).reshape(-1), minlength=256) / (cnt + 1e-8)
+    assert oracle.max_rel(got, ref) <= TOL_LUT
+    assert np.all(np.abs(got.astype(np.float64) - ref) <= 1e-5 * abs_sum + 1e-30)
+
+
+@pytest.mark.parametrize("x_scale", [1e-36, 1e30])
+def test_dlut_extreme_magnitudes(cuda, x_scale):
+    """Tiles whose values all lie below 2^-106 (added in f32 directly) and
+    near the top of the f32 range (scaled down by the tile exponent)."""
+    c = _dlut_case(96, 256, 512, seed=4, x_scale=x_scale)
+    got, ref = _dlut_of(c)
+    assert np.all(np.isfinite(got)) and oracle.max_rel(got, ref) <= TOL_LUT
+
+
+def test_dlut_non_finite_gradient(cuda):
+    """An Inf in dY (bf16 x): the bins holding the affected dW entries become
+    Inf or NaN exactly where the oracle's f32 sums do; the other bins stay
+    within tolerance."""
+    c = _dlut_case(64, 384, 640, seed=5, x_dtype=torch.bfloat16)
+    c["dY"][7, 100] = float("inf")
+    got, ref = _dlut_of(c)
+    fin = np.isfinite(ref)
+    assert np.array_equal(np.isfinite(got), fin)
+    assert np.array_equal(np.isnan(got), np.isnan(ref))
+    assert np.array_equal(np.sign(got[~np.isnan(ref) & ~fin]), np.sign(ref[~np.isnan(ref) & ~fin]))
+    assert oracle.max_rel(got[fin], ref[fin]) <= TOL_LUT
