@@ -266,41 +266,66 @@ __global__ void __launch_bounds__(kThreads, (MB <= 2 ? PACKR_GEMV_MIN_CTAS : 2))
   cluster_sync_all();  // no CTA leaves while a peer may still read its sums
 }
 
-// out[m, n] = sum over splits of partial[s][m][n] + bias[n], in a fixed
-// order: warp w of the CTA sums splits w, w+8, ... (four loads in flight),
-// then the 8 warp sums are added in warp order.  One CTA per 32 columns of
-// one row m.
+// out[m, n] = sum over splits of partial[s][m][n] (added in split order
+// 0, 1, ...) + bias[n].  One thread per 4 consecutive columns of one row:
+// 16-byte loads of the splits, four in flight, and one 16-byte store where
+// N and the output allow it.
 __global__ void __launch_bounds__(256) gemv_reduce_kernel(const float* __restrict__ partial, int splits, int M, int N,
                                                          const void* __restrict__ bias, int bias_f32,
                                                          float* __restrict__ out, long long ld_out) {
-  __shared__ float red[kWarps][32];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int m = blockIdx.y;
-  const long long n = (long long)blockIdx.x * 32 + lane;
-  float s = 0.0f;
-  if (n < N) {
-    const float* p = partial + (long long)m * N + n;
-    const long long step = (long long)M * N;
-    int sp = warp;
-    for (; sp + 3 * kWarps < splits; sp += 4 * kWarps) {
-      const float a = __ldcs(p + sp * step), b = __ldcs(p + (sp + kWarps) * step);
-      const float c = __ldcs(p + (sp + 2 * kWarps) * step), d = __ldcs(p + (sp + 3 * kWarps) * step);
-      s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, a), b), c), d);
+  const long long qpr = (N + 3) / 4;  // column quads per row
+  const long long q = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= (long long)M * qpr) return;
+  const int m = (int)(q / qpr);
+  const int n = (int)(q - (long long)m * qpr) * 4;
+  const int nv = min(4, N - n);
+  const long long step = (long long)M * N;
+  const float* p = partial + (long long)m * N + n;
+  float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  if (nv == 4 && (N & 3) == 0) {  // partial rows are 16-byte aligned
+    auto add4 = [&](const float4 v) {
+      s[0] = __fadd_rn(s[0], v.x);
+      s[1] = __fadd_rn(s[1], v.y);
+      s[2] = __fadd_rn(s[2], v.z);
+      s[3] = __fadd_rn(s[3], v.w);
+    };
+    int sp = 0;
+    for (; sp + 4 <= splits; sp += 4) {
+      const float4 a = __ldcs(reinterpret_cast<const float4*>(p + sp * step));
+      const float4 b = __ldcs(reinterpret_cast<const float4*>(p + (sp + 1) * step));
+      const float4 c = __ldcs(reinterpret_cast<const float4*>(p + (sp + 2) * step));
+      const float4 d = __ldcs(reinterpret_cast<const float4*>(p + (sp + 3) * step));
+      add4(a);
+      add4(b);
+      add4(c);
+      add4(d);
     }
-    for (; sp < splits; sp += kWarps) s = __fadd_rn(s, __ldcs(p + sp * step));
-  }
-  red[warp][lane] = s;
-  __syncthreads();
-  if (warp == 0 && n < N) {
-    float t = red[0][lane];
+    for (; sp < splits; ++sp) add4(__ldcs(reinterpret_cast<const float4*>(p + sp * step)));
+  } else {
+    for (int sp = 0; sp < splits; ++sp)
 #pragma unroll
-    for (int w = 1; w < kWarps; ++w) t = __fadd_rn(t, red[w][lane]);
-    if (bias != nullptr)
-      t = __fadd_rn(t, bias_f32 ? __ldg(static_cast<const float*>(bias) + n)
-                                : bf16_to_f32(__ldg(static_cast<const uint16_t*>(bias) + n)));
-    out[(long long)m * ld_out + n] = t;
+      for (int j = 0; j < 4; ++j)
+        if (j < nv) s[j] = __fadd_rn(s[j], __ldcs(p + sp * step + j));
+  }
+  if (bias != nullptr) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (j < nv)
+        s[j] = __fadd_rn(s[j], bias_f32 ? __ldg(static_cast<const float*>(bias) + n + j)
+                                        : bf16_to_f32(__ldg(static_cast<const uint16_t*>(bias) + n + j)));
+  }
+  float* o = out + (long long)m * ld_out + n;
+  if (nv == 4 && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+    *reinterpret_cast<float4*>(o) = make_float4(s[0], s[1], s[2], s[3]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (j < nv) o[j] = s[j];
   }
 }
+
+// Grid of gemv_reduce_kernel for M rows of N columns.
+inline unsigned reduce_blocks(long long M, long long N) { return (unsigned)((M * ((N + 3) / 4) + 255) / 256); }
 
 inline int row_bound(long long M) { return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : M <= 8 ? 8 : 16; }
 

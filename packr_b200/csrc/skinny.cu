@@ -352,21 +352,44 @@ int skinny_run(const uint16_t* act_bf16, long long ld_act, const uint8_t* W_p, c
 }
 
 // dX[m, k] = bf16(sum over splits of partial[split][m][k]), summed in split
-// order, stored as bf16 or as the f32 value of that bf16 (f32 x).
+// order, stored as bf16 or as the f32 value of that bf16 (f32 x).  One
+// thread per 4 consecutive k of one row (16-byte loads when K % 4 == 0).
 __global__ void __launch_bounds__(256) skinny_reduce_dx_kernel(const float* __restrict__ partial, int splits, int M,
                                                                int Kout, void* __restrict__ dX, int out_f32) {
-  const int m = blockIdx.y;
-  const long long k = (long long)blockIdx.x * 256 + threadIdx.x;
-  if (k >= Kout) return;
-  const float* p = partial + (long long)m * Kout + k;
+  const long long qpr = (Kout + 3) / 4;
+  const long long q = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= (long long)M * qpr) return;
+  const int m = (int)(q / qpr);
+  const int k = (int)(q - (long long)m * qpr) * 4;
+  const int nv = min(4, Kout - k);
   const long long step = (long long)M * Kout;
-  float s = 0.0f;
-  for (int sp = 0; sp < splits; ++sp) s = __fadd_rn(s, __ldcs(p + sp * step));
-  const uint32_t h = pack_bf16x2_rne(s, 0.0f) & 0xFFFFu;
-  if (out_f32)
-    static_cast<float*>(dX)[(long long)m * Kout + k] = bf16_to_f32(h);
-  else
-    static_cast<uint16_t*>(dX)[(long long)m * Kout + k] = (uint16_t)h;
+  const float* p = partial + (long long)m * Kout + k;
+  float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  if (nv == 4 && (Kout & 3) == 0) {
+    for (int sp = 0; sp < splits; ++sp) {
+      const float4 v = __ldcs(reinterpret_cast<const float4*>(p + sp * step));
+      s[0] = __fadd_rn(s[0], v.x);
+      s[1] = __fadd_rn(s[1], v.y);
+      s[2] = __fadd_rn(s[2], v.z);
+      s[3] = __fadd_rn(s[3], v.w);
+    }
+  } else {
+    for (int sp = 0; sp < splits; ++sp)
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (j < nv) s[j] = __fadd_rn(s[j], __ldcs(p + sp * step + j));
+  }
+  const long long o = (long long)m * Kout + k;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    if (j < nv) {
+      const uint32_t h = pack_bf16x2_rne(s[j], 0.0f) & 0xFFFFu;
+      if (out_f32)
+        static_cast<float*>(dX)[o + j] = bf16_to_f32(h);
+      else
+        static_cast<uint16_t*>(dX)[o + j] = (uint16_t)h;
+    }
+  }
 }
 
 // dX of few tokens: dY_bf16 [M, ldd] (ldd % 8 == 0), dX [M, K] bf16 or f32;
@@ -376,8 +399,7 @@ int skinny_dx(const uint16_t* dY_bf16, long long ldd, const uint8_t* W_p, const 
   SkPlan pl;
   int rc = skinny_run<DX>(dY_bf16, ldd, W_p, W_f, lut, M, K, N, partial, pl, st);
   if (rc != PACKR_OK) return rc;
-  skinny_reduce_dx_kernel<<<dim3((unsigned)((K + 255) / 256), (unsigned)M), 256, 0, st>>>(partial, pl.splits, (int)M,
-                                                                                         (int)K, dX, out_f32);
+  skinny_reduce_dx_kernel<<<gemv::reduce_blocks(M, K), 256, 0, st>>>(partial, pl.splits, (int)M, (int)K, dX, out_f32);
   return launch_status();
 }
 
@@ -389,9 +411,8 @@ int skinny_forward(const uint16_t* x_bf16, long long ldx, const uint8_t* W_p, co
   SkPlan pl;
   int rc = skinny_run<FWD>(x_bf16, ldx, W_p, W_f, lut, M, K, N, partial, pl, st);
   if (rc != PACKR_OK) return rc;
-  gemv::gemv_reduce_kernel<<<dim3((unsigned)((N + 31) / 32), (unsigned)M), 256, 0, st>>>(partial, pl.splits, (int)M,
-                                                                                         (int)N, bias, bias_f32, out,
-                                                                                         N);
+  gemv::gemv_reduce_kernel<<<gemv::reduce_blocks(M, N), 256, 0, st>>>(partial, pl.splits, (int)M, (int)N, bias,
+                                                                       bias_f32, out, N);
   return launch_status();
 }
 
