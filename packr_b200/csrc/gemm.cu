@@ -132,17 +132,19 @@ struct Cfg {
   static constexpr bool kWtma = kDecode && BSRC == B_WTMA;
   static constexpr bool kPlainB = MODE != DW && BSRC == B_PLAIN;  // FWD / DX with B by TMA
   static constexpr int kMSub = MSUB;
-  static constexpr int kStages = kWtma ? (MSUB == 2 ? 3 : 4) : (kPlainB && MSUB == 2 ? 4 : (MODE == DW ? 5 : 6));
+  static constexpr int kStages = kWtma ? (MSUB == 2 ? 3 : 4) : (kPlainB && MSUB == 2 ? 4 : (MODE == DW ? 4 : 6));
   static constexpr int kABytes = MSUB * A_BYTES;            // A subtiles per stage
   static constexpr int kWpBytes = kWtma ? BN_CTA * BK : 0;  // u8 W_p tile per stage
   static constexpr int kStageBytes = kABytes + B_BYTES + kWpBytes;
   // DW's histogram epilogue is the heavier one: two warps per TMEM lane
   // quarter, each taking half of the tile's columns.
   static constexpr int kEpiWarps = kDecode ? 4 : 8;
-  // TMA-staged decode modes pass each 32-row output block through a 4 KB
+  // The TMA-fed modes and DW pass each 32-row output block through a 4 KB
   // per-warp shared-memory buffer, so that global stores cover whole rows
-  // segments of 128 (f32) or 64 (bf16) bytes instead of 16 bytes per row.
-  static constexpr bool kStageOut = kWtma || kPlainB;
+  // segments of 128 (f32) or 64 (bf16) bytes instead of 16 bytes per row
+  // (for DW at few tokens, where its epilogue is the bound, the row-per-lane
+  // stores made two half-sector L2 writes per 32 bytes of dW_f).
+  static constexpr bool kStageOut = kWtma || kPlainB || MODE == DW;
   // stream-K code compiled in (used when Params::sk): the plain FWD / DX
   // GEMMs only (for DW the split-tile fix-up measured slower than the wave
   // quantisation it removes)
@@ -158,7 +160,8 @@ struct Cfg {
   static constexpr bool kBmn = MODE != DX;   // B stored MN-major in smem
   static constexpr int kHistBytes = HIST_COPIES * HIST_COPY_BYTES + HIST_SUM_BYTES + HIST_XCHG_BYTES;
   static constexpr int kLutBytes = kDecode ? LUT_BYTES : 0;
-  static constexpr int kAuxBytes = MODE == DW ? kHistBytes : kLutBytes + kStgBytes;
+  static constexpr int kStgOff = MODE == DW ? kHistBytes : kLutBytes;  // staging buffers in the aux region
+  static constexpr int kAuxBytes = kStgOff + kStgBytes;
   static constexpr int kBarOff = kStages * kStageBytes + kAuxBytes;
   static constexpr int kSmemBytes = kBarOff + 256 + 1024;  // barriers + alignment slack
   static constexpr uint32_t kIdesc = idesc_bf16_f32(2 * BM, BN, kAmn, kBmn);
@@ -724,7 +727,7 @@ __global__ void __launch_bounds__(Cfg<MODE, BSRC, MSUB>::kThreads, 1)
     const uint32_t tempty0 = mapa(smem_u32(&bars->tempty[0]), 0);
     const uint32_t tempty1 = mapa(smem_u32(&bars->tempty[1]), 0);
     const uint32_t hist_lane = smem_u32(sAux) + (uint32_t)(((warp - 2) >> 2) * HIST_COPY_BYTES + lane * 4);
-    const uint32_t stg = smem_u32(sAux) + (uint32_t)(C::kLutBytes + (warp - 2) * 4096);
+    const uint32_t stg = smem_u32(sAux) + (uint32_t)(C::kStgOff + (warp - 2) * 4096);
     // DW: the W_p bytes of the next tile's chunks are fetched before its
     // accumulator is ready (they do not depend on it)
     uint4 wpa[C::kChunksPerEpiWarp], wpb[C::kChunksPerEpiWarp];
@@ -734,19 +737,22 @@ __global__ void __launch_bounds__(Cfg<MODE, BSRC, MSUB>::kThreads, 1)
 #pragma unroll
       for (int c = 0; c < C::kChunksPerEpiWarp; ++c) {
         const int gn0 = n0 + (cc0 + c) * 32;
+        if (gn0 + 32 <= P.Ng && (P.ld_out & 15) == 0 && P.idx_vec) {
+          // straight into the registers (a row past W_p reads row 0, whose
+          // values the histogram skips): no merge with zeros, so the loads
+          // stay in flight until the histogram needs them
+          const uint8_t* ip = P.hist_idx + (gm < P.Mg ? gm : 0) * P.ld_out + gn0;
+          wpa[c] = __ldg(reinterpret_cast<const uint4*>(ip));
+          wpb[c] = __ldg(reinterpret_cast<const uint4*>(ip + 16));
+          continue;
+        }
         uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
         if (gm < P.Mg && gn0 < P.Ng) {
           const uint8_t* ip = P.hist_idx + gm * P.ld_out + gn0;
           const int nval = min(32, P.Ng - gn0);
-          if (nval == 32 && (P.ld_out & 15) == 0 && P.idx_vec) {
-            const uint4 a = __ldg(reinterpret_cast<const uint4*>(ip));
-            const uint4 b = __ldg(reinterpret_cast<const uint4*>(ip + 16));
-            w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w; w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
-          } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (j < nval) w[j >> 2] |= (uint32_t)__ldg(ip + j) << (8 * (j & 3));
-          }
+          for (int j = 0; j < 32; ++j)
+            if (j < nval) w[j >> 2] |= (uint32_t)__ldg(ip + j) << (8 * (j & 3));
         }
         wpa[c] = make_uint4(w[0], w[1], w[2], w[3]);
         wpb[c] = make_uint4(w[4], w[5], w[6], w[7]);
@@ -888,7 +894,7 @@ __global__ void __launch_bounds__(Cfg<MODE, BSRC, MSUB>::kThreads, 1)
             }
           }
           if (warp == 2 && lane == 0) PACKR_TRACE_EVENT(13, (t_local * 2 + sub) * 8 + c);
-          if (MODE == DW && want_hist) {
+          if (MODE == DW && want_hist && row_ok) {
 #pragma unroll
             for (int j = 0; j < 32; ++j)
               if (j < nval) hmax = max(hmax, v[j] & 0x7FFFFFFFu);  // NaN and Inf order above every finite value
@@ -924,7 +930,7 @@ __global__ void __launch_bounds__(Cfg<MODE, BSRC, MSUB>::kThreads, 1)
               tmem_ld_wait();
               const int gn0 = n0 + cc * 32;
               if (gn0 >= P.Ng || m0 + q * 32 >= P.Mg) continue;
-              const int nval = min(32, P.Ng - gn0);
+              const int nval = (int)(m0 + q * 32 + lane) < P.Mg ? min(32, P.Ng - gn0) : 0;  // rows past dW: none
               const uint32_t w[8] = {wpa[c].x, wpa[c].y, wpa[c].z, wpa[c].w, wpb[c].x, wpb[c].y, wpb[c].z, wpb[c].w};
 #pragma unroll
               for (int j = 0; j < 32; ++j) {
