@@ -588,8 +588,8 @@ def layer_launches(M: int, K: int, N: int) -> int:
     """libpackr_b200 kernels one PackRLinear forward + backward launches for
     bf16 x (K % 8 == 0), no bias, cached lut counts: forward = [predecode] +
     GEMM; backward = dY split + [predecode] + DX GEMM + DW GEMM + lut finalize.
-    The predecode route is taken from 1024 rows on when N % 16 == 0."""
-    pre = 1 if (M >= 1024 and N % 16 == 0) else 0
+    The predecode route is taken from 129 rows on when N % 16 == 0."""
+    pre = 1 if (M >= 129 and N % 16 == 0) else 0
     return (pre + 1) + (1 + pre + 1 + 1 + 1)
 
 

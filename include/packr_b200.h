@@ -91,8 +91,8 @@ int packr_selfcheck_rounding(unsigned long long* mismatches, void* stream);
 /* ---- PackRLinear ---------------------------------------------------------
  * out[M,N] (f32) = x[M,K] @ W + bias,  W = bf16(W_f + bf16(lut[W_p])),
  * computed on the tensor cores with x and W as bf16 operands and an f32
- * accumulator.  Below 1024 rows W is decoded tile by tile in shared memory
- * and never written to HBM; from 1024 rows on (N % 16 == 0, 16-byte aligned
+ * accumulator.  Below 129 rows W is decoded tile by tile in shared memory
+ * and never written to HBM; from 129 rows on (N % 16 == 0, 16-byte aligned
  * W_p / W_f) W is decoded once into the workspace and read back by TMA,
  * provided the workspace holds it (packr_forward_workspace_bytes counts it;
  * a smaller workspace that fits the fused route selects that route).  For
@@ -135,7 +135,7 @@ int packr_forward_decoded(const void* x, int x_dtype, const uint16_t* Wd, const 
  * [+ x_lo.dY_hi]); without it dY is rounded to bf16 as the reference does for
  * dX.  A workspace of packr_backward_workspace_bytes(M, K, N, x_dtype, flags)
  * bytes (256-byte aligned) holds bf16(dY), its split parts, a bf16 copy of an
- * f32 x, the partial sums and, for dX from 1024 rows on, the decoded W (the
+ * f32 x, the partial sums and, for dX from 129 rows on, the decoded W (the
  * same route choice as packr_forward). */
 #define PACKR_BWD_DW_SPLIT 1
 size_t packr_backward_workspace_bytes(int64_t M, int64_t K, int64_t N, int x_dtype, int flags);
@@ -164,7 +164,7 @@ int packr_predecode_bf16(const uint8_t* W_p, const uint16_t* W_f, const float* l
 
 /* Backward with the caller's decoded W (Wd [K, N] bf16, 16-byte aligned,
  * equal to packr_predecode_bf16(W_p, W_f, lut)): where packr_backward would
- * predecode W for the plain dX GEMM (M >= 1024, N % 16 == 0, 16-byte aligned
+ * predecode W for the plain dX GEMM (M >= 129, N % 16 == 0, 16-byte aligned
  * W_p / W_f) it uses Wd instead; otherwise Wd is ignored.  A forward that
  * predecodes (packr_predecode_bf16 + packr_forward_decoded, which is what
  * packr_forward runs on the same route) can keep its W for the backward and
@@ -231,7 +231,7 @@ int packr_state_v_sums(const packr_vsum_desc* descs, int n, double* sums, void* 
  * Within the array the backward takes the fastest route whose scratch fits,
  * exactly as packr_backward does with a workspace of that size: for dX the
  * decode-first route (W decoded into the array, K*N*2 more bytes, plus the
- * stream-K partial tiles when those fit too) from 1024 rows on, otherwise
+ * stream-K partial tiles when those fit too) from 129 rows on, otherwise
  * the GEMM that decodes W in shared memory.
  * The first successful call on each device looks up the array's device
  * address (make it before any stream capture; a failed lookup is retried by

@@ -97,10 +97,13 @@ constexpr int ACC_COLS = BN;
 // slots from the roles on the critical path.
 constexpr uint32_t kEpilogueSleepNs = 1000;
 // FWD / DX switch from the fused decode to predecode + plain GEMM at this
-// many output rows (tokens): below it the decode traffic of the fused kernel
-// costs less than an extra HBM pass over W.
+// many output rows (tokens), the first count above the skinny GEMM's range.
+// Measured on the Llama-7B FFN layers (fwd+bwd of gate/up/down, same box):
+// M = 129, 192, 256, 512 take 0.97, 0.98, 0.98, 1.09 ms that way against
+// 1.22, 1.23, 1.22, 1.54 ms with the shared-memory decode, whose 256-row
+// tiles number only N / 256 (16 to 43 here) and leave most SMs idle.
 #ifndef PACKR_PREDECODE_MIN_M
-#define PACKR_PREDECODE_MIN_M 1024
+#define PACKR_PREDECODE_MIN_M 129
 #endif
 // Stream-K work split for the GEMMs without a fused decode (1: on).
 #ifndef PACKR_STREAM_K

@@ -44,8 +44,9 @@ inline bool skinny_eligible(long long M, long long N) {
 inline bool skinny_dx_eligible(long long M, long long N) { return M >= 1 && M <= kSkinnyMaxM && (N & 15) == 0; }
 
 // FWD / DX take the predecode + plain GEMM route for M >= PACKR_PREDECODE_MIN_M
-// when W's layout allows TMA (N % 16 == 0, 16-byte aligned W_p / W_f) and the
-// workspace holds the decoded W; otherwise the fused-decode GEMM runs.
+// (129: above the skinny GEMM's range) when W's layout allows TMA (N % 16 ==
+// 0, 16-byte aligned W_p / W_f) and the workspace holds the decoded W;
+// otherwise the fused-decode GEMM runs.
 inline bool predecode_eligible(long long M, long long N) { return M >= PACKR_PREDECODE_MIN_M && (N & 15) == 0; }
 
 // Stream-K scratch (partial tiles and flags) for up to this many CTA pairs.
