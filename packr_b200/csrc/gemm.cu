@@ -197,9 +197,11 @@ struct Params {
   int idx_vec;               // hist_idx base 16-B aligned
   // stream-K (sk = 1): the (tile, k-block) iteration space is cut into equal
   // contiguous ranges, one per CTA pair.  A tile split between pairs p and
-  // p+1: p+1 computes its last k-blocks first ("head") and leaves the f32
-  // partial in sk_partial slot p+1; p computes its first k-blocks last
-  // ("tail"), adds the partial and runs the epilogue.
+  // p+1 (.. p+h when the tiles are fewer than the pairs): each later pair
+  // computes its share of the tile's k-blocks first ("head") and leaves the
+  // f32 partial in its own sk_partial slot; p computes the tile's first
+  // k-blocks last ("tail"), adds the partials in pair order and runs the
+  // epilogue.
   int sk;
   float* sk_partial;         // [pairs][MSUB][2 ranks][256 cols][128 rows]
   int* sk_flags;             // [pairs][2 ranks][epilogue warps], zeroed before the launch
@@ -241,6 +243,14 @@ __device__ __forceinline__ Sched make_sched(const Params& P, int pair, int npair
   s.tile = pair;
   s.step = npairs;
   return s;
+}
+
+// First (tile, k-block) iteration of pair q's stream-K range (make_sched).
+__device__ __forceinline__ long long sk_start(const Params& P, int q, int npairs) {
+  const long long kbt = (long long)P.nseg * P.k_blocks;
+  const long long num_tiles = (long long)P.m_tiles * P.n_tiles;
+  const long long base = (long long)P.sk_dp_tiles * kbt;
+  return base + (num_tiles - P.sk_dp_tiles) * kbt * q / npairs;
 }
 
 __device__ __forceinline__ bool next_unit(Sched& s, Unit& u) {
@@ -769,6 +779,7 @@ __global__ void __launch_bounds__(Cfg<MODE, BSRC, MSUB>::kThreads, 1)
     if (want_hist && have) fetch_idx(u.tile);
     int t_local = 0;
     bool alive = true;
+    int n_heads = 0;  // stream-K: head partials the current tail tile adds
     // With the histogram, every epilogue warp takes the per-tile named
     // barriers of every tile of its schedule, also after an abort (then
     // without waiting on or reading the accumulator), so that the barrier
@@ -795,12 +806,20 @@ __global__ void __launch_bounds__(Cfg<MODE, BSRC, MSUB>::kThreads, 1)
       const bool row_ok = gm < P.Mg;
       // stream-K partial slots ([col][row] f32, this CTA rank's 128 rows)
       float* const my_slot = P.sk_partial + (((size_t)pair * MSUB + sub) * 2 + rank) * (size_t)(BN * BM);
-      const float* const next_slot = P.sk_partial + (((size_t)(pair + 1) * MSUB + sub) * 2 + rank) * (size_t)(BN * BM);
-      if (C::kStreamK && u.kind == 2 && sub == 0) {  // tail: the next pair's head partial must be published
-        if (!wait_flag(P.sk_flags + ((pair + 1) * 2 + (int)rank) * C::kEpiWarps + ew, abort_flag)) {
-          alive = false;
-          break;
+      if (C::kStreamK && u.kind == 2 && sub == 0) {
+        // tail: every following pair whose range starts inside this tile
+        // left a head partial (one pair, or several when a tile spans more
+        // than two ranges); wait until all of them are published
+        const long long tile_end = (long long)(tile + 1) * kb_total;
+        n_heads = 0;
+        for (int q2 = pair + 1; q2 < npairs && sk_start(P, q2, npairs) < tile_end; ++q2) {
+          if (!wait_flag(P.sk_flags + (q2 * 2 + (int)rank) * C::kEpiWarps + ew, abort_flag)) {
+            alive = false;
+            break;
+          }
+          ++n_heads;
         }
+        if (!alive) break;
       }
 #pragma unroll
       for (int c = 0; c < C::kChunksPerEpiWarp; ++c) {
@@ -817,10 +836,14 @@ __global__ void __launch_bounds__(Cfg<MODE, BSRC, MSUB>::kThreads, 1)
           for (int j = 0; j < 32; ++j) __stcg(my_slot + (cc * 32 + j) * BM + row, __uint_as_float(v[j]));
           continue;
         }
-        if (C::kStreamK && u.kind == 2) {
+        if (C::kStreamK && u.kind == 2) {  // the heads' partials, added in pair order
+          for (int h = 1; h <= n_heads; ++h) {
+            const float* const slot =
+                P.sk_partial + (((size_t)(pair + h) * MSUB + sub) * 2 + rank) * (size_t)(BN * BM);
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
-            v[j] = __float_as_uint(__fadd_rn(__uint_as_float(v[j]), __ldcg(next_slot + (cc * 32 + j) * BM + row)));
+            for (int j = 0; j < 32; ++j)
+              v[j] = __float_as_uint(__fadd_rn(__uint_as_float(v[j]), __ldcg(slot + (cc * 32 + j) * BM + row)));
+          }
         }
         if (!C::kStageOut && !row_ok) continue;
         const int nval = min(32, P.Ng - gn0);
@@ -1188,14 +1211,27 @@ int launch_impl(Params P, const Maps& maps, cudaStream_t stream) {
   const int tiles = P.m_tiles * P.n_tiles;
   if (tiles == 0) return PACKR_OK;
   const int max_pairs = resident_pairs[dev & 63];
-  const int pairs = tiles < max_pairs ? tiles : max_pairs;
+  const long long kbt = (long long)P.nseg * P.k_blocks;
+  // Fewer tiles than resident pairs (few output tiles, a long reduction):
+  // every pair takes an equal share of the (tile, k-block) iterations, a
+  // tile's share spanning several pairs whose partials its first pair adds
+  // (measured: the plain forward and dX at 256 rows, 16-43 tiles of the
+  // Llama FFN layers, otherwise leave most SMs idle).
+  const bool sk_all = C::kStreamK && PACKR_STREAM_K && P.sk_partial != nullptr && P.sk_flags != nullptr &&
+                      tiles < max_pairs && max_pairs > 1 && max_pairs <= P.sk_slots && kbt >= 2 &&
+                      (long long)tiles * kbt >= max_pairs;  // every pair a non-empty range (it publishes a flag)
+  const int pairs = sk_all ? max_pairs : (tiles < max_pairs ? tiles : max_pairs);
   cfg.gridDim = dim3(2 * pairs, 1, 1);
   // stream-K when every pair gets at least one tile's worth of k-blocks (so a
   // tile is split between two pairs at most) and the workspace has the slots
   P.sk = 0;
-  if (C::kStreamK && PACKR_STREAM_K && P.sk_partial != nullptr && P.sk_flags != nullptr && pairs > 1 &&
-      pairs <= P.sk_slots) {
-    const long long kbt = (long long)P.nseg * P.k_blocks;
+  if (sk_all) {
+    P.sk = 1;
+    P.sk_dp_tiles = 0;
+    if (cudaMemsetAsync(P.sk_flags, 0, (size_t)pairs * 2 * C::kEpiWarps * sizeof(int), stream) != cudaSuccess)
+      return PACKR_ERR_CUDA;
+  } else if (C::kStreamK && PACKR_STREAM_K && P.sk_partial != nullptr && P.sk_flags != nullptr && pairs > 1 &&
+             pairs <= P.sk_slots) {
     // Only when the last wave of whole tiles would be less than half full:
     // a split tile costs an extra accumulator drain and a partial read, more
     // than a fuller last wave wastes.  Whole waves but the last go
