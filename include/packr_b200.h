@@ -79,6 +79,32 @@ int packr_adam8_multi(const packr_adam_tensor* tensors, int n_tensors, float lr,
                       float beta1, float beta2, float eps, float bc1, float bc2,
                       float weight_decay, void* stream);
 
+/* packr_adam8_multi that also stores every updated parameter value into
+ * n_peers (0..7) other copies of the same tensor: peer_p[i * n_peers + q] is
+ * tensor i's p in the memory of another GPU of this node (a pointer from
+ * packr_ipc_open, plus the tensor's offset in that buffer).  The data-parallel
+ * optimizer uses it to replace the parameter all-gather: each process updates
+ * its 1/N shard and writes it into every other process's parameter buffer in
+ * the same kernel.  The kernel ends with a system-scope fence; the caller
+ * still needs a barrier (e.g. a one-element all-reduce on `stream`) before
+ * other GPUs read the values.  The reference has no counterpart (it has no
+ * distributed code; it replaces no reference interface). */
+int packr_adam8_multi_push(const packr_adam_tensor* tensors, int n_tensors, void* const* peer_p,
+                           int n_peers, float lr, float beta1, float beta2, float eps, float bc1,
+                           float bc2, float weight_decay, void* stream);
+
+/* Buffers shared between the processes of one node (CUDA IPC).  An IPC
+ * handle names a whole cudaMalloc allocation, hence packr_device_alloc.
+ * packr_ipc_open maps another process's buffer into this process on the
+ * current device (peer access enabled on first use); packr_ipc_close unmaps
+ * it.  Host-side calls, synchronous.  No counterpart in the reference. */
+#define PACKR_IPC_HANDLE_BYTES 64
+int packr_device_alloc(size_t bytes, void** ptr);
+int packr_device_free(void* ptr);
+int packr_ipc_export(const void* ptr, void* handle /* PACKR_IPC_HANDLE_BYTES */);
+int packr_ipc_open(const void* handle, void** ptr);
+int packr_ipc_close(void* ptr);
+
 /* Self-check of the short correctly rounded sequences packr_adam8_multi uses
  * on most blocks, against CUDA's IEEE operations, on the current device:
  * mismatches (device, 4 x u64) = [0] reciprocals over every positive normal

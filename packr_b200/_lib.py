@@ -48,6 +48,13 @@ SIGNATURES = {
     "packr_abi_version": (_I32, []),
     "packr_device_status": (_I32, [_VP]),
     "packr_adam8_multi": (_I32, [ctypes.POINTER(AdamTensor), _I32, _F32, _F32, _F32, _F32, _F32, _F32, _F32, _VP]),
+    "packr_adam8_multi_push": (_I32, [ctypes.POINTER(AdamTensor), _I32, ctypes.POINTER(_VP), _I32, _F32, _F32, _F32,
+                                      _F32, _F32, _F32, _F32, _VP]),
+    "packr_device_alloc": (_I32, [_SZ, ctypes.POINTER(_VP)]),
+    "packr_device_free": (_I32, [_VP]),
+    "packr_ipc_export": (_I32, [_VP, _VP]),
+    "packr_ipc_open": (_I32, [_VP, ctypes.POINTER(_VP)]),
+    "packr_ipc_close": (_I32, [_VP]),
     "packr_forward_workspace_bytes": (_SZ, [_I64, _I64, _I64, _I32]),
     "packr_forward": (_I32, [_VP, _I32, _VP, _VP, _VP, _VP, _I32, _VP, _I64, _I64, _I64, _VP, _SZ, _VP]),
     "packr_forward_decoded_workspace_bytes": (_SZ, [_I64, _I64, _I64, _I32]),
@@ -72,6 +79,7 @@ SIGNATURES = {
                                              _I64, _I32, _VP]),
 }
 PACKR_BWD_DW_SPLIT = 1
+PACKR_IPC_HANDLE_BYTES = 64
 
 
 class VSumDesc(ctypes.Structure):

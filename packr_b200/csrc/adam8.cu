@@ -54,6 +54,14 @@ namespace adam {
 constexpr int kQuantBlock = 256;
 constexpr int kMaxTensorsPerLaunch = 96;
 constexpr int kThreads = 256;
+constexpr int kMaxPeers = 7;  // packr_adam8_multi_push: other GPUs of one node
+#ifndef PACKR_ADAM_WAVES
+#define PACKR_ADAM_WAVES 1
+#endif
+// Grid = min(work, resident CTAs x kWaves): more than one wave lets CTAs start
+// on the SMs that another kernel running at the same time (a collective on
+// another stream) leaves free, instead of waiting for that kernel to end.
+constexpr int kWaves = PACKR_ADAM_WAVES;
 
 // Elements per lane: 16 for bf16 parameters (half a warp per block), 8 for
 // f32 (a whole warp per block, to stay within 128 registers).
@@ -76,10 +84,13 @@ struct Slot {
   float* vs;
   long long numel;
   int vec_ok;  // every base pointer allows the 128-bit lane accesses
+  int v8_ok;   // p and every peer copy are 32-byte aligned: one 256-bit store per lane
+  char* peer[kMaxPeers];  // the same parameter in other GPUs' memory (push launches)
 };
 
 struct Launch {
   int n;
+  int n_peers;  // p_new is also stored to Slot::peer[0, n_peers)
   long long block_begin[kMaxTensorsPerLaunch + 1];
   Slot t[kMaxTensorsPerLaunch];
 };
@@ -282,6 +293,21 @@ __device__ __forceinline__ f32x2 raw_pair(const uint4* q, int j) {
   }
 }
 
+// A lane's 32 bytes of parameters in one 256-bit store: a warp's store then
+// covers whole 32-byte sectors (two 128-bit stores leave every sector half
+// written per instruction, which costs twice the NVLink packets when the
+// destination is another GPU's memory).
+__device__ __forceinline__ void st_v8_cs(void* p, const uint32_t* w) {
+  asm volatile("st.global.cs.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(w[0]), "r"(w[1]),
+               "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
+               : "memory");
+}
+__device__ __forceinline__ void st_v8_cg(void* p, const uint32_t* w) {
+  asm volatile("st.global.cg.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(w[0]), "r"(w[1]),
+               "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
+               : "memory");
+}
+
 // Largest tensor index t with block_begin[t] <= b.
 __device__ __forceinline__ int find_tensor(const Launch& L, long long b) {
   int lo = 0, hi = L.n - 1;
@@ -466,7 +492,34 @@ __global__ void __launch_bounds__(kThreads, 2) adam8_kernel(const __grid_constan
       const float d_hi = (sqrt_rn_residual(amax_v * h.inv_bc2) + h.eps) * 2.0f;
       ok = st_lo >= 0x1p-99f && st_lo >= 0x1p-120f * d_hi && st_hi < 0x1p+70f;
     }
-    const bool fast = (__ballot_sync(0xFFFFFFFFu, ok || !live) & blk_mask) == blk_mask;
+    bool fast = (__ballot_sync(0xFFFFFFFFu, ok || !live) & blk_mask) == blk_mask;
+    // A block whose only obstacle is a first moment of exactly +-0 (a zero
+    // gradient on a zero m code: frequent where rank-averaged gradients
+    // cancel exactly) also takes the fast sequences: the same check over the
+    // nonzero |m_new|, and such an element's update is m_new itself, the
+    // IEEE value RN(lr * (+-0 / bc1)) / d = +-0 (Markstein's correction
+    // returns +0 for -0); its code is 0 either way.
+    bool zfix = false;
+    if (__any_sync(0xFFFFFFFFu, !fast)) {
+      float amin_nz = 0x1p+127f;
+#pragma unroll
+      for (int j = 0; j < kPairs; ++j) {
+        float a0, a1;
+        upk2(MN[j], a0, a1);
+        if (2 * j < my_n && a0 != 0.0f) amin_nz = fminf(amin_nz, fabsf(a0));
+        if (2 * j + 1 < my_n && a1 != 0.0f) amin_nz = fminf(amin_nz, fabsf(a1));
+      }
+      bool ok2 = h.fast_ok && amin_nz >= 0x1p-96f && amin_v >= 0x1p-96f && amax_m < 0x1p+100f && amax_v < 0x1p+100f;
+      if (ok2 && h.lr != 0.0f) {
+        const float st_lo = amin_nz * h.lr_bc1 * 0.5f;
+        const float st_hi = amax_m * h.lr_bc1 * 2.0f;
+        const float d_hi = (sqrt_rn_residual(amax_v * h.inv_bc2) + h.eps) * 2.0f;
+        ok2 = st_lo >= 0x1p-99f && st_lo >= 0x1p-120f * d_hi && st_hi < 0x1p+70f;
+      }
+      const bool fz = (__ballot_sync(0xFFFFFFFFu, ok2 || !live) & blk_mask) == blk_mask;
+      zfix = fz && !fast;
+      fast = fast || fz;
+    }
 
     float nms, nvs;
     if (fast) {
@@ -532,7 +585,13 @@ __global__ void __launch_bounds__(kThreads, 2) adam8_kernel(const __grid_constan
           mw[j >> 1] = pack4(cm[0], cm[1], cm[2], cm[3]);
           vw[j >> 1] = pack4(cv[0], cv[1], cv[2], cv[3]);
         }
-        const f32x2 upd = fast_update2(T1, nT2, C);
+        f32x2 upd = fast_update2(T1, nT2, C);
+        if (zfix) {
+          float m0, m1, u0, u1;
+          upk2(MN[j], m0, m1);
+          upk2(upd, u0, u1);
+          upd = pk2(m0 == 0.0f ? m0 : u0, m1 == 0.0f ? m1 : u1);
+        }
         f32x2 P = raw_pair<BF16>(praw, j);
         if (h.wd > 0.0f) P = fma2(C.nlrwd, P, P);
         float p0, p1;
@@ -580,9 +639,21 @@ __global__ void __launch_bounds__(kThreads, 2) adam8_kernel(const __grid_constan
     }
 
     if (cur_vec) {
-      uint4* pp = reinterpret_cast<uint4*>(static_cast<char*>(s.p) + e0 * (BF16 ? 2 : 4));
+      static_assert(Gm::kPw == 2, "32 bytes of parameters per lane");
+      if (s.v8_ok) {
+        st_v8_cs(static_cast<char*>(s.p) + e0 * (BF16 ? 2 : 4), po);
+        // the same store into each peer's copy (NVLink)
+        for (int q = 0; q < L.n_peers; ++q) st_v8_cg(s.peer[q] + e0 * (BF16 ? 2 : 4), po);
+      } else {
+        uint4* pp = reinterpret_cast<uint4*>(static_cast<char*>(s.p) + e0 * (BF16 ? 2 : 4));
 #pragma unroll
-      for (int k = 0; k < Gm::kPw; ++k) __stcs(pp + k, make_uint4(po[4 * k], po[4 * k + 1], po[4 * k + 2], po[4 * k + 3]));
+        for (int k = 0; k < Gm::kPw; ++k) __stcs(pp + k, make_uint4(po[4 * k], po[4 * k + 1], po[4 * k + 2], po[4 * k + 3]));
+        for (int q = 0; q < L.n_peers; ++q) {
+          uint4* qp = reinterpret_cast<uint4*>(s.peer[q] + e0 * (BF16 ? 2 : 4));
+#pragma unroll
+          for (int k = 0; k < Gm::kPw; ++k) __stcg(qp + k, make_uint4(po[4 * k], po[4 * k + 1], po[4 * k + 2], po[4 * k + 3]));
+        }
+      }
       if constexpr (Gm::kMw == 4) {
         __stcs(reinterpret_cast<uint4*>(s.m + e0), make_uint4(mw[0], mw[1], mw[2], mw[3]));
         __stcs(reinterpret_cast<uint4*>(s.v + e0), make_uint4(vw[0], vw[1], vw[2], vw[3]));
@@ -594,10 +665,14 @@ __global__ void __launch_bounds__(kThreads, 2) adam8_kernel(const __grid_constan
 #pragma unroll
       for (int i = 0; i < kEpl; ++i) {
         if (i < my_n) {
-          if constexpr (BF16)
+          if constexpr (BF16) {
             static_cast<uint16_t*>(s.p)[e0 + i] = (uint16_t)(po[i >> 1] >> (16 * (i & 1)));
-          else
+            for (int q = 0; q < L.n_peers; ++q)
+              reinterpret_cast<uint16_t*>(s.peer[q])[e0 + i] = (uint16_t)(po[i >> 1] >> (16 * (i & 1)));
+          } else {
             static_cast<uint32_t*>(s.p)[e0 + i] = po[i];
+            for (int q = 0; q < L.n_peers; ++q) reinterpret_cast<uint32_t*>(s.peer[q])[e0 + i] = po[i];
+          }
           s.m[e0 + i] = (int8_t)((mw[i >> 2] >> (8 * (i & 3))) & 0xFFu);
           s.v[e0 + i] = (int8_t)((vw[i >> 2] >> (8 * (i & 3))) & 0xFFu);
         }
@@ -606,6 +681,10 @@ __global__ void __launch_bounds__(kThreads, 2) adam8_kernel(const __grid_constan
     stage = stage == kStages - 1 ? 0 : stage + 1;
   }
   cp_async_wait<0>();
+  // the stores into other GPUs' memory are ordered before anything this
+  // thread's GPU does after the kernel (the caller's barrier that tells the
+  // peers their copies are complete)
+  if (L.n_peers > 0) __threadfence_system();
 }
 
 Hyper make_hyper(float lr, float beta1, float beta2, float eps, float bc1, float bc2, float weight_decay) {
@@ -693,7 +772,8 @@ __global__ void selfcheck_kernel(unsigned long long* bad, const Hyper h, unsigne
 }
 
 template <bool BF16>
-int launch_dtype(const packr_adam_tensor* tensors, int n_tensors, const Hyper& h, cudaStream_t stream) {
+int launch_dtype(const packr_adam_tensor* tensors, int n_tensors, void* const* peer_p, int n_peers, const Hyper& h,
+                 cudaStream_t stream) {
   // per-device cache; relaxed atomics: concurrent first calls store the same value
   static std::atomic<int> occ[kMaxDevices];
   int dev = 0;
@@ -712,6 +792,7 @@ int launch_dtype(const packr_adam_tensor* tensors, int n_tensors, const Hyper& h
   const int max_ctas = sm_count() * occ_dev;
   const int want_dtype = BF16 ? PACKR_DTYPE_BF16 : PACKR_DTYPE_F32;
   Launch L;
+  L.n_peers = n_peers;
   int i = 0;
   while (i < n_tensors) {
     L.n = 0;
@@ -729,6 +810,12 @@ int launch_dtype(const packr_adam_tensor* tensors, int n_tensors, const Hyper& h
       s.numel = t.numel;
       s.vec_ok = aligned(t.p, 16) && aligned(t.g, 16) && aligned(t.m, 4 * Geo<BF16>::kMw) &&
                  aligned(t.v, 4 * Geo<BF16>::kMw);
+      s.v8_ok = aligned(t.p, 32);
+      for (int q = 0; q < kMaxPeers; ++q) {
+        s.peer[q] = q < n_peers ? static_cast<char*>(peer_p[(size_t)i * n_peers + q]) : nullptr;
+        if (q < n_peers && !aligned(s.peer[q], 16)) s.vec_ok = 0;
+        if (q < n_peers && !aligned(s.peer[q], 32)) s.v8_ok = 0;
+      }
       L.block_begin[L.n] = blocks;
       blocks += (t.numel + kQuantBlock - 1) / kQuantBlock;
       ++L.n;
@@ -737,7 +824,8 @@ int launch_dtype(const packr_adam_tensor* tensors, int n_tensors, const Hyper& h
     L.block_begin[L.n] = blocks;
     const long long per_cta = (long long)(kThreads / 32) * Geo<BF16>::kBpw;
     const long long want = (blocks + per_cta - 1) / per_cta;
-    const int grid = (int)(want < max_ctas ? want : max_ctas);
+    const long long cap = (long long)max_ctas * kWaves;
+    const int grid = (int)(want < cap ? want : cap);
     adam8_kernel<BF16><<<grid, kThreads, kSmem, stream>>>(L, h);
     const int st = launch_status();
     if (st != PACKR_OK) return st;
@@ -748,11 +836,13 @@ int launch_dtype(const packr_adam_tensor* tensors, int n_tensors, const Hyper& h
 }  // namespace adam
 }  // namespace packr
 
-extern "C" int packr_adam8_multi(const packr_adam_tensor* tensors, int n_tensors, float lr, float beta1,
-                                 float beta2, float eps, float bc1, float bc2, float weight_decay,
-                                 void* stream) {
-  using namespace packr;
+namespace packr {
+namespace adam {
+int multi_impl(const packr_adam_tensor* tensors, int n_tensors, void* const* peer_p, int n_peers, float lr,
+               float beta1, float beta2, float eps, float bc1, float bc2, float weight_decay, void* stream) {
   if (n_tensors < 0 || (n_tensors > 0 && tensors == nullptr)) return PACKR_ERR_INVALID_ARGUMENT;
+  if (n_peers < 0 || n_peers > kMaxPeers || (n_peers > 0 && n_tensors > 0 && peer_p == nullptr))
+    return PACKR_ERR_INVALID_ARGUMENT;
   if (n_tensors == 0) return PACKR_OK;
   int st = check_device();
   if (st != PACKR_OK) return st;
@@ -767,13 +857,34 @@ extern "C" int packr_adam8_multi(const packr_adam_tensor* tensors, int n_tensors
     const uintptr_t esz = t.dtype == PACKR_DTYPE_BF16 ? 2 : 4;
     if (!aligned(t.p, esz) || !aligned(t.g, esz) || !aligned(t.m_scale, 4) || !aligned(t.v_scale, 4))
       return PACKR_ERR_ALIGNMENT;
+    for (int q = 0; q < n_peers; ++q) {
+      const void* pq = peer_p[(size_t)i * n_peers + q];
+      if (pq == nullptr) return PACKR_ERR_INVALID_ARGUMENT;
+      if (!aligned(pq, esz)) return PACKR_ERR_ALIGNMENT;
+    }
     (t.dtype == PACKR_DTYPE_BF16 ? any_bf16 : any_f32) = true;
   }
-  const adam::Hyper h = adam::make_hyper(lr, beta1, beta2, eps, bc1, bc2, weight_decay);
+  const Hyper h = make_hyper(lr, beta1, beta2, eps, bc1, bc2, weight_decay);
   cudaStream_t s = as_stream(stream);
-  if (any_bf16 && (st = adam::launch_dtype<true>(tensors, n_tensors, h, s)) != PACKR_OK) return st;
-  if (any_f32 && (st = adam::launch_dtype<false>(tensors, n_tensors, h, s)) != PACKR_OK) return st;
+  if (any_bf16 && (st = launch_dtype<true>(tensors, n_tensors, peer_p, n_peers, h, s)) != PACKR_OK) return st;
+  if (any_f32 && (st = launch_dtype<false>(tensors, n_tensors, peer_p, n_peers, h, s)) != PACKR_OK) return st;
   return PACKR_OK;
+}
+}  // namespace adam
+}  // namespace packr
+
+extern "C" int packr_adam8_multi(const packr_adam_tensor* tensors, int n_tensors, float lr, float beta1,
+                                 float beta2, float eps, float bc1, float bc2, float weight_decay,
+                                 void* stream) {
+  return packr::adam::multi_impl(tensors, n_tensors, nullptr, 0, lr, beta1, beta2, eps, bc1, bc2, weight_decay,
+                                 stream);
+}
+
+extern "C" int packr_adam8_multi_push(const packr_adam_tensor* tensors, int n_tensors, void* const* peer_p,
+                                      int n_peers, float lr, float beta1, float beta2, float eps, float bc1,
+                                      float bc2, float weight_decay, void* stream) {
+  return packr::adam::multi_impl(tensors, n_tensors, peer_p, n_peers, lr, beta1, beta2, eps, bc1, bc2,
+                                 weight_decay, stream);
 }
 
 extern "C" int packr_selfcheck_rounding(unsigned long long* mismatches, void* stream) {

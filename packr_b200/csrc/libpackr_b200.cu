@@ -12,3 +12,4 @@
 #include "static_scratch.cu"
 #include "velvet.cu"
 #include "compress.cu"
+#include "peer.cu"

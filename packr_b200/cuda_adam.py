@@ -52,12 +52,8 @@ def selfcheck_rounding(device="cuda") -> list[int]:
     return [int(v) for v in out.cpu().tolist()]
 
 
-def adam8_launch(entries, lr, b1, b2, eps, bc1, bc2, wd, stream=None) -> None:
-    """Runs packr_adam8_multi over `entries` = [(p, g, m, v, ms, vs), ...] of
-    CUDA tensors on one device.  p/g are bf16 or f32 (same dtype), contiguous."""
-    if not entries:
-        return
-    lib = _lib.load()
+def _adam_tensors(entries):
+    """ctypes packr_adam_tensor array of `entries` and their device."""
     arr = (_lib.AdamTensor * len(entries))()
     dev = None
     for i, (p, g, m, v, ms, vs) in enumerate(entries):
@@ -78,11 +74,41 @@ def adam8_launch(entries, lr, b1, b2, eps, bc1, bc2, wd, stream=None) -> None:
         e.numel = p.numel()
         e.dtype = _lib.PACKR_DTYPE_BF16 if p.dtype == torch.bfloat16 else _lib.PACKR_DTYPE_F32
         e.reserved = 0
+    return arr, dev
+
+
+def adam8_launch(entries, lr, b1, b2, eps, bc1, bc2, wd, stream=None) -> None:
+    """Runs packr_adam8_multi over `entries` = [(p, g, m, v, ms, vs), ...] of
+    CUDA tensors on one device.  p/g are bf16 or f32 (same dtype), contiguous."""
+    if not entries:
+        return
+    lib = _lib.load()
+    arr, dev = _adam_tensors(entries)
     with torch.cuda.device(dev):
         s = stream if stream is not None else torch.cuda.current_stream(dev)
         code = lib.packr_adam8_multi(arr, len(entries), lr, b1, b2, eps, bc1, bc2, wd,
                                      ctypes.c_void_p(s.cuda_stream))
     _lib.check("packr_adam8_multi", code)
+
+
+def adam8_launch_push(entries, peer_ptrs, lr, b1, b2, eps, bc1, bc2, wd, stream=None) -> None:
+    """adam8_launch that also stores entry i's updated values at each device
+    address in peer_ptrs[i] (the same tensor in other GPUs' memory, mapped
+    with packr_ipc_open; every entry has the same number of peers, at most 7)
+    through packr_adam8_multi_push."""
+    if not entries:
+        return
+    n_peers = len(peer_ptrs[0]) if peer_ptrs else 0
+    if len(peer_ptrs) != len(entries) or any(len(q) != n_peers for q in peer_ptrs):
+        raise ValueError("adam8_launch_push: one list of peer addresses per entry, all of one length")
+    lib = _lib.load()
+    arr, dev = _adam_tensors(entries)
+    flat = (ctypes.c_void_p * max(len(entries) * n_peers, 1))(*[a for q in peer_ptrs for a in q])
+    with torch.cuda.device(dev):
+        s = stream if stream is not None else torch.cuda.current_stream(dev)
+        code = lib.packr_adam8_multi_push(arr, len(entries), flat, n_peers, lr, b1, b2, eps, bc1, bc2, wd,
+                                          ctypes.c_void_p(s.cuda_stream))
+    _lib.check("packr_adam8_multi_push", code)
 
 
 class CUDA8BitAdam(torch.optim.Optimizer):

@@ -23,7 +23,15 @@ Step (identical collective sequence on every rank), per bucket:
   3. packr_adam8_multi over the parameter sub-ranges of the shard (the same
      per-block arithmetic as CUDA8BitAdam, so the result equals the
      single-process step on the averaged gradient)
-  4. all_gather_into_tensor           -> every rank holds the new parameters
+  4. every rank receives the new parameters:
+     transport "push" (one node, NCCL, CUDA): the buckets are cudaMalloc
+       buffers shared between the ranks by CUDA IPC; packr_adam8_multi_push
+       stores each updated value into the rank's own bucket and into every
+       other rank's copy over NVLink, and one one-element all-reduce after
+       the last bucket orders those stores before any rank's next read.  No
+       all-gather kernel runs, so nothing competes for SMs with the next
+       step's persistent GEMMs or with AdamW itself;
+     transport "nccl": all_gather_into_tensor per bucket.
 With overlap_grad_reduce=True (world_size > 1) step 2 of a bucket is issued
 asynchronously from a post-accumulate-grad hook as soon as the last gradient
 of the bucket is produced, so it runs on NCCL's stream while the backward of
@@ -35,6 +43,8 @@ optimizer reads the flat gradient buffer itself.
 from __future__ import annotations
 
 import contextlib
+import ctypes
+import socket
 from dataclasses import dataclass, field
 
 import torch
@@ -63,12 +73,46 @@ class _Bucket:
     ms: torch.Tensor | None = None
     vs: torch.Tensor | None = None
     entries: list = field(default_factory=list)  # (p_view, g_view, m, v, ms, vs)
+    peer_ptrs: list = field(default_factory=list)  # push: per entry, its address in every other rank's bucket
+    owner: object = None                          # push: the _DeviceBuffer behind `flat`
     ready: int = 0                                # gradients produced since the last step (overlap mode)
     work: object = None                           # pending reduce-scatter
 
 
 def _round_up(x: int, m: int) -> int:
     return (x + m - 1) // m * m
+
+
+class _DeviceBuffer:
+    """A cudaMalloc allocation (packr_device_alloc: exportable by CUDA IPC as
+    a whole) with the CUDA array interface, so torch.as_tensor views it; the
+    tensor keeps this object, and so the allocation, alive."""
+
+    def __init__(self, nbytes: int, device: torch.device):
+        from . import _lib
+        self._lib = _lib.load()
+        ptr = ctypes.c_void_p()
+        with torch.cuda.device(device):
+            _lib.check("packr_device_alloc", self._lib.packr_device_alloc(nbytes, ctypes.byref(ptr)))
+        self.ptr, self.nbytes, self.device = ptr.value, nbytes, device
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (self.ptr, False),
+                                         "version": 3, "strides": None}
+
+    def tensor(self, dtype: torch.dtype, numel: int) -> torch.Tensor:
+        t = torch.as_tensor(self, device=self.device)[:numel * torch.empty((), dtype=dtype).element_size()]
+        return t.view(dtype).zero_()
+
+    def handle(self) -> bytes:
+        from . import _lib
+        h = ctypes.create_string_buffer(_lib.PACKR_IPC_HANDLE_BYTES)
+        _lib.check("packr_ipc_export", self._lib.packr_ipc_export(ctypes.c_void_p(self.ptr), h))
+        return h.raw
+
+    def __del__(self):
+        if getattr(self, "ptr", None):
+            with torch.cuda.device(self.device):
+                self._lib.packr_device_free(ctypes.c_void_p(self.ptr))
+            self.ptr = None
 
 
 class ShardedAdam8:
@@ -80,7 +124,8 @@ class ShardedAdam8:
     """
 
     def __init__(self, params, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0, process_group=None,
-                 adam_fn=None, bucket_bytes: int = 32 << 20, overlap_grad_reduce: bool = False):
+                 adam_fn=None, bucket_bytes: int = 32 << 20, overlap_grad_reduce: bool = False,
+                 transport: str = "auto"):
         self.params = [p for p in params if p.requires_grad]
         if not self.params:
             raise ValueError("ShardedAdam8: no trainable parameters")
@@ -95,12 +140,22 @@ class ShardedAdam8:
             self.rank = dist.get_rank(self.pg)
         else:
             self.world, self.rank = 1, 0
+        if transport not in ("auto", "push", "nccl"):
+            raise ValueError(f"ShardedAdam8: transport must be 'auto', 'push' or 'nccl', not {transport!r}")
+        custom_adam = adam_fn is not None
         if adam_fn is None:
             from .cuda_adam import adam8_launch
             adam_fn = adam8_launch
         self.adam_fn = adam_fn
-        self.step_count = 0
         self.device = self.params[0].device
+        self.transport = "nccl"
+        if self.world > 1 and transport != "nccl":
+            why = self._push_unavailable(custom_adam)
+            if why is None:
+                self.transport = "push"
+            elif transport == "push":
+                raise RuntimeError(f"ShardedAdam8: transport 'push' unavailable: {why}")
+        self.step_count = 0
         self.buckets: list[_Bucket] = []
         open_bucket: dict[torch.dtype, _Bucket] = {}
         for p in self.params:
@@ -119,17 +174,101 @@ class ShardedAdam8:
             self._build(b)
             for s in b.slots:
                 self._bucket_of[id(s.param)] = b
+        self._peer_maps: list[int] = []
+        if self.transport == "push" and not self._connect_peers():
+            self.transport = "nccl"
+        self._barrier = torch.zeros(1, dtype=torch.int32, device=self.device) if self.transport == "push" else None
         self.overlap = bool(overlap_grad_reduce) and self.world > 1
         self._sync = True
         if self.overlap:
             for p in self.params:
                 p.register_post_accumulate_grad_hook(self._on_grad)
 
+    # -------------------------------------------------------------- transport
+    def _push_unavailable(self, custom_adam: bool):
+        """None when every rank can take the push transport, else the reason
+        (the same answer on every rank: one all_gather_object)."""
+        local = None
+        if custom_adam:
+            local = "a custom adam_fn"
+        elif dist.get_backend(self.pg) != "nccl" or self.device.type != "cuda":
+            local = "needs the NCCL backend and CUDA parameters"
+        elif self.world - 1 > 7:
+            local = "more than 8 ranks"
+        info = [None] * self.world
+        dist.all_gather_object(info, (socket.gethostname(), local), group=self.pg)
+        reasons = [r for _, r in info if r is not None]
+        if reasons:
+            return reasons[0]
+        if len({h for h, _ in info}) != 1:
+            return "ranks on more than one node"
+        return None
+
+    def _connect_peers(self) -> bool:
+        """Exchanges the buckets' IPC handles and maps every other rank's
+        buckets; True when every rank mapped all of them (an all-reduce of
+        the outcome, so the ranks agree)."""
+        from . import _lib
+        lib = _lib.load()
+        mine = [b.owner.handle() for b in self.buckets]
+        everyone = [None] * self.world
+        dist.all_gather_object(everyone, mine, group=self.pg)
+        bases = {}  # (rank, bucket index) -> mapped address
+        ok = True
+        with torch.cuda.device(self.device):
+            for q in range(self.world):
+                if q == self.rank:
+                    continue
+                for i, h in enumerate(everyone[q]):
+                    ptr = ctypes.c_void_p()
+                    if lib.packr_ipc_open(ctypes.create_string_buffer(h, len(h)), ctypes.byref(ptr)) != 0:
+                        ok = False
+                        break
+                    self._peer_maps.append(ptr.value)
+                    bases[(q, i)] = ptr.value
+                if not ok:
+                    break
+        flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=self.device)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=self.pg)
+        if int(flag.item()) == 0:
+            self.close()
+            return False
+        for i, b in enumerate(self.buckets):
+            esz = b.flat.element_size()
+            b.peer_ptrs = [[bases[(q, i)] + off * esz for q in range(self.world) if q != self.rank]
+                           for off in b._entry_offsets]
+        return True
+
+    def close(self) -> None:
+        """Unmaps the other ranks' buckets (push transport); the optimizer
+        then uses the all-gather.  Collective with the push transport: every
+        rank calls it, and it returns when every rank has unmapped, so that no
+        rank frees a bucket another rank still maps."""
+        from . import _lib
+        was_push = self.transport == "push" or bool(self._peer_maps)
+        if self._peer_maps:
+            lib = _lib.load()
+            torch.cuda.synchronize(self.device)
+            with torch.cuda.device(self.device):
+                for ptr in self._peer_maps:
+                    lib.packr_ipc_close(ctypes.c_void_p(ptr))
+            self._peer_maps = []
+        for b in self.buckets:
+            b.peer_ptrs = []
+        self.transport = "nccl"
+        self._barrier = None
+        if was_push and self.world > 1:
+            dist.barrier(group=self.pg)
+
     # -------------------------------------------------------------- layout
     def _build(self, b: _Bucket) -> None:
         total = _round_up(max(b.total, 1), BLOCK * self.world)
         b.total = total
-        b.flat = torch.zeros(total, dtype=b.dtype, device=self.device)
+        if self.transport == "push":
+            b.owner = _DeviceBuffer(total * torch.empty((), dtype=b.dtype).element_size(), self.device)
+            b.flat = b.owner.tensor(b.dtype, total)
+        else:
+            b.flat = torch.zeros(total, dtype=b.dtype, device=self.device)
         b.grad = torch.zeros(total, dtype=b.dtype, device=self.device)
         for s in b.slots:
             b.flat[s.offset:s.offset + s.numel].copy_(s.param.detach().reshape(-1))
@@ -144,6 +283,7 @@ class ShardedAdam8:
         b.vs = torch.ones(shard // BLOCK, dtype=torch.float32, device=self.device)
         # parameter sub-ranges inside this rank's shard; both ends of each
         # range are 256-aligned except a parameter's own last element
+        b._entry_offsets = []
         for s in b.slots:
             a, e = max(s.offset, s0), min(s.offset + s.numel, s0 + shard)
             if a >= e:
@@ -151,6 +291,7 @@ class ShardedAdam8:
             la, le = a - s0, e - s0
             ba, be = la // BLOCK, (le + BLOCK - 1) // BLOCK
             b.entries.append((b.flat[a:e], b.shard_grad[la:le], b.m[la:le], b.v[la:le], b.ms[ba:be], b.vs[ba:be]))
+            b._entry_offsets.append(a)
 
     @property
     def lr(self) -> float:
@@ -213,11 +354,19 @@ class ShardedAdam8:
             if b.work is None:
                 self._launch_reduce(b)
         gathers = []
+        push = self.transport == "push"
+        if push:
+            from .cuda_adam import adam8_launch_push
         for b in self.buckets:
             if self.world > 1:
                 b.work.wait()
             b.work = None
             b.ready = 0
+            if push:
+                if b.entries:
+                    adam8_launch_push(b.entries, b.peer_ptrs, self.lr, b1, b2, self.eps, bc1, bc2,
+                                      self.weight_decay)
+                continue
             if b.entries:
                 self.adam_fn(b.entries, self.lr, b1, b2, self.eps, bc1, bc2, self.weight_decay)
             if self.world > 1:
@@ -225,6 +374,11 @@ class ShardedAdam8:
                 mine = b.flat[self.rank * shard:(self.rank + 1) * shard]
                 src = mine if self.device.type == "cuda" else mine.clone()
                 gathers.append(dist.all_gather_into_tensor(b.flat, src, group=self.pg, async_op=True))
+        if push:
+            # every rank's stores into the others' buckets precede (stream
+            # order, system-scope fence at the end of each AdamW kernel) its
+            # part of this all-reduce, which every rank's stream waits for
+            dist.all_reduce(self._barrier, group=self.pg)
         for w in gathers:
             w.wait()
 

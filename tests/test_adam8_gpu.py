@@ -84,6 +84,37 @@ def test_special_values_vs_oracle(cuda, dtype, nonfinite):
             assert np.array_equal(got[fin], hp[fin]), s
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_zero_first_moments_vs_oracle(cuda, dtype):
+    """Exact zero gradients on zero m codes give first moments of exactly 0
+    in about half of the blocks (as rank-averaged gradients that cancel do);
+    those blocks take the fast sequences with the zero update, and every
+    code, scale and parameter (some of them -0) equals the oracle bit for
+    bit."""
+    n = 65536 + 300
+    p = adam_params(n, dtype=dtype, seed=21, device="cuda")
+    p[5::97] = -0.0
+    st = new_state(n)
+    hp, hm, hv, hms, hvs = np_bits(p), *[np_bits(t) for t in st]
+    lr, b1, b2, eps, wd = 1e-3, 0.9, 0.999, 1e-8, 0.01
+    keep = torch.Generator(device="cpu").manual_seed(3)
+    for s in range(1, 7):
+        bc1, bc2 = oracle.adam8_bias_corrections(b1, b2, s)
+        g = adam_grad(n, s, dtype=dtype, device="cuda", std=1e-2).clone()
+        if s > 1:
+            g[(torch.rand(n, generator=keep) < 0.3).to("cuda")] = 0
+        adam8_launch([(p, g, *st)], lr, b1, b2, eps, bc1, bc2, wd)
+        torch.cuda.synchronize()
+        oracle.adam8_step(hp, np_bits(g), hm, hv, hms, hvs, lr, b1, b2, eps, bc1, bc2, wd)
+        assert np.array_equal(np_bits(st[2]).view(np.uint32), hms.view(np.uint32)), s
+        assert np.array_equal(np_bits(st[3]).view(np.uint32), hvs.view(np.uint32)), s
+        assert np.array_equal(np_bits(st[0]), hm), s
+        assert np.array_equal(np_bits(st[1]), hv), s
+        assert np.array_equal(np_bits(p), hp), s
+    m = torch.from_numpy(hm.astype(np.int32))
+    assert int((m == 0).sum()) > 100  # the case occurred
+
+
 @pytest.mark.parametrize("wd", [0.0, 0.01])
 def test_multi_tensor_bit_exact_vs_oracle(cuda, wd):
     sizes = [1, 7, 255, 256, 257, 4096 + 13, 3 * 256, 100_003]

@@ -1,6 +1,7 @@
 """Data-parallel training over NCCL on 2 GPUs (skipped with fewer): the
 sharded 8-bit AdamW step (reduce-scatter, sm_100a AdamW on the rank's shard,
-all-gather) equals the single-GPU CUDA8BitAdam step on the averaged gradient,
+the new parameters pushed into the other rank's buckets by the AdamW kernel,
+or all-gathered) equals the single-GPU CUDA8BitAdam step on the averaged gradient,
 bit for bit; and a two-layer compressed model trained data-parallel stays
 identical on both ranks and close to single-GPU training on the whole batch."""
 import os
@@ -49,22 +50,28 @@ def _worker(rank, world, port, q):
     try:
         from packr_b200.dp import ShardedAdam8
         from packr_b200.cuda_adam import CUDA8BitAdam
-        # 1. optimizer step vs single GPU on the (exactly) averaged gradient
-        ps = _params(dev)
-        opt = ShardedAdam8(ps, lr=1e-3, weight_decay=0.01)
-        ref = [torch.nn.Parameter(p.detach().clone()) for p in _params(dev)]
-        ropt = CUDA8BitAdam(ref, lr=1e-3, weight_decay=0.01)
-        for s in range(1, 4):
-            for p, gr in zip(ps, _grads(rank, s, dev)):
-                p.grad = gr
-            opt.step()
-            avg = [(sum(_grads(r, s, dev)[i].double() for r in range(world)) / world).to(ref[i].dtype)
-                   for i in range(len(ref))]
-            for p, gr in zip(ref, avg):
-                p.grad = gr
-            ropt.step()
-        torch.cuda.synchronize()
-        exact = all(torch.equal(a.detach(), b.detach()) for a, b in zip(ps, ref))
+        # 1. optimizer step vs single GPU on the (exactly) averaged gradient,
+        #    with the parameters pushed to the peers by the AdamW kernel and
+        #    with the NCCL all-gather
+        exact = True
+        for transport in ("push", "nccl"):
+            ps = _params(dev)
+            opt = ShardedAdam8(ps, lr=1e-3, weight_decay=0.01, transport=transport)
+            exact = exact and opt.transport == transport
+            ref = [torch.nn.Parameter(p.detach().clone()) for p in _params(dev)]
+            ropt = CUDA8BitAdam(ref, lr=1e-3, weight_decay=0.01)
+            for s in range(1, 4):
+                for p, gr in zip(ps, _grads(rank, s, dev)):
+                    p.grad = gr
+                opt.step()
+                avg = [(sum(_grads(r, s, dev)[i].double() for r in range(world)) / world).to(ref[i].dtype)
+                       for i in range(len(ref))]
+                for p, gr in zip(ref, avg):
+                    p.grad = gr
+                ropt.step()
+            torch.cuda.synchronize()
+            exact = exact and all(torch.equal(a.detach(), b.detach()) for a, b in zip(ps, ref))
+            opt.close()
         # 2. two compressed layers trained data-parallel for 3 steps
         from packr_b200 import PackRLinear
         torch.manual_seed(7)
@@ -72,6 +79,7 @@ def _worker(rank, world, port, q):
         mp_ = [p for l in layers for p in (l.W_f, l.lut, l.bias_f)]
         # several buckets, each reduce-scatter started from the gradient hooks
         dopt = ShardedAdam8(mp_, lr=1e-2, bucket_bytes=1 << 14, overlap_grad_reduce=True)
+        same_transport = dopt.transport == "push"  # the default on one node
         gx = torch.Generator().manual_seed(99)
         X = torch.randn(8, 64, generator=gx).to(dev)
         Y = torch.randn(8, 32, generator=gx).to(dev)
@@ -91,7 +99,7 @@ def _worker(rank, world, port, q):
         flat = torch.cat([p.detach().float().reshape(-1) for p in mp_])
         gathered = [torch.empty_like(flat) for _ in range(world)]
         dist.all_gather(gathered, flat)
-        same = all(torch.equal(gathered[0], g) for g in gathered)
+        same = same_transport and all(torch.equal(gathered[0], g) for g in gathered)
         # VelvetController's v means over the sharded state: one all-reduce,
         # the same on every rank, and a controller step sets the same lr
         from packr_b200 import VelvetController
