@@ -166,12 +166,26 @@ def timed(fn, steps: int, warmup: int, world: int, flush=None, warm_seconds: flo
     with CUDA events on the current stream; returns (max-over-ranks total ms,
     per-step ms)."""
     t0 = time.perf_counter()
-    done = 0
-    while done < warmup or time.perf_counter() - t0 < warm_seconds:
+    for _ in range(warmup):
         fn()
-        done += 1
-        if done % 16 == 0:
-            torch.cuda.synchronize()
+    torch.cuda.synchronize()
+    if warm_seconds > 0:
+        # the extra warm-up count is agreed over ranks (MAX): every rank
+        # must take the same collective steps
+        t1 = time.perf_counter()
+        fn()
+        torch.cuda.synchronize()
+        one = max(time.perf_counter() - t1, 1e-6)
+        extra = min(int(math.ceil(max(0.0, warm_seconds - (time.perf_counter() - t0)) / one)), 5000)
+        if world > 1:
+            import torch.distributed as dist
+            t = torch.tensor([extra], device="cuda", dtype=torch.int64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            extra = int(t.item())
+        for i in range(extra):
+            fn()
+            if (i + 1) % 16 == 0:
+                torch.cuda.synchronize()
     torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()

@@ -322,7 +322,8 @@ __device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
   return __byte_perm(__byte_perm(a, b, 0x0040u), __byte_perm(c, d, 0x0040u), 0x5410u);
 }
 
-template <bool BF16>
+// PUSH: also store the new parameters into L.n_peers other GPUs' copies.
+template <bool BF16, bool PUSH>
 __global__ void __launch_bounds__(kThreads, 2) adam8_kernel(const __grid_constant__ Launch L, const Hyper h) {
   using Gm = Geo<BF16>;
   constexpr int kEpl = Gm::kEpl, kLpb = Gm::kLpb, kBpw = Gm::kBpw, kPairs = Gm::kPairs;
@@ -562,7 +563,9 @@ __global__ void __launch_bounds__(kThreads, 2) adam8_kernel(const __grid_constan
     uint4 praw[Gm::kPw];
 #pragma unroll
     for (int k = 0; k < Gm::kPw; ++k) praw[k] = lds_chunk<BF16>(st, Sg::kP, k, lane);
-    if (fast) {
+    // the fast sequences, compiled twice: with the zero-moment select only
+    // for the blocks that need it
+    auto fast_pass = [&](auto zero_moments) {
       const f32x2 yms = splat(rcp_rn_newton(nms)), yvs = splat(rcp_rn_newton(nvs));
       const f32x2 nms2 = splat(-nms), nvs2 = splat(-nvs);
       int cm[4], cv[4];
@@ -586,7 +589,7 @@ __global__ void __launch_bounds__(kThreads, 2) adam8_kernel(const __grid_constan
           vw[j >> 1] = pack4(cv[0], cv[1], cv[2], cv[3]);
         }
         f32x2 upd = fast_update2(T1, nT2, C);
-        if (zfix) {
+        if constexpr (decltype(zero_moments)::value) {
           float m0, m1, u0, u1;
           upk2(MN[j], m0, m1);
           upk2(upd, u0, u1);
@@ -603,6 +606,11 @@ __global__ void __launch_bounds__(kThreads, 2) adam8_kernel(const __grid_constan
           po[2 * j + 1] = __float_as_uint(p1);
         }
       }
+    };
+    if (fast && !zfix) {
+      fast_pass(std::false_type{});
+    } else if (fast) {
+      fast_pass(std::true_type{});
     } else {
       int cm[4], cv[4];
 #pragma unroll
@@ -643,12 +651,13 @@ __global__ void __launch_bounds__(kThreads, 2) adam8_kernel(const __grid_constan
       if (s.v8_ok) {
         st_v8_cs(static_cast<char*>(s.p) + e0 * (BF16 ? 2 : 4), po);
         // the same store into each peer's copy (NVLink)
-        for (int q = 0; q < L.n_peers; ++q) st_v8_cg(s.peer[q] + e0 * (BF16 ? 2 : 4), po);
+        if constexpr (PUSH)
+          for (int q = 0; q < L.n_peers; ++q) st_v8_cg(s.peer[q] + e0 * (BF16 ? 2 : 4), po);
       } else {
         uint4* pp = reinterpret_cast<uint4*>(static_cast<char*>(s.p) + e0 * (BF16 ? 2 : 4));
 #pragma unroll
         for (int k = 0; k < Gm::kPw; ++k) __stcs(pp + k, make_uint4(po[4 * k], po[4 * k + 1], po[4 * k + 2], po[4 * k + 3]));
-        for (int q = 0; q < L.n_peers; ++q) {
+        for (int q = 0; PUSH && q < L.n_peers; ++q) {
           uint4* qp = reinterpret_cast<uint4*>(s.peer[q] + e0 * (BF16 ? 2 : 4));
 #pragma unroll
           for (int k = 0; k < Gm::kPw; ++k) __stcg(qp + k, make_uint4(po[4 * k], po[4 * k + 1], po[4 * k + 2], po[4 * k + 3]));
@@ -667,11 +676,11 @@ __global__ void __launch_bounds__(kThreads, 2) adam8_kernel(const __grid_constan
         if (i < my_n) {
           if constexpr (BF16) {
             static_cast<uint16_t*>(s.p)[e0 + i] = (uint16_t)(po[i >> 1] >> (16 * (i & 1)));
-            for (int q = 0; q < L.n_peers; ++q)
+            for (int q = 0; PUSH && q < L.n_peers; ++q)
               reinterpret_cast<uint16_t*>(s.peer[q])[e0 + i] = (uint16_t)(po[i >> 1] >> (16 * (i & 1)));
           } else {
             static_cast<uint32_t*>(s.p)[e0 + i] = po[i];
-            for (int q = 0; q < L.n_peers; ++q) reinterpret_cast<uint32_t*>(s.peer[q])[e0 + i] = po[i];
+            for (int q = 0; PUSH && q < L.n_peers; ++q) reinterpret_cast<uint32_t*>(s.peer[q])[e0 + i] = po[i];
           }
           s.m[e0 + i] = (int8_t)((mw[i >> 2] >> (8 * (i & 3))) & 0xFFu);
           s.v[e0 + i] = (int8_t)((vw[i >> 2] >> (8 * (i & 3))) & 0xFFu);
@@ -684,7 +693,7 @@ __global__ void __launch_bounds__(kThreads, 2) adam8_kernel(const __grid_constan
   // the stores into other GPUs' memory are ordered before anything this
   // thread's GPU does after the kernel (the caller's barrier that tells the
   // peers their copies are complete)
-  if (L.n_peers > 0) __threadfence_system();
+  if (PUSH) __threadfence_system();
 }
 
 Hyper make_hyper(float lr, float beta1, float beta2, float eps, float bc1, float bc2, float weight_decay) {
@@ -782,10 +791,13 @@ int launch_dtype(const packr_adam_tensor* tensors, int n_tensors, void* const* p
   constexpr int kSmem = Stage<BF16>::kCtaBytes;
   int occ_dev = occ[dev].load(std::memory_order_relaxed);
   if (occ_dev == 0) {
-    if (cudaFuncSetAttribute(adam8_kernel<BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess)
+    if (cudaFuncSetAttribute(adam8_kernel<BF16, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(adam8_kernel<BF16, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) !=
+            cudaSuccess)
       return launch_status();
     int o = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, adam8_kernel<BF16>, kThreads, kSmem) != cudaSuccess || o < 1) o = 1;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, adam8_kernel<BF16, false>, kThreads, kSmem) != cudaSuccess || o < 1) o = 1;
     occ[dev].store(o, std::memory_order_relaxed);
     occ_dev = o;
   }
@@ -826,7 +838,10 @@ int launch_dtype(const packr_adam_tensor* tensors, int n_tensors, void* const* p
     const long long want = (blocks + per_cta - 1) / per_cta;
     const long long cap = (long long)max_ctas * kWaves;
     const int grid = (int)(want < cap ? want : cap);
-    adam8_kernel<BF16><<<grid, kThreads, kSmem, stream>>>(L, h);
+    if (n_peers > 0)
+      adam8_kernel<BF16, true><<<grid, kThreads, kSmem, stream>>>(L, h);
+    else
+      adam8_kernel<BF16, false><<<grid, kThreads, kSmem, stream>>>(L, h);
     const int st = launch_status();
     if (st != PACKR_OK) return st;
   }
