@@ -210,9 +210,14 @@ class ShardedAdam8:
         the outcome, so the ranks agree)."""
         from . import _lib
         lib = _lib.load()
-        mine = [b.owner.handle() for b in self.buckets]
+        try:
+            mine = [b.owner.handle() for b in self.buckets]
+        except RuntimeError:
+            mine = None
         everyone = [None] * self.world
         dist.all_gather_object(everyone, mine, group=self.pg)
+        if any(e is None or len(e) != len(self.buckets) for e in everyone):
+            return False  # the same answer on every rank; nothing mapped yet
         bases = {}  # (rank, bucket index) -> mapped address
         ok = True
         with torch.cuda.device(self.device):
