@@ -210,6 +210,29 @@ def timed(fn, steps: int, warmup: int, world: int, flush=None, warm_seconds: flo
     return max_over_ranks(total, world), ms
 
 
+def write_timeline(step, path: str, rank: int, meta: dict) -> None:
+    """Three more steps under torch.profiler (CUPTI) on every rank; rank 0
+    writes each GPU activity (kernel, copy, memset) as [start_us, dur_us,
+    name, stream] relative to the first, plus `meta`."""
+    from torch.profiler import ProfilerActivity, profile
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(3):
+            step()
+        torch.cuda.synchronize()
+    if rank != 0:
+        return
+    evs = sorted((e.time_range.start, e.time_range.end, e.name, getattr(e, "device_resource_id", -1))
+                 for e in prof.events() if e.device_type.name == "CUDA")
+    t0 = evs[0][0] if evs else 0
+    out = dict(meta, events=[[round(a - t0, 1), round(b - a, 1), n, sid] for a, b, n, sid in evs])
+    d = os.path.dirname(path)
+    if d:
+        os.makedirs(d, exist_ok=True)
+    with open(path, "w") as f:
+        json.dump(out, f)
+
+
 def b2b_ms(fn, reps: int, warm: int = 3, min_seconds: float = 0.0) -> float:
     """Mean device time of one fn() call over `reps` calls launched back to
     back between one pair of CUDA events on the current stream (after `warm`
@@ -624,7 +647,7 @@ def bench_ffn(args, world, rank, peaks, peak_kind):
         layers.append(lay)
     params = [p for lay in layers for p in (lay.W_f, lay.lut)]
     opt = ShardedAdam8(params, lr=2e-5, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01,
-                       overlap_grad_reduce=True)
+                       overlap_grad_reduce=True, transport=getattr(args, "transport", "auto"))
 
     def zero():
         for lay, x in zip(layers, xs):
@@ -646,6 +669,9 @@ def bench_ffn(args, world, rank, peaks, peak_kind):
     ms_step = total_ms / args.steps
     flops = ffn_flops(M)
     value = world * flops / (ms_step * 1e-3) / 1e12
+    if getattr(args, "timeline", None):
+        write_timeline(step, args.timeline, rank, {"n_gpus": world, "transport": opt.transport, "tokens": M,
+                                                  "ms_per_step": ms_step})
     fb_total, _ = timed(fwd_bwd, args.steps, 2, world)
     fb_ms = fb_total / args.steps
     # the forward of the gate layer (predecode + GEMM), then its two kernels
@@ -710,11 +736,14 @@ def bench_ffn(args, world, rank, peaks, peak_kind):
                                f"M={M} tokens per GPU",
                    "step": "forward + backward of the three layers, then the data-parallel 8-bit AdamW update "
                            "(gradient reduce-scatter started per bucket from the gradient hooks during the "
-                           "backward, AdamW on this rank's 1/N state shard, W_f/lut all-gather; "
-                           "no collectives at N=1); value counts the 6*M*K*N GEMM FLOPs",
+                           "backward, AdamW on this rank's 1/N state shard; transport 'push': the AdamW kernel "
+                           "also stores the new W_f/lut shard into every other GPU's copy over NVLink, then one "
+                           "1-element all-reduce; 'nccl': all-gather; no collectives at N=1); value counts the "
+                           "6*M*K*N GEMM FLOPs",
                    "hidden": FFN_HIDDEN, "intermediate": FFN_INTER, "tokens_per_gpu": M,
                    "flops_per_step_per_gpu": flops, "l2": "inputs larger than L2 (~0.9 GB of operands per step)",
-                   "parallelism": f"dp{world}, ZeRO-1 sharded 8-bit optimizer state"},
+                   "parallelism": f"dp{world}, ZeRO-1 sharded 8-bit optimizer state",
+                   "transport": opt.transport if world > 1 else None},
         "fwd_bwd_only": {"tflops": round(world * flops / (fb_ms * 1e-3) / 1e12, 2), "ms_per_step": round(fb_ms, 4)},
         "phases_ms_gate_layer": {"forward": round(f_ms, 4), "forward_gemm": round(g_ms, 4),
                                  "predecode": round(p_ms, 4), "backward": round(b_ms, 4),
@@ -1074,6 +1103,11 @@ def main():
     ap.add_argument("--no-extras", action="store_true",
                     help="ffn: leave out the adam8 / sweep / decode / llama8b keys of the default line")
     ap.add_argument("--no-llama", action="store_true", help="ffn: leave out the llama8b key")
+    ap.add_argument("--transport", default="auto", choices=["auto", "push", "nccl"],
+                    help="ffn, N>1: how ShardedAdam8 hands out the new parameters")
+    ap.add_argument("--timeline", default=None,
+                    help="ffn: after the timed steps, write rank 0's CUPTI timeline of 3 more steps "
+                         "(every kernel and copy: start, duration, stream) to this JSON file")
     ap.add_argument("--profile-once", action="store_true",
                     help="ffn: run each kernel of one gate-layer step once (for ncu captures), print nothing")
     args = ap.parse_args()
