@@ -68,6 +68,8 @@ constexpr int BN = 256;          // MMA N (output columns per tile)
 constexpr int BN_CTA = 128;      // B columns held by each CTA
 constexpr int BK = 64, UK = 16;
 constexpr int MAX_STAGES = 6;
+constexpr int TILE_Q = 4;        // dynamic-tile queue slots
+constexpr int BARS_BYTES = 512;  // shared memory reserved for struct Bars
 constexpr int A_BYTES = BM * BK * 2;      // 16 KB
 constexpr int B_BYTES = BN_CTA * BK * 2;  // 16 KB
 constexpr int DEC_WARPS = 8;           // decode warps, register-ring path (and the decode check)
@@ -108,6 +110,10 @@ constexpr uint32_t kEpilogueSleepNs = 1000;
 // Stream-K work split for the GEMMs without a fused decode (1: on).
 #ifndef PACKR_STREAM_K
 #define PACKR_STREAM_K 1
+#endif
+// Whole tiles of those GEMMs taken from a launch-wide counter (1: on).
+#ifndef PACKR_DYN_TILES
+#define PACKR_DYN_TILES 1
 #endif
 // Plain GEMMs use 512-row pair tiles from this many rows on.
 #ifndef PACKR_PLAIN_MSUB2_MIN_M
@@ -166,7 +172,10 @@ struct Cfg {
   static constexpr int kStgOff = MODE == DW ? kHistBytes : kLutBytes;  // staging buffers in the aux region
   static constexpr int kAuxBytes = kStgOff + kStgBytes;
   static constexpr int kBarOff = kStages * kStageBytes + kAuxBytes;
-  static constexpr int kSmemBytes = kBarOff + 256 + 1024;  // barriers + alignment slack
+  static constexpr int kSmemBytes = kBarOff + BARS_BYTES + 1024;  // barriers + alignment slack
+  // dynamic-tile queue consumers: the odd CTA's producer, the MMA issuer and
+  // every epilogue warp of both CTAs
+  static constexpr int kQConsumers = 2 + 2 * kEpiWarps;
   static constexpr uint32_t kIdesc = idesc_bf16_f32(2 * BM, BN, kAmn, kBmn);
   static constexpr uint32_t kTxBytes = 2 * (kDecode ? kABytes : kABytes + B_BYTES);  // both CTAs
   static constexpr uint32_t kWTxBytes = B_BYTES + kWpBytes;                          // this CTA's W tiles
@@ -207,6 +216,12 @@ struct Params {
   int* sk_flags;             // [pairs][2 ranks][epilogue warps], zeroed before the launch
   int sk_slots;              // pairs the two buffers above have room for (0: no stream-K)
   int sk_dp_tiles;           // with sk: tiles [0, sk_dp_tiles) go round-robin first (whole tiles)
+  // dynamic tiles (plain FWD / DX without stream-K): each pair takes its next
+  // whole tile from this counter (zeroed before the launch), so that pairs
+  // that start late (SMs held by a kernel on another stream, e.g. a
+  // collective) take fewer tiles instead of ending the launch late
+  int dyn;
+  int* tile_counter;
 };
 
 // Workspace for stream-K: partial slots and flags for up to `pairs` CTA pairs.
@@ -292,9 +307,16 @@ struct Bars {
   uint64_t tfull[2];        // accumulator complete                 (count 1)
   uint64_t tempty[2];       // accumulator drained by both CTAs     (count 2*epilogue warps)
   uint64_t drain;           // every MMA complete                   (count 1)
+  // dynamic tiles: the even CTA's producer writes tile numbers into qtile of
+  // both CTAs and arrives on both CTAs' qfull; every other role reads its own
+  // CTA's copy and arrives on the even CTA's qempty
+  uint64_t qfull[TILE_Q];   // tile number published                 (count 1)
+  uint64_t qempty[TILE_Q];  // read by every consumer of both CTAs    (count kQConsumers)
+  int qtile[TILE_Q];        // tile number, or -1 after the last tile
   uint32_t tmem_base;
   int abort;
 };
+static_assert(sizeof(Bars) <= BARS_BYTES, "barrier region");
 
 __device__ __forceinline__ uint32_t bf16x2_add(uint32_t a, uint32_t b) {
   uint32_t d;
@@ -583,6 +605,10 @@ __global__ void __launch_bounds__(Cfg<MODE, BSRC, MSUB>::kThreads, 1)
       mbar_init(&bars->tempty[a], 2 * C::kEpiWarps);
     }
     mbar_init(&bars->drain, 1);
+    for (int r = 0; r < TILE_Q; ++r) {
+      mbar_init(&bars->qfull[r], 1);
+      mbar_init(&bars->qempty[r], C::kQConsumers);
+    }
     bars->abort = 0;
     fence_barrier_init();
   }
@@ -616,6 +642,40 @@ __global__ void __launch_bounds__(Cfg<MODE, BSRC, MSUB>::kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = bars->tmem_base;
 
+  // Dynamic tiles (one thread per role).  Entry i of the pair's sequence sits
+  // in queue slot i % TILE_Q, phase (i / TILE_Q) & 1.
+  const bool dyn = C::kPlainB && P.dyn != 0;
+  // the even CTA's producer: takes the next tile (-1 past the last) and
+  // publishes it to both CTAs; -2 if the kernel aborted
+  auto q_push = [&](int i) -> int {
+    const int slot = i % TILE_Q;
+    const uint32_t ph = (uint32_t)(i / TILE_Q) & 1u;
+    if (!mbar_wait_cluster(&bars->qempty[slot], ph ^ 1u, abort_flag)) return -2;
+    int t = atomicAdd(P.tile_counter, 1);
+    if (t >= num_tiles) t = -1;
+    bars->qtile[slot] = t;
+    st_shared_cluster_u32(mapa(smem_u32(&bars->qtile[slot]), 1), (uint32_t)t);
+    mbar_arrive_release_cluster(mapa(smem_u32(&bars->qfull[slot]), 0));
+    mbar_arrive_release_cluster(mapa(smem_u32(&bars->qfull[slot]), 1));
+    return t;
+  };
+  // any other role: reads entry i from its own CTA's queue and releases the
+  // slot on the even CTA; false if the kernel aborted
+  auto q_pop = [&](int i, int& t) -> bool {
+    const int slot = i % TILE_Q;
+    const uint32_t ph = (uint32_t)(i / TILE_Q) & 1u;
+    if (!mbar_wait_cluster(&bars->qfull[slot], ph, abort_flag)) return false;
+    t = *reinterpret_cast<volatile int*>(&bars->qtile[slot]);
+    mbar_arrive_release_cluster(mapa(smem_u32(&bars->qempty[slot]), 0));
+    return true;
+  };
+  auto whole_tile = [&](int t, Unit& x) {
+    x.tile = t;
+    x.k0 = 0;
+    x.k1 = kb_total;
+    x.kind = 0;
+  };
+
   if (warp == 0) {
     // ------------------------------------------------ TMA producer (both CTAs)
     if (lane == 0) {
@@ -623,7 +683,20 @@ __global__ void __launch_bounds__(Cfg<MODE, BSRC, MSUB>::kThreads, 1)
       bool ok = true;
       Sched sc = make_sched(P, pair, npairs);
       Unit u;
-      while (ok && next_unit(sc, u)) {
+      for (int qi = 0; ok; ++qi) {
+        if (dyn) {
+          int t = -1;
+          if (rank == 0) {
+            t = q_push(qi);
+            if (t == -2) break;
+          } else if (!q_pop(qi, t)) {
+            break;
+          }
+          if (t < 0) break;
+          whole_tile(t, u);
+        } else if (!next_unit(sc, u)) {
+          break;
+        }
         const int tile = u.tile;
         const int m0 = (tile % P.m_tiles) * (2 * BM * MSUB) + (int)rank * BM;
         const int n0 = (tile / P.m_tiles) * BN + (int)rank * BN_CTA;
@@ -685,7 +758,14 @@ __global__ void __launch_bounds__(Cfg<MODE, BSRC, MSUB>::kThreads, 1)
       const uint32_t sA0 = smem_u32(sA), sB0 = smem_u32(sB);
       Sched sc = make_sched(P, pair, npairs);
       Unit u;
-      for (; ok && next_unit(sc, u); ++t_local) {
+      for (; ok; ++t_local) {
+        if (dyn) {
+          int t = -1;
+          if (!q_pop(t_local, t) || t < 0) break;
+          whole_tile(t, u);
+        } else if (!next_unit(sc, u)) {
+          break;
+        }
         // accumulator slots (256 TMEM columns each): MSUB = 1 alternates the
         // two slots between tiles; MSUB = 2 uses slot `sub` for subtile `sub`
         const int acc = MSUB == 1 ? (t_local & 1) : 0;
@@ -775,17 +855,35 @@ __global__ void __launch_bounds__(Cfg<MODE, BSRC, MSUB>::kThreads, 1)
     const int ew = warp - 2;  // epilogue warp index
     Sched sc = make_sched(P, pair, npairs);
     Unit u, un;
-    bool have = next_unit(sc, u);
+    bool alive = true;
+    int qi = 0;
+    // the warp's next unit: lane 0 reads the queue (dynamic tiles), every
+    // lane gets the same answer
+    auto next_any = [&](Unit& x) -> bool {
+      if (!dyn) return next_unit(sc, x);
+      int t = -1, got = 1;
+      if (lane == 0) got = q_pop(qi, t) ? 1 : 0;
+      got = __shfl_sync(0xFFFFFFFFu, got, 0);
+      t = __shfl_sync(0xFFFFFFFFu, t, 0);
+      ++qi;
+      if (!got) alive = false;
+      if (!got || t < 0) return false;
+      whole_tile(t, x);
+      return true;
+    };
+    bool have = next_any(u);
     if (want_hist && have) fetch_idx(u.tile);
     int t_local = 0;
-    bool alive = true;
     int n_heads = 0;  // stream-K: head partials the current tail tile adds
     // With the histogram, every epilogue warp takes the per-tile named
     // barriers of every tile of its schedule, also after an abort (then
     // without waiting on or reading the accumulator), so that the barrier
     // sequence of the eight warps always matches.
     for (; have && (alive || want_hist); ++t_local) {
-    const bool have_next = next_unit(sc, un);
+    // static schedules look one unit ahead (DW fetches the next tile's W_p
+    // early); the queue is read after the tile, so that this warp never
+    // waits for the producer to start a tile while it holds an accumulator
+    bool have_next = dyn ? false : next_unit(sc, un);
     const int tile = u.tile;
     for (int sub = 0; sub < MSUB; ++sub) {
       const int acc = MSUB == 1 ? (t_local & 1) : sub;
@@ -1013,6 +1111,7 @@ __global__ void __launch_bounds__(Cfg<MODE, BSRC, MSUB>::kThreads, 1)
         asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(f), "r"(1) : "memory");
       }
     }
+    if (dyn) have_next = alive && next_any(un);
     if (want_hist && have_next) fetch_idx(un.tile);
     u = un;
     have = have_next;
@@ -1244,6 +1343,15 @@ int launch_impl(Params P, const Maps& maps, cudaStream_t stream) {
       if (cudaMemsetAsync(P.sk_flags, 0, (size_t)pairs * 2 * C::kEpiWarps * sizeof(int), stream) != cudaSuccess)
         return PACKR_ERR_CUDA;
     }
+  }
+  // whole tiles from a counter when there is no stream-K split (the counter
+  // is the first word of the stream-K flags, unused then)
+  P.dyn = 0;
+  P.tile_counter = nullptr;
+  if (C::kPlainB && PACKR_DYN_TILES && !P.sk && P.sk_flags != nullptr && tiles > pairs) {
+    P.dyn = 1;
+    P.tile_counter = P.sk_flags;
+    if (cudaMemsetAsync(P.tile_counter, 0, sizeof(int), stream) != cudaSuccess) return PACKR_ERR_CUDA;
   }
   if (cudaLaunchKernelEx(&cfg, packr_gemm_kernel<MODE, BSRC, MSUB>, P, maps) != cudaSuccess) {
     cudaGetLastError();
