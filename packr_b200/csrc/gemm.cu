@@ -111,6 +111,11 @@ constexpr uint32_t kEpilogueSleepNs = 1000;
 #ifndef PACKR_STREAM_K
 #define PACKR_STREAM_K 1
 #endif
+// Stream-K over the last waves when the last wave of whole tiles would be at
+// most this full (percent of the pairs).
+#ifndef PACKR_SK_LAST_WAVE_PCT
+#define PACKR_SK_LAST_WAVE_PCT 50
+#endif
 // Whole tiles of those GEMMs taken from a launch-wide counter (1: on).
 #ifndef PACKR_DYN_TILES
 #define PACKR_DYN_TILES 1
@@ -1338,7 +1343,8 @@ int launch_impl(Params P, const Maps& maps, cudaStream_t stream) {
     // pair.
     const int waves = tiles / pairs, rem = tiles % pairs;
     P.sk_dp_tiles = waves >= 2 ? (waves - 1) * pairs : 0;
-    if (waves >= 1 && rem != 0 && rem * 2 <= pairs && (long long)(tiles - P.sk_dp_tiles) * kbt / pairs >= kbt) {
+    if (waves >= 1 && rem != 0 && rem * 100 <= pairs * PACKR_SK_LAST_WAVE_PCT &&
+        (long long)(tiles - P.sk_dp_tiles) * kbt / pairs >= kbt) {
       P.sk = 1;
       if (cudaMemsetAsync(P.sk_flags, 0, (size_t)pairs * 2 * C::kEpiWarps * sizeof(int), stream) != cudaSuccess)
         return PACKR_ERR_CUDA;
