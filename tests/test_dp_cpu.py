@@ -280,3 +280,52 @@ def test_cuda8bit_adam_loads_consolidated_state():
     for i in sd["state"]:
         for k in ("m", "v", "m_scale", "v_scale"):
             assert torch.equal(re["state"][i][k], sd["state"][i][k]), (i, k)
+
+
+def _transport_worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        out = {}
+        opt = ShardedAdam8(make_params(), lr=1e-3, adam_fn=oracle_adam_fn)
+        out["auto"] = opt.transport
+        opt = ShardedAdam8(make_params(), lr=1e-3)
+        out["auto_default_adam"] = opt.transport
+        try:
+            ShardedAdam8(make_params(), lr=1e-3, transport="push")
+            out["push"] = "accepted"
+        except RuntimeError as e:
+            out["push"] = str(e)
+        try:
+            ShardedAdam8(make_params(), lr=1e-3, transport="bogus")
+            out["bogus"] = "accepted"
+        except ValueError:
+            out["bogus"] = "ValueError"
+        opt.close()  # nothing mapped: no collective, returns
+        out["closed"] = opt.transport
+        q.put((rank, out))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_transport_selection_on_gloo():
+    """The push transport needs NCCL and CUDA parameters on one node: with
+    gloo every rank agrees on the all-gather ("nccl"), an explicit request for
+    "push" raises on every rank with the reason, and an unknown name raises."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_transport_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r in range(world):
+        o = res[r]
+        assert o["auto"] == "nccl" and o["auto_default_adam"] == "nccl" and o["closed"] == "nccl"
+        assert "unavailable" in o["push"] and "NCCL" in o["push"], o["push"]
+        assert o["bogus"] == "ValueError"
