@@ -74,7 +74,7 @@ class _Bucket:
     vs: torch.Tensor | None = None
     entries: list = field(default_factory=list)  # (p_view, g_view, m, v, ms, vs)
     peer_ptrs: list = field(default_factory=list)  # push: per entry, its address in every other rank's bucket
-    owner: object = None                          # push: the _DeviceBuffer behind `flat`
+    arena_off: int = 0                            # push: byte offset of `flat` in the rank's arena
     ready: int = 0                                # gradients produced since the last step (overlap mode)
     work: object = None                           # pending reduce-scatter
 
@@ -98,8 +98,10 @@ class _DeviceBuffer:
         self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (self.ptr, False),
                                          "version": 3, "strides": None}
 
-    def tensor(self, dtype: torch.dtype, numel: int) -> torch.Tensor:
-        t = torch.as_tensor(self, device=self.device)[:numel * torch.empty((), dtype=dtype).element_size()]
+    def tensor(self, dtype: torch.dtype, numel: int, offset: int = 0) -> torch.Tensor:
+        """Zeroed [numel] `dtype` view starting `offset` bytes in."""
+        esz = torch.empty((), dtype=dtype).element_size()
+        t = torch.as_tensor(self, device=self.device)[offset:offset + numel * esz]
         return t.view(dtype).zero_()
 
     def handle(self) -> bytes:
@@ -171,6 +173,17 @@ class ShardedAdam8:
         self._index = {id(p): i for i, p in enumerate(self.params)}
         self._bucket_of = {}
         for b in self.buckets:
+            b.total = _round_up(max(b.total, 1), BLOCK * self.world)
+        # push: every bucket of this rank in one cudaMalloc arena, so that one
+        # IPC handle per rank maps all of them
+        self._arena = None
+        if self.transport == "push":
+            off = 0
+            for b in self.buckets:
+                b.arena_off = off
+                off = _round_up(off + b.total * torch.empty((), dtype=b.dtype).element_size(), 256)
+            self._arena = _DeviceBuffer(off, self.device)
+        for b in self.buckets:
             self._build(b)
             for s in b.slots:
                 self._bucket_of[id(s.param)] = b
@@ -205,42 +218,40 @@ class ShardedAdam8:
         return None
 
     def _connect_peers(self) -> bool:
-        """Exchanges the buckets' IPC handles and maps every other rank's
-        buckets; True when every rank mapped all of them (an all-reduce of
-        the outcome, so the ranks agree)."""
+        """Exchanges the arenas' IPC handles and maps every other rank's
+        arena; True when every rank mapped all of them (an all-reduce of the
+        outcome, so the ranks agree)."""
         from . import _lib
         lib = _lib.load()
         try:
-            mine = [b.owner.handle() for b in self.buckets]
+            mine = (self._arena.handle(), [b.arena_off for b in self.buckets])
         except RuntimeError:
             mine = None
         everyone = [None] * self.world
         dist.all_gather_object(everyone, mine, group=self.pg)
-        if any(e is None or len(e) != len(self.buckets) for e in everyone):
+        if any(e is None or e[1] != mine[1] for e in everyone):
             return False  # the same answer on every rank; nothing mapped yet
-        bases = {}  # (rank, bucket index) -> mapped address
+        bases = {}  # rank -> mapped address of its arena
         ok = True
         with torch.cuda.device(self.device):
             for q in range(self.world):
                 if q == self.rank:
                     continue
-                for i, h in enumerate(everyone[q]):
-                    ptr = ctypes.c_void_p()
-                    if lib.packr_ipc_open(ctypes.create_string_buffer(h, len(h)), ctypes.byref(ptr)) != 0:
-                        ok = False
-                        break
-                    self._peer_maps.append(ptr.value)
-                    bases[(q, i)] = ptr.value
-                if not ok:
+                h = everyone[q][0]
+                ptr = ctypes.c_void_p()
+                if lib.packr_ipc_open(ctypes.create_string_buffer(h, len(h)), ctypes.byref(ptr)) != 0:
+                    ok = False
                     break
+                self._peer_maps.append(ptr.value)
+                bases[q] = ptr.value
         flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=self.device)
         dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=self.pg)
         if int(flag.item()) == 0:
             self.close()
             return False
-        for i, b in enumerate(self.buckets):
+        for b in self.buckets:
             esz = b.flat.element_size()
-            b.peer_ptrs = [[bases[(q, i)] + off * esz for q in range(self.world) if q != self.rank]
+            b.peer_ptrs = [[bases[q] + b.arena_off + off * esz for q in range(self.world) if q != self.rank]
                            for off in b._entry_offsets]
         return True
 
@@ -267,11 +278,9 @@ class ShardedAdam8:
 
     # -------------------------------------------------------------- layout
     def _build(self, b: _Bucket) -> None:
-        total = _round_up(max(b.total, 1), BLOCK * self.world)
-        b.total = total
-        if self.transport == "push":
-            b.owner = _DeviceBuffer(total * torch.empty((), dtype=b.dtype).element_size(), self.device)
-            b.flat = b.owner.tensor(b.dtype, total)
+        total = b.total
+        if self._arena is not None:
+            b.flat = self._arena.tensor(b.dtype, total, b.arena_off)
         else:
             b.flat = torch.zeros(total, dtype=b.dtype, device=self.device)
         b.grad = torch.zeros(total, dtype=b.dtype, device=self.device)
