@@ -51,6 +51,7 @@ import torch
 import torch.distributed as dist
 
 BLOCK = 256
+AUTO_PUSH_MAX_RANKS = 4
 
 
 @dataclass
@@ -151,7 +152,11 @@ class ShardedAdam8:
         self.adam_fn = adam_fn
         self.device = self.params[0].device
         self.transport = "nccl"
-        if self.world > 1 and transport != "nccl":
+        # "auto" takes the push transport up to AUTO_PUSH_MAX_RANKS ranks, the
+        # sizes it was measured at; above that every GPU must take in 7/8 of
+        # the parameters either way (pushes or all-gather), and the all-gather
+        # is the measured path there
+        if self.world > 1 and (transport == "push" or (transport == "auto" and self.world <= AUTO_PUSH_MAX_RANKS)):
             why = self._push_unavailable(custom_adam)
             if why is None:
                 self.transport = "push"
