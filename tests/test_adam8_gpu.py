@@ -321,3 +321,33 @@ def test_fused_quantized_adam_step_with_closure(cuda):
         for k in ("m", "v", "m_scale", "v_scale"):
             assert torch.equal(fq.state[p][k], ref.state[q][k]), k
     assert fq.step() is None  # without a closure there is no loss to return
+
+
+def test_push_stores_every_copy(cuda):
+    """packr_adam8_multi_push on one GPU with the "peer" copies in local
+    buffers: after each step every copy equals the updated parameter bit for
+    bit (vector stores, ragged tails, an unaligned view, bf16 and f32), and
+    the parameters equal the oracle's."""
+    from packr_b200.cuda_adam import adam8_launch_push
+    sizes = [1, 255, 257, 4096 + 13, 100_003]
+    dtypes = [torch.bfloat16, torch.float32, torch.bfloat16, torch.float32, torch.bfloat16]
+    params = [adam_params(n, dtype=dt, seed=40 + i, device="cuda") for i, (n, dt) in enumerate(zip(sizes, dtypes))]
+    big = adam_params(9000, dtype=torch.bfloat16, seed=99, device="cuda")
+    params.append(big[5:5 + 7000])  # an unaligned view: the element-wise path
+    states = [new_state(p.numel()) for p in params]
+    host = [(np_bits(p), *[np_bits(t) for t in st]) for p, st in zip(params, states)]
+    copies = [[torch.full_like(p, 7.0) for _ in range(3)] for p in params]
+    lr, b1, b2, eps, wd = 1e-3, 0.9, 0.999, 1e-8, 0.01
+    for s in range(1, 4):
+        bc1, bc2 = oracle.adam8_bias_corrections(b1, b2, s)
+        grads = [adam_grad(p.numel(), s + 17 * i, dtype=p.dtype, device="cuda", std=1e-2)
+                 for i, p in enumerate(params)]
+        adam8_launch_push([(p, g, *st) for p, g, st in zip(params, grads, states)],
+                          [[c.data_ptr() for c in cs] for cs in copies], lr, b1, b2, eps, bc1, bc2, wd)
+        torch.cuda.synchronize()
+        for i, (p, g) in enumerate(zip(params, grads)):
+            hp, hm, hv, hms, hvs = host[i]
+            oracle.adam8_step(hp, np_bits(g), hm, hv, hms, hvs, lr, b1, b2, eps, bc1, bc2, wd)
+            assert np.array_equal(np_bits(p), hp), (i, s)
+            for c in copies[i]:
+                assert np.array_equal(np_bits(c), hp), (i, s)
