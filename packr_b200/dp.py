@@ -113,8 +113,11 @@ class _DeviceBuffer:
 
     def __del__(self):
         if getattr(self, "ptr", None):
-            with torch.cuda.device(self.device):
-                self._lib.packr_device_free(ctypes.c_void_p(self.ptr))
+            try:
+                with torch.cuda.device(self.device):
+                    self._lib.packr_device_free(ctypes.c_void_p(self.ptr))
+            except Exception:  # interpreter shutdown: the CUDA context may already be gone
+                pass
             self.ptr = None
 
 
