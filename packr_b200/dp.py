@@ -24,8 +24,9 @@ Step (identical collective sequence on every rank), per bucket:
      per-block arithmetic as CUDA8BitAdam, so the result equals the
      single-process step on the averaged gradient)
   4. every rank receives the new parameters:
-     transport "push" (one node, NCCL, CUDA): the buckets are cudaMalloc
-       buffers shared between the ranks by CUDA IPC; packr_adam8_multi_push
+     transport "push" (one node, NCCL, CUDA; "auto" takes it for 2-4
+       ranks): a rank's buckets sit in one cudaMalloc arena that the other
+       ranks map by CUDA IPC; packr_adam8_multi_push
        stores each updated value into the rank's own bucket and into every
        other rank's copy over NVLink, and one one-element all-reduce after
        the last bucket orders those stores before any rank's next read.  No
