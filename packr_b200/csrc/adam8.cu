@@ -8,7 +8,10 @@
 // memory, no __syncthreads), the loads of the lane's next block are in
 // flight while the current one is computed, and one launch per parameter
 // dtype walks every tensor of a group through a block-offset table passed as
-// a __grid_constant__ parameter.
+// a __grid_constant__ parameter.  The push variant (packr_adam8_multi_push)
+// repeats each lane's 256-bit parameter store into up to 7 copies of the
+// tensor in other GPUs' memory (a data-parallel rank's shard going to every
+// other rank over NVLink) and ends with a system-scope fence.
 //
 // Arithmetic (every operation rounds to nearest, as the reference's does):
 //   wd decay  p  = fma(-(lr*wd), p, p)                     (cuda_adam_kernel.cu:34)
